@@ -1,0 +1,397 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized linear hot path on B200.
+
+Workload (the config the headline metric is quoted on):
+the FP8 e4m3 linear set of one Wan2.1-1.3B 3-latent-frame chunk, M = 4680
+tokens, dim 1536:
+    QKV   1536 -> 4608
+    out   1536 -> 1536
+    FFN1  1536 -> 8960, GELU-tanh
+    FFN2  8960 -> 1536, + gated residual into h (dit.rs:748-760)
+Weights N(0, 0.02) quantized with the reference's FP8 quantizer (group-128
+scales along K), activations bf16 N(0, 1), all seeded (lightx2v-core Rng).
+One step = those four linears. Every arithmetic op is bf16 x bf16 -> f32 on
+tcgen05 tensor cores after exact in-register dequantisation.
+
+value  TFLOP/s with inputs resident in HBM, device-timed with CUDA events per
+       step on the library's stream; L2 is flushed (256 MB write) before every
+       timed step, outside the timed region.
+e2e    the same TFLOP/s through the C ABI with host buffers: every step uploads
+       x and h from pinned f32 host memory and downloads h (f32) back.
+Multi-GPU (torchrun): weak scaling, each rank runs its own 4680-token chunk
+with replicated weights and no collective in the data path; time = max over
+ranks.
+
+--impl reference times the reference's CPU implementation of the path
+(CpuBackend::linear, restated in C under oracle/ because the Rust reference
+cannot be built here) on this host's cores, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "lightx2v-rs_b200"))
+
+M_TOKENS = 4680
+DIM = 1536
+FFN = 8960
+LINEARS = [  # name, N, K, act, seed
+    ("qkv", 3 * DIM, DIM, 0, 101),
+    ("out", DIM, DIM, 0, 102),
+    ("ffn1", FFN, DIM, 1, 103),
+    ("ffn2", DIM, FFN, 0, 104),
+]
+GATE_FFN = 5
+WORKLOAD = "fp8_linear_set_wan1.3b_chunk_m4680"
+
+
+def step_flops(m: int) -> float:
+    return float(sum(2.0 * m * n * k for _, n, k, _, _ in LINEARS))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gemm_fp8_linear_set.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.out = []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.out.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(m: int, seed_offset: int = 0):
+    """Seeded host inputs: FP8-quantized weights, biases, x, h, mods."""
+    from lightx2v_cuda import quant, rng
+    ws = {}
+    for name, n, k, act, seed in LINEARS:
+        w = rng.normal(seed, n * k, 0.02)
+        ws[name] = (quant.Fp8E4M3.quantize(w, n, k), rng.normal(seed + 1000, n, 0.01))
+    x = rng.normal(11 + seed_offset, m * DIM)
+    hid0 = None
+    h = rng.normal(12 + seed_offset, m * DIM)
+    mods = rng.normal(13, 6 * DIM, 0.01)
+    return ws, x, h, mods, hid0
+
+
+# ---------------------------------------------------------------------------------------------
+def cpu_sample_rows(total_rows: int, n: int):
+    return np.linspace(0, total_rows - 1, n).astype(int)
+
+
+def run_cpu_linear_set(ws, x, rows_idx, threads: int) -> float:
+    """The reference CPU linear (oracle port) on a sample of token rows for all
+    four linears; returns seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    deq = {name: (q.dequantize(), b) for name, (q, b) in ws.items()}
+    xs = np.ascontiguousarray(x.reshape(-1, DIM)[rows_idx])
+    r = len(rows_idx)
+    t0 = time.perf_counter()
+    qkv = oracle.linear(xs, r, deq["qkv"][0], 3 * DIM, DIM, bias=deq["qkv"][1], threads=threads)
+    out = oracle.linear(xs, r, deq["out"][0], DIM, DIM, bias=deq["out"][1], threads=threads)
+    hid = oracle.linear(xs, r, deq["ffn1"][0], FFN, DIM, bias=deq["ffn1"][1], act=1, threads=threads)
+    y = oracle.linear(hid, r, deq["ffn2"][0], DIM, FFN, bias=deq["ffn2"][1], threads=threads)
+    dt = time.perf_counter() - t0
+    del qkv, out, y
+    return dt
+
+
+def reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    threads = oracle.openmp_threads()
+    ws, x, h, mods, _ = make_inputs(M_TOKENS)
+    rows_per_step = max(8, 4 * threads)
+    if args.warmup > 0:
+        run_cpu_linear_set(ws, x, cpu_sample_rows(M_TOKENS, min(rows_per_step, 8)), threads)
+    times = []
+    for s in range(args.steps):
+        idx = (cpu_sample_rows(M_TOKENS, rows_per_step) + s) % M_TOKENS
+        times.append(run_cpu_linear_set(ws, x, idx, threads))
+    flops = step_flops(rows_per_step) * args.steps
+    tflops = flops / sum(times) / 1e12
+    ms_full_step = sum(times) / args.steps * (M_TOKENS / rows_per_step) * 1e3
+    line = {
+        "impl": "reference", "metric": "fp8_linear_set_tflops", "value": tflops, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_full_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens": M_TOKENS, "dim": DIM, "ffn": FFN,
+                   "sampled_rows_per_step": rows_per_step},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows_per_step} of {M_TOKENS} token rows per step through all four "
+                                   "linears; ms_per_step scaled to the full chunk"},
+        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+def cuda_arm(args, rank: int, world: int, local_rank: int):
+    import torch
+    from lightx2v_cuda import BF16, F32, CudaBackend
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    be = CudaBackend(local_rank)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    m = M_TOKENS
+    ws, x, h, mods, _ = make_inputs(m, seed_offset=rank)
+    dw = {name: (be.weight_fp8(q), be.upload(b)) for name, (q, b) in ws.items()}
+    xb = be.upload(x)                     # bf16 activations (the CUDA backend's precision)
+    hb = be.upload(h, F32)                # f32 residual stream
+    mb = be.upload(mods)
+    qkv = be.alloc(m * 3 * DIM)
+    tmp = be.alloc(m * DIM)
+    hid = be.alloc(m * FFN)
+
+    def step():
+        be.linear(xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, qkv, 0)
+        be.linear(xb, 0, m, dw["out"][0], dw["out"][1], 0, tmp, 0)
+        be.linear(xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, hid, 0)
+        be.linear_gate_residual(hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0, hb, 0, mb, GATE_FFN)
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+
+    def flush_l2():
+        with torch.cuda.stream(ext):
+            flush.zero_()
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    be.sync()
+
+    # --- device-resident timing -----------------------------------------------------------
+    def barrier():
+        be.sync()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    launches0 = be.launch_count()
+    pairs = []
+    with ClockSampler(local_rank) as clk:
+        for _ in range(args.steps):
+            flush_l2()
+            a, b = ev(), ev()
+            a.record(ext)
+            step()
+            b.record(ext)
+            pairs.append((a, b))
+        be.sync()
+    barrier()
+    launches = be.launch_count() - launches0
+    step_ms = [a.elapsed_time(b) for a, b in pairs]
+    total_ms = float(sum(step_ms))
+
+    # --- per-kernel timing for the roofline (same launches, one event pair each) ----------
+    kern_ms = {name: [] for name, *_ in LINEARS}
+    for _ in range(max(3, min(args.steps, 20))):
+        for name, n, k, act, _s in LINEARS:
+            flush_l2()
+            a, b = ev(), ev()
+            a.record(ext)
+            if name == "qkv":
+                be.linear(xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, qkv, 0)
+            elif name == "out":
+                be.linear(xb, 0, m, dw["out"][0], dw["out"][1], 0, tmp, 0)
+            elif name == "ffn1":
+                be.linear(xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, hid, 0)
+            else:
+                be.linear_gate_residual(hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0, hb, 0, mb, GATE_FFN)
+            b.record(ext)
+            kern_ms[name].append((a, b))
+    be.sync()
+    per_kernel = {}
+    for name, n, k, act, _s in LINEARS:
+        ms = float(np.mean([a.elapsed_time(b) for a, b in kern_ms[name]]))
+        per_kernel[name] = {"ms": ms, "tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12}
+    gemm_ms = sum(v["ms"] for v in per_kernel.values())
+
+    # --- end to end through the C ABI with host buffers --------------------------------------
+    x_host = torch.from_numpy(x).pin_memory()
+    h_host = torch.from_numpy(h).pin_memory()
+    h_out = torch.empty(m * DIM, dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        be.write_ptr(xb, x_host.data_ptr(), m * DIM)
+        be.write_ptr(hb, h_host.data_ptr(), m * DIM)
+        step()
+        be.download_ptr(hb, h_out.data_ptr(), m * DIM)
+    barrier()
+    e2e_pairs = []
+    for _ in range(args.steps):
+        flush_l2()
+        a, b = ev(), ev()
+        a.record(ext)
+        be.write_ptr(xb, x_host.data_ptr(), m * DIM)
+        be.write_ptr(hb, h_host.data_ptr(), m * DIM)
+        step()
+        be.download_ptr(hb, h_out.data_ptr(), m * DIM)
+        b.record(ext)
+        e2e_pairs.append((a, b))
+    be.sync()
+    barrier()
+    e2e_ms = float(sum(a.elapsed_time(b) for a, b in e2e_pairs))
+
+    # --- max over ranks --------------------------------------------------------------------
+    if dist:
+        t = torch.tensor([total_ms, e2e_ms, gemm_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms, gemm_ms = (float(v) for v in t.tolist())
+
+    flops_all = step_flops(m) * args.steps * world
+    value = flops_all / (total_ms * 1e-3) / 1e12
+    e2e_value = flops_all / (e2e_ms * 1e-3) / 1e12
+    peak, _hbm, peak_src = measured_peaks()
+    achieved = step_flops(m) / (gemm_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            rows = args.cpu_rows
+            idx = cpu_sample_rows(m, rows)
+            dt = run_cpu_linear_set(ws, x, idx, threads=1)
+            cpu = {"value": step_flops(rows) / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                   "sample": f"{rows} of {m} token rows through all four linears, single thread "
+                             f"({dt:.1f} s); CpuBackend::linear restated in C (oracle/)"}
+        clocks = clk.summary()
+        line = {
+            "metric": "fp8_linear_set_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": m, "global_tokens": m * world, "dim": DIM,
+                       "ffn": FFN, "weights": "fp8-e4m3 group-128 (reference quantizer)",
+                       "linears": [f"{nm} {k}->{n}{' gelu' if a else ''}" for nm, n, k, a, _ in LINEARS]
+                       + ["ffn2 fused gated residual into f32 h"],
+                       "l2": "flushed (256 MB write) before every timed step, outside the timed region",
+                       "parallelism": f"dp{world} (token rows; weights replicated; no collective)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * m * DIM * 4,
+                    "d2h_bytes_per_step": m * DIM * 4,
+                    "path": "C ABI: lx2v_buf_write_f32 x and h from pinned host, 4 linears, "
+                            "lx2v_buf_download_f32 h"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": f"bf16 dense burst, {peak_src}",
+                         "traffic": profile_traffic(),
+                         "kernel": "gemm_dq_kernel<FP8> (tcgen05, A=weights from TMEM)",
+                         "per_linear": per_kernel},
+            "cpu_baseline": cpu,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+    del pairs, e2e_pairs
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=96)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+    else:
+        cuda_arm(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

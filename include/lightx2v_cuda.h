@@ -1,0 +1,180 @@
+/*
+ * lightx2v_cuda.h — C ABI of the B200 (sm_100a) backend for lightx2v-rs's
+ * quantized linear path.
+ *
+ * The entry points are what a `lightx2v-cuda` crate's `impl Backend for
+ * CudaBackend` binds (crates/lightx2v-core/src/backend.rs:145-446). Each
+ * declaration names the trait method or reference function it serves.
+ *
+ * Conventions
+ *   - Every call returns lx2v_status (0 = LX2V_OK). On failure the message is
+ *     available from lx2v_last_error(ctx) until the next call on that ctx.
+ *   - Handles are opaque and owned by the library; *_free releases them.
+ *   - Host arrays passed in are copied during the call and never retained.
+ *   - A context owns one CUDA stream on one device. Calls on a context are
+ *     ordered on that stream. Use a context from one thread at a time; it may
+ *     be moved between threads (the reference moves its backend into the
+ *     serve engine thread, crates/lightx2v-cli/src/serve.rs:592-612).
+ *   - Activation buffers hold bf16 or f32 elements. The trait's own buffers are
+ *     bf16 on CUDA (backend.rs:9-11); f32 is offered for outputs and for the
+ *     residual stream. Host data crosses the boundary as f32 in both cases.
+ *   - Nothing here falls back to the CPU. A missing or unusable device is an
+ *     error (LX2V_ERR_NO_DEVICE), which the Rust side maps to
+ *     `CudaBackend::try_new() -> None`, like WgpuBackend::try_new
+ *     (crates/lightx2v-wgpu/src/lib.rs:285-290).
+ */
+#ifndef LIGHTX2V_CUDA_H
+#define LIGHTX2V_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LX2V_API __attribute__((visibility("default")))
+#else
+#define LX2V_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int lx2v_status;
+enum {
+    LX2V_OK = 0,
+    LX2V_ERR_INVALID = 1,     /* bad handle, shape, offset or length */
+    LX2V_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+    LX2V_ERR_OOM = 3,         /* device allocation failed */
+    LX2V_ERR_UNSUPPORTED = 4, /* valid request this build cannot run */
+    LX2V_ERR_NO_DEVICE = 5,   /* no usable sm_100 device */
+    LX2V_ERR_DEVICE = 6       /* a kernel reported an error (bounded wait expired) */
+};
+
+/* Epilogue activation of linear, backend.rs:38-43. */
+enum { LX2V_ACT_NONE = 0, LX2V_ACT_GELU_TANH = 1 };
+
+/* Element type of an activation buffer. */
+enum { LX2V_BF16 = 0, LX2V_F32 = 1 };
+
+/* Storage format of a weight matrix (quant.rs:27-43). */
+enum { LX2V_W_BF16 = 0, LX2V_W_Q8 = 1, LX2V_W_Q4 = 2, LX2V_W_FP8 = 3 };
+
+typedef struct lx2v_ctx lx2v_ctx;
+typedef struct lx2v_buf lx2v_buf;
+typedef struct lx2v_weight lx2v_weight;
+
+/* ---- context ------------------------------------------------------------ */
+/* Create a context on CUDA device `device` (backend construction; the
+ * reference's try_new, crates/lightx2v-wgpu/src/lib.rs:285-290). */
+LX2V_API lx2v_status lx2v_init(int device, lx2v_ctx **out);
+LX2V_API void lx2v_free_ctx(lx2v_ctx *ctx);
+/* Message of the last failed call on ctx ("" if none). Valid until the next
+ * call on ctx. NULL ctx returns the message of the last failed lx2v_init. */
+LX2V_API const char *lx2v_last_error(const lx2v_ctx *ctx);
+/* Backend::name, backend.rs:158. Writes a NUL-terminated name. */
+LX2V_API lx2v_status lx2v_name(lx2v_ctx *ctx, char *buf, size_t cap);
+/* Backend::sync, backend.rs:190: wait for queued work; also reports a kernel
+ * error (LX2V_ERR_DEVICE) raised since the last sync. */
+LX2V_API lx2v_status lx2v_sync(lx2v_ctx *ctx);
+/* The context's CUDA stream (a cudaStream_t), for callers that order their
+ * own work with the library's. */
+LX2V_API void *lx2v_stream(lx2v_ctx *ctx);
+
+/* ---- buffers (backend.rs:160-177) ---------------------------------------- */
+/* Backend::alloc: `len` zero-filled elements of `dtype`. */
+LX2V_API lx2v_status lx2v_buf_alloc(lx2v_ctx *ctx, size_t len, int dtype, lx2v_buf **out);
+/* Backend::upload: a new buffer holding `data` converted to `dtype`. */
+LX2V_API lx2v_status lx2v_buf_upload_f32(lx2v_ctx *ctx, const float *data, size_t len, int dtype,
+                                lx2v_buf **out);
+/* Backend::write: overwrite the first `len` elements. */
+LX2V_API lx2v_status lx2v_buf_write_f32(lx2v_ctx *ctx, lx2v_buf *buf, const float *data, size_t len);
+/* Backend::download: blocking read of the first `len` elements as f32. */
+LX2V_API lx2v_status lx2v_buf_download_f32(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len);
+/* Backend::buf_len. */
+LX2V_API lx2v_status lx2v_buf_len(lx2v_ctx *ctx, const lx2v_buf *buf, size_t *len);
+/* Element type and device address of a buffer (for tests and benchmarks). */
+LX2V_API lx2v_status lx2v_buf_info(lx2v_ctx *ctx, const lx2v_buf *buf, int *dtype, void **dev_ptr);
+/* Backend::copy: dst[dst_off..][..len] = src[src_off..][..len] (converting
+ * between dtypes when they differ). */
+LX2V_API lx2v_status lx2v_buf_copy(lx2v_ctx *ctx, const lx2v_buf *src, size_t src_off, lx2v_buf *dst,
+                          size_t dst_off, size_t len);
+LX2V_API void lx2v_buf_free(lx2v_ctx *ctx, lx2v_buf *buf);
+
+/* ---- weights (backend.rs:178-188) ---------------------------------------- */
+/* Backend::weight: a [rows, cols] f32 matrix stored as bf16 (the CUDA
+ * backend's native precision, quant.rs:28-29). */
+LX2V_API lx2v_status lx2v_weight_f32(lx2v_ctx *ctx, const float *data, size_t rows, size_t cols,
+                            lx2v_weight **out);
+/* Backend::weight_q8 for Q8 (quant.rs:144-205): codes i8 [rows*cols]
+ * row-major, scales f32 [rows, cols/group]. */
+LX2V_API lx2v_status lx2v_weight_q8(lx2v_ctx *ctx, const int8_t *q, const float *scales, size_t rows,
+                           size_t cols, size_t group, lx2v_weight **out);
+/* Backend::weight_q4 for Q4 (quant.rs:212-356): `packed` is Q4::packed()
+ * ((rows*cols+1)/2 bytes, element 2i in the low nibble, quant.rs:306-311);
+ * scales / zeros f32 [rows*cols/group], each exactly an f16 value as
+ * Q4::quantize stores them (quant.rs:280-281). A non-f16 value is rejected. */
+LX2V_API lx2v_status lx2v_weight_q4(lx2v_ctx *ctx, const uint8_t *packed, const float *scales,
+                           const float *zeros, size_t rows, size_t cols, size_t group,
+                           lx2v_weight **out);
+/* Backend::weight_fp8 for Fp8E4M3 (quant.rs:365-460): e4m3 code bytes
+ * [rows*cols] and scales f32 [rows*cols/group]. Codes decode through the
+ * reference's own e4m3_to_f32 (quant.rs:409-420), not hardware e4m3. */
+LX2V_API lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const float *scales, size_t rows,
+                            size_t cols, size_t group, lx2v_weight **out);
+LX2V_API void lx2v_weight_free(lx2v_ctx *ctx, lx2v_weight *w);
+/* Format, rows, cols and group of a weight. */
+LX2V_API lx2v_status lx2v_weight_info(lx2v_ctx *ctx, const lx2v_weight *w, int *format, size_t *rows,
+                             size_t *cols, size_t *group);
+/* Test hook: the weight dequantized on the device to f32 [rows*cols], with
+ * the arithmetic of Q8/Q4/Fp8E4M3::dequantize (quant.rs:180-186, 294-303,
+ * 449-455). Bit-exact against those functions. */
+LX2V_API lx2v_status lx2v_weight_dequant_f32(lx2v_ctx *ctx, const lx2v_weight *w, float *out);
+
+/* ---- linear (backend.rs:199-212) ----------------------------------------- */
+/* Backend::linear:
+ *   y[y_row + i, :] = act(x[x_row + i, :] . W^T + bias)   for i < rows
+ * x row stride = cols(W) (K), y row stride = rows(W) (N). bias may be NULL
+ * (length >= N otherwise). y must not alias x. The product is the exact
+ * dequantized weight rounded to bf16 times bf16 activations, accumulated in
+ * f32 (the backend's activation rounding, backend.rs:179-181). */
+LX2V_API lx2v_status lx2v_linear(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
+                        const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                        size_t y_row);
+/* linear fused with gate_residual (backend.rs:244-253), the sequence of
+ * crates/lightx2v-model/src/dit.rs:748-760:
+ *   h[h_row + i, j] += act(x[x_row + i, :] . W^T + bias)[j] * mods[gate * N + j]
+ * The linear output never goes through an intermediate buffer. */
+LX2V_API lx2v_status lx2v_linear_gate_residual(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row,
+                                      size_t rows, const lx2v_weight *w, const lx2v_buf *bias,
+                                      int act, lx2v_buf *h, size_t h_row, const lx2v_buf *mods,
+                                      size_t gate);
+/* Backend::gate_residual (backend.rs:244-253): h[r, j] += a[r, j] * mods[gate*dim + j]. */
+LX2V_API lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_buf *a, size_t rows,
+                               size_t dim, const lx2v_buf *mods, size_t gate);
+
+/* ---- profiling (backend.rs:192-196) -------------------------------------- */
+/* Backend::profile_report: per-op device time since the last reset, as JSON
+ * {"op": {"calls": n, "ms": t}, ...}. Profiling is on when the context was
+ * created with LIGHTX2V_PROFILE set to anything but "0" (the reference's
+ * switch, crates/lightx2v-cpu/src/lib.rs:27-34). `written` gets the length
+ * needed including the NUL. */
+LX2V_API lx2v_status lx2v_profile_json(lx2v_ctx *ctx, char *buf, size_t cap, size_t *written);
+/* Backend::profile_reset. */
+LX2V_API lx2v_status lx2v_profile_reset(lx2v_ctx *ctx);
+
+/* ---- knobs for tests and benchmarks -------------------------------------- */
+/* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05),
+ * 2 = small-M GEMV, 3 = generic CUDA-core kernel. A forced choice that cannot
+ * run the shape returns LX2V_ERR_UNSUPPORTED. */
+LX2V_API lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path);
+/* Bounded-wait limit of the pipelined kernels, in nanoseconds (default 2e9).
+ * A wait that expires makes the kernel stop and record an error that the
+ * next lx2v_sync returns as LX2V_ERR_DEVICE. */
+LX2V_API lx2v_status lx2v_set_wait_limit_ns(lx2v_ctx *ctx, uint64_t ns);
+/* Kernels this context has launched (for launch accounting in benchmarks). */
+LX2V_API lx2v_status lx2v_launch_count(lx2v_ctx *ctx, uint64_t *count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LIGHTX2V_CUDA_H */

@@ -1,0 +1,61 @@
+// gemm.h — parameters and launchers of the linear kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace lx2v {
+
+// Everything one linear launch needs; passed by value as a __grid_constant__.
+struct alignas(64) GemmParams {
+    CUtensorMap tmap_x;  // x: bf16 [x_row + M, K], box {64, BT}, 128-byte swizzle
+    CUtensorMap tmap_y;  // y (or h): bf16/f32 [y_row + M, N], box {128, 32}
+    const uint8_t *codes;     // weight codes in the reference layout (dequant.cuh)
+    const float *scales_t;    // Q8/FP8 scales, [G][N]
+    const uint32_t *sz_t;     // Q4 (scale, zero) half2 words, [G][N]
+    const void *bias;         // [N] or null
+    const void *gate;         // [N] (mods + gate * N) or null
+    int *err;                 // error word (ptx.cuh error codes)
+    uint64_t wait_limit_ns;   // bounded-wait limit
+    int M, N, K, group;
+    int x_row, y_row;
+    int act;                  // 0 none, 1 GELU-tanh
+    int out_f32;              // y element type: 1 f32, 0 bf16
+    int reduce;               // 1: reduce-add into y (gated residual)
+    int bias_f32, gate_f32;   // element types of bias / gate
+    int fp8_fast;
+};
+
+// Tensor-core (tcgen05) dequant GEMM. `bt` = token tile (128, 192 or 256).
+cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
+int gemm_dq_token_tile(int M);
+
+// Small-M path and the generic CUDA-core path (kernels.cu); they take plain
+// pointers instead of tensor maps.
+struct LinearArgs {
+    int fmt;
+    const uint8_t *codes;
+    const float *scales_t;
+    const uint32_t *sz_t;
+    int fp8_fast;
+    int M, N, K, group;
+    const void *x; int x_f32; int64_t x_row;
+    void *y; int y_f32; int64_t y_row;
+    const void *bias; int bias_f32;
+    const void *gate; int gate_f32;   // non-null: y += gate * act(...)
+    int act;
+};
+cudaError_t linear_simt_launch(const LinearArgs &a, cudaStream_t st);
+cudaError_t linear_gemv_launch(const LinearArgs &a, int num_sms, cudaStream_t st);
+bool gemv_supported(const LinearArgs &a);
+
+// Elementwise helpers (kernels.cu).
+cudaError_t convert_launch(const void *src, int src_f32, void *dst, int dst_f32, size_t n,
+                           cudaStream_t st);
+cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, const void *gate,
+                                 int gate_f32, size_t rows, size_t dim, cudaStream_t st);
+cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,
+                               const uint32_t *sz_t, int fp8_fast, int N, int K, int group,
+                               float *out, cudaStream_t st);
+
+}  // namespace lx2v

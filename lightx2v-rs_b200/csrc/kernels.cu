@@ -1,0 +1,163 @@
+// kernels.cu — the non-tensor-core kernels of the backend:
+//   convert          f32 <-> bf16 element conversion (upload / download / copy)
+//   gate_residual    Backend::gate_residual, crates/lightx2v-cpu/src/lib.rs:394-404
+//   dequant_f32      bit-exact weight decode (test hook for quant.rs dequantize)
+//   linear_simt      Backend::linear for shapes the tensor-core kernel does not
+//                    take (K not a multiple of 16, odd groups, tiny M, f32 x).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "dequant.cuh"
+#include "gemm.h"
+
+namespace lx2v {
+
+__device__ __forceinline__ float load_elem(const void *p, int f32, int64_t i) {
+    return f32 ? reinterpret_cast<const float *>(p)[i]
+               : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+}
+__device__ __forceinline__ void store_elem(void *p, int f32, int64_t i, float v) {
+    if (f32) reinterpret_cast<float *>(p)[i] = v;
+    else reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+}
+
+static int grid_for(size_t n, int threads) {
+    size_t g = (n + threads - 1) / threads;
+    if (g > 148 * 32) g = 148 * 32;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+// ---- convert --------------------------------------------------------------
+__global__ void convert_kernel(const void *src, int src_f32, void *dst, int dst_f32, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        store_elem(dst, dst_f32, (int64_t)i, load_elem(src, src_f32, (int64_t)i));
+}
+
+cudaError_t convert_launch(const void *src, int src_f32, void *dst, int dst_f32, size_t n,
+                           cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    convert_kernel<<<grid_for(n, 256), 256, 0, st>>>(src, src_f32, dst, dst_f32, n);
+    return cudaGetLastError();
+}
+
+// ---- gate_residual ---------------------------------------------------------
+// h[r, j] += a[r, j] * gate[j]   (gate = mods + gate_slot * dim)
+__global__ void gate_residual_kernel(void *h, int h_f32, const void *a, int a_f32, const void *gate,
+                                     int gate_f32, size_t rows, size_t dim) {
+    const size_t n = rows * dim;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t j = i % dim;
+        const float v = load_elem(h, h_f32, (int64_t)i) +
+                        load_elem(a, a_f32, (int64_t)i) * load_elem(gate, gate_f32, (int64_t)j);
+        store_elem(h, h_f32, (int64_t)i, v);
+    }
+}
+
+cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, const void *gate,
+                                 int gate_f32, size_t rows, size_t dim, cudaStream_t st) {
+    const size_t n = rows * dim;
+    if (n == 0) return cudaSuccess;
+    gate_residual_kernel<<<grid_for(n, 256), 256, 0, st>>>(h, h_f32, a, a_f32, gate, gate_f32, rows, dim);
+    return cudaGetLastError();
+}
+
+// ---- dequant hook ------------------------------------------------------------
+// Unit path: the same decode functions the GEMM's dequant warps run.
+__global__ void dequant_units_kernel(WeightView w, float *out) {
+    const int units_per_row = w.k / 16;
+    const int64_t total = (int64_t)w.n * units_per_row;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        const int n = (int)(u / units_per_row), k0 = (int)(u % units_per_row) * 16;
+        float v[16];
+        dq_unit(w, n, k0, v);
+        float4 *o = reinterpret_cast<float4 *>(out + (int64_t)n * w.k + k0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+}
+// Element path for shapes outside the unit path.
+__global__ void dequant_elems_kernel(WeightView w, float *out) {
+    const int64_t total = (int64_t)w.n * w.k;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = dq_elem(w, i / w.k, i % w.k);
+}
+
+cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,
+                               const uint32_t *sz_t, int fp8_fast, int N, int K, int group,
+                               float *out, cudaStream_t st) {
+    WeightView w{fmt, N, K, group, codes, scales_t, sz_t, fp8_fast};
+    if ((size_t)N * K == 0) return cudaSuccess;
+    if (unit_path_ok(fmt, K, group)) {
+        dequant_units_kernel<<<grid_for((size_t)N * K / 16, 256), 256, 0, st>>>(w, out);
+    } else {
+        dequant_elems_kernel<<<grid_for((size_t)N * K, 256), 256, 0, st>>>(w, out);
+    }
+    return cudaGetLastError();
+}
+
+// ---- generic CUDA-core linear ----------------------------------------------
+// 64x64 output tile per 256-thread block, 4x4 outputs per thread, K step 16.
+// Weights are the exact decoded value rounded to bf16 and activations are
+// rounded to bf16, the same operand rounding as the tensor-core kernel.
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__global__ void __launch_bounds__(256) linear_simt_kernel(LinearArgs a) {
+    __shared__ float xs[16][65];
+    __shared__ float ws[16][65];
+    WeightView w{a.fmt, a.N, a.K, a.group, a.codes, a.scales_t, a.sz_t, a.fp8_fast};
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < a.K; k0 += 16) {
+        for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+            const int r = e / 16, kk = e % 16, gk = k0 + kk;
+            float xv = 0.0f, wv = 0.0f;
+            if (m0 + r < a.M && gk < a.K)
+                xv = round_bf16(load_elem(a.x, a.x_f32, (a.x_row + m0 + r) * (int64_t)a.K + gk));
+            if (n0 + r < a.N && gk < a.K) wv = round_bf16(dq_elem(w, n0 + r, gk));
+            xs[kk][r] = xv;
+            ws[kk][r] = wv;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            float xa[4], wb[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { xa[i] = xs[kk][ty + 16 * i]; wb[i] = ws[kk][tx + 16 * i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wb[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty + 16 * i;
+        if (m >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx + 16 * j;
+            if (n >= a.N) continue;
+            float v = acc[i][j];
+            if (a.bias) v += load_elem(a.bias, a.bias_f32, n);
+            if (a.act == 1) {
+                const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+                v = v / (1.0f + expf(-2.0f * u));
+            }
+            const int64_t yi = (a.y_row + m) * (int64_t)a.N + n;
+            if (a.gate) v = load_elem(a.y, a.y_f32, yi) + v * load_elem(a.gate, a.gate_f32, n);
+            store_elem(a.y, a.y_f32, yi, v);
+        }
+    }
+}
+
+cudaError_t linear_simt_launch(const LinearArgs &a, cudaStream_t st) {
+    if (a.M == 0 || a.N == 0) return cudaSuccess;
+    dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
+    linear_simt_kernel<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace lx2v

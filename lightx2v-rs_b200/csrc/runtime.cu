@@ -1,0 +1,729 @@
+// runtime.cu — the C ABI declared in include/lightx2v_cuda.h: contexts,
+// activation buffers, weight upload into the device layout, linear dispatch,
+// errors and per-op profiling.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/lightx2v_cuda.h"
+#include "dequant.cuh"
+#include "gemm.h"
+
+using namespace lx2v;
+
+struct ProfEntry {
+    uint64_t calls = 0;
+    double ms = 0.0;
+};
+struct PendingEvent {
+    std::string op;
+    cudaEvent_t a, b;
+};
+
+struct lx2v_ctx {
+    int dev = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    int *err_dev = nullptr;
+    uint64_t wait_limit_ns = 2000000000ull;
+    int path = 0;
+    uint64_t launches = 0;
+    bool profile = false;
+    std::map<std::string, ProfEntry> prof;
+    std::vector<PendingEvent> pending;
+    std::vector<cudaEvent_t> event_pool;
+    void *staging = nullptr;
+    size_t staging_bytes = 0;
+    std::string last_err;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+};
+
+struct lx2v_buf {
+    void *ptr = nullptr;
+    size_t len = 0;
+    int dtype = LX2V_BF16;
+};
+
+struct lx2v_weight {
+    int fmt = LX2V_W_BF16;
+    size_t rows = 0, cols = 0, group = 0;
+    void *codes = nullptr;
+    float *scales_t = nullptr;
+    uint32_t *sz_t = nullptr;
+    int fp8_fast = 0;
+};
+
+static thread_local std::string g_init_err;
+
+static lx2v_status fail(lx2v_ctx *ctx, lx2v_status code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_err = buf;
+    else g_init_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(ctx, expr)                                                                       \
+    do {                                                                                          \
+        cudaError_t e_ = (expr);                                                                  \
+        if (e_ != cudaSuccess)                                                                    \
+            return fail(ctx, e_ == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA,     \
+                        "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__);     \
+    } while (0)
+
+static size_t esize(int dtype) { return dtype == LX2V_F32 ? 4 : 2; }
+
+static lx2v_status enter(lx2v_ctx *ctx) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    ctx->last_err.clear();
+    CUDA_TRY(ctx, cudaSetDevice(ctx->dev));
+    return LX2V_OK;
+}
+
+// ---- profiling ---------------------------------------------------------------
+struct OpScope {
+    lx2v_ctx *ctx;
+    const char *op;
+    cudaEvent_t a = nullptr;
+    OpScope(lx2v_ctx *c, const char *name) : ctx(c), op(name) {
+        if (!ctx->profile) return;
+        a = take();
+        cudaEventRecord(a, ctx->stream);
+    }
+    cudaEvent_t take() {
+        if (!ctx->event_pool.empty()) {
+            cudaEvent_t e = ctx->event_pool.back();
+            ctx->event_pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        return e;
+    }
+    ~OpScope() {
+        if (!ctx->profile || !a) return;
+        cudaEvent_t b = take();
+        cudaEventRecord(b, ctx->stream);
+        ctx->pending.push_back({op, a, b});
+    }
+};
+
+static void resolve_profile(lx2v_ctx *ctx) {
+    if (ctx->pending.empty()) return;
+    cudaStreamSynchronize(ctx->stream);
+    for (auto &p : ctx->pending) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, p.a, p.b);
+        auto &e = ctx->prof[p.op];
+        e.calls += 1;
+        e.ms += ms;
+        ctx->event_pool.push_back(p.a);
+        ctx->event_pool.push_back(p.b);
+    }
+    ctx->pending.clear();
+}
+
+static lx2v_status ensure_staging(lx2v_ctx *ctx, size_t bytes) {
+    if (ctx->staging_bytes >= bytes) return LX2V_OK;
+    if (ctx->staging) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->staging);
+        ctx->staging = nullptr;
+        ctx->staging_bytes = 0;
+    }
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    CUDA_TRY(ctx, cudaMalloc(&ctx->staging, want));
+    ctx->staging_bytes = want;
+    return LX2V_OK;
+}
+
+// ---- context -------------------------------------------------------------------
+extern "C" lx2v_status lx2v_init(int device, lx2v_ctx **out) {
+    if (!out) return fail(nullptr, LX2V_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return fail(nullptr, LX2V_ERR_NO_DEVICE, "no CUDA device is visible");
+    if (device < 0 || device >= n)
+        return fail(nullptr, LX2V_ERR_NO_DEVICE, "device %d out of range (%d visible)", device, n);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+        return fail(nullptr, LX2V_ERR_NO_DEVICE, "cannot query device %d", device);
+    if (prop.major != 10)
+        return fail(nullptr, LX2V_ERR_NO_DEVICE,
+                    "device %d is sm_%d%d; this library is built for sm_100a (B200)", device,
+                    prop.major, prop.minor);
+    auto *ctx = new lx2v_ctx();
+    ctx->dev = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->err_dev, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->err_dev, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        lx2v_status st = fail(nullptr, LX2V_ERR_CUDA, "context setup: %s", cudaGetErrorString(e));
+        lx2v_free_ctx(ctx);
+        return st;
+    }
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        lx2v_free_ctx(ctx);
+        return fail(nullptr, LX2V_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+    }
+    ctx->encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    const char *pe = getenv("LIGHTX2V_PROFILE");
+    ctx->profile = pe && strcmp(pe, "0") != 0;
+    *out = ctx;
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->dev);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (auto &p : ctx->pending) {
+        cudaEventDestroy(p.a);
+        cudaEventDestroy(p.b);
+    }
+    for (auto e : ctx->event_pool) cudaEventDestroy(e);
+    if (ctx->staging) cudaFree(ctx->staging);
+    if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+extern "C" const char *lx2v_last_error(const lx2v_ctx *ctx) {
+    return ctx ? ctx->last_err.c_str() : g_init_err.c_str();
+}
+
+extern "C" lx2v_status lx2v_name(lx2v_ctx *ctx, char *buf, size_t cap) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    cudaDeviceProp prop;
+    CUDA_TRY(ctx, cudaGetDeviceProperties(&prop, ctx->dev));
+    char tmp[320];
+    snprintf(tmp, sizeof tmp, "cuda:%d (%s, sm_%d%d, %d SMs)", ctx->dev, prop.name, prop.major,
+             prop.minor, prop.multiProcessorCount);
+    if (!buf || cap == 0) return fail(ctx, LX2V_ERR_INVALID, "null buffer");
+    snprintf(buf, cap, "%s", tmp);
+    return LX2V_OK;
+}
+
+static lx2v_status check_device_error(lx2v_ctx *ctx) {
+    int h = 0;
+    CUDA_TRY(ctx, cudaMemcpyAsync(&h, ctx->err_dev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    if (h != 0) {
+        CUDA_TRY(ctx, cudaMemsetAsync(ctx->err_dev, 0, sizeof(int), ctx->stream));
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        return fail(ctx, LX2V_ERR_DEVICE,
+                    "a kernel stopped: a pipeline wait exceeded the %llu ns limit (code %d)",
+                    (unsigned long long)ctx->wait_limit_ns, h);
+    }
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_sync(lx2v_ctx *ctx) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return check_device_error(ctx);
+}
+
+extern "C" void *lx2v_stream(lx2v_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+// ---- buffers -----------------------------------------------------------------------
+static bool valid_dtype(int d) { return d == LX2V_BF16 || d == LX2V_F32; }
+
+extern "C" lx2v_status lx2v_buf_alloc(lx2v_ctx *ctx, size_t len, int dtype, lx2v_buf **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !valid_dtype(dtype)) return fail(ctx, LX2V_ERR_INVALID, "bad output or dtype");
+    auto *b = new lx2v_buf();
+    b->len = len;
+    b->dtype = dtype;
+    if (len) {
+        cudaError_t e = cudaMalloc(&b->ptr, len * esize(dtype));
+        if (e == cudaSuccess) e = cudaMemsetAsync(b->ptr, 0, len * esize(dtype), ctx->stream);
+        if (e != cudaSuccess) {
+            if (b->ptr) cudaFree(b->ptr);
+            delete b;
+            return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA,
+                        "alloc of %zu elements: %s", len, cudaGetErrorString(e));
+        }
+    }
+    *out = b;
+    return LX2V_OK;
+}
+
+static lx2v_status write_f32(lx2v_ctx *ctx, lx2v_buf *b, const float *data, size_t len) {
+    if (len == 0) return LX2V_OK;
+    if (b->dtype == LX2V_F32) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(b->ptr, data, len * 4, cudaMemcpyHostToDevice, ctx->stream));
+        return LX2V_OK;
+    }
+    lx2v_status s = ensure_staging(ctx, len * 4);
+    if (s) return s;
+    CUDA_TRY(ctx, cudaMemcpyAsync(ctx->staging, data, len * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(ctx, convert_launch(ctx->staging, 1, b->ptr, 0, len, ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_buf_upload_f32(lx2v_ctx *ctx, const float *data, size_t len, int dtype,
+                                           lx2v_buf **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || (len && !data) || !valid_dtype(dtype)) return fail(ctx, LX2V_ERR_INVALID, "bad arguments");
+    OpScope ps(ctx, "upload");
+    lx2v_buf *b = nullptr;
+    s = lx2v_buf_alloc(ctx, len, dtype, &b);
+    if (s) return s;
+    s = write_f32(ctx, b, data, len);
+    if (s) {
+        lx2v_buf_free(ctx, b);
+        return s;
+    }
+    *out = b;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_buf_write_f32(lx2v_ctx *ctx, lx2v_buf *buf, const float *data, size_t len) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!buf || (len && !data)) return fail(ctx, LX2V_ERR_INVALID, "null buffer or data");
+    if (len > buf->len) return fail(ctx, LX2V_ERR_INVALID, "write of %zu elements into a buffer of %zu", len, buf->len);
+    OpScope ps(ctx, "write");
+    return write_f32(ctx, buf, data, len);
+}
+
+extern "C" lx2v_status lx2v_buf_download_f32(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!buf || (len && !out)) return fail(ctx, LX2V_ERR_INVALID, "null buffer or output");
+    if (len > buf->len) return fail(ctx, LX2V_ERR_INVALID, "download of %zu elements from a buffer of %zu", len, buf->len);
+    {
+        OpScope ps(ctx, "download");
+        if (len) {
+            if (buf->dtype == LX2V_F32) {
+                CUDA_TRY(ctx, cudaMemcpyAsync(out, buf->ptr, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
+            } else {
+                s = ensure_staging(ctx, len * 4);
+                if (s) return s;
+                CUDA_TRY(ctx, convert_launch(buf->ptr, 0, ctx->staging, 1, len, ctx->stream));
+                ctx->launches++;
+                CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->staging, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
+            }
+        }
+    }
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return check_device_error(ctx);
+}
+
+extern "C" lx2v_status lx2v_buf_len(lx2v_ctx *ctx, const lx2v_buf *buf, size_t *len) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!buf || !len) return fail(ctx, LX2V_ERR_INVALID, "null buffer or output");
+    *len = buf->len;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_buf_info(lx2v_ctx *ctx, const lx2v_buf *buf, int *dtype, void **dev_ptr) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!buf) return fail(ctx, LX2V_ERR_INVALID, "null buffer");
+    if (dtype) *dtype = buf->dtype;
+    if (dev_ptr) *dev_ptr = buf->ptr;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_buf_copy(lx2v_ctx *ctx, const lx2v_buf *src, size_t src_off, lx2v_buf *dst,
+                                     size_t dst_off, size_t len) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!src || !dst) return fail(ctx, LX2V_ERR_INVALID, "null buffer");
+    if (src_off + len > src->len || dst_off + len > dst->len)
+        return fail(ctx, LX2V_ERR_INVALID, "copy range out of bounds");
+    if (len == 0) return LX2V_OK;
+    OpScope ps(ctx, "copy");
+    const char *sp = (const char *)src->ptr + src_off * esize(src->dtype);
+    char *dp = (char *)dst->ptr + dst_off * esize(dst->dtype);
+    if (src->dtype == dst->dtype) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(dp, sp, len * esize(src->dtype), cudaMemcpyDeviceToDevice, ctx->stream));
+    } else {
+        CUDA_TRY(ctx, convert_launch(sp, src->dtype == LX2V_F32, dp, dst->dtype == LX2V_F32, len, ctx->stream));
+        ctx->launches++;
+    }
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_buf_free(lx2v_ctx *ctx, lx2v_buf *buf) {
+    if (!buf) return;
+    if (ctx) {
+        cudaSetDevice(ctx->dev);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    if (buf->ptr) cudaFree(buf->ptr);
+    delete buf;
+}
+
+// ---- weights -------------------------------------------------------------------------
+static void weight_release(lx2v_weight *w) {
+    if (!w) return;
+    if (w->codes) cudaFree(w->codes);
+    if (w->scales_t) cudaFree(w->scales_t);
+    if (w->sz_t) cudaFree(w->sz_t);
+    delete w;
+}
+
+static lx2v_status check_shape(lx2v_ctx *ctx, size_t rows, size_t cols, size_t group) {
+    if (rows == 0 || cols == 0) return fail(ctx, LX2V_ERR_INVALID, "empty weight %zux%zu", rows, cols);
+    if (rows > (1u << 30) || cols > (1u << 30)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "weight too large");
+    if (group == 0 || cols % group != 0)
+        return fail(ctx, LX2V_ERR_INVALID, "group %zu does not divide cols %zu", group, cols);
+    return LX2V_OK;
+}
+
+// Scales [rows, G] -> device [G, rows].
+static std::vector<float> transpose_scales(const float *s, size_t rows, size_t G) {
+    std::vector<float> t(rows * G);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t g = 0; g < G; ++g) t[g * rows + r] = s[r * G + g];
+    return t;
+}
+
+extern "C" lx2v_status lx2v_weight_f32(lx2v_ctx *ctx, const float *data, size_t rows, size_t cols,
+                                       lx2v_weight **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !data) return fail(ctx, LX2V_ERR_INVALID, "null data or output");
+    if ((s = check_shape(ctx, rows, cols, cols))) return s;
+    OpScope ps(ctx, "weight");
+    auto *w = new lx2v_weight();
+    w->fmt = LX2V_W_BF16;
+    w->rows = rows; w->cols = cols; w->group = cols;
+    const size_t n = rows * cols;
+    cudaError_t e = cudaMalloc(&w->codes, n * 2);
+    if (e != cudaSuccess) { weight_release(w); return fail(ctx, LX2V_ERR_OOM, "weight alloc: %s", cudaGetErrorString(e)); }
+    if ((s = ensure_staging(ctx, n * 4))) { weight_release(w); return s; }
+    e = cudaMemcpyAsync(ctx->staging, data, n * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = convert_launch(ctx->staging, 1, w->codes, 0, n, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    ctx->launches++;
+    if (e != cudaSuccess) { weight_release(w); return fail(ctx, LX2V_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e)); }
+    *out = w;
+    return LX2V_OK;
+}
+
+static lx2v_status upload_codes_scales(lx2v_ctx *ctx, lx2v_weight *w, const void *codes, size_t code_bytes,
+                                       const std::vector<float> *scales_t, const std::vector<uint32_t> *sz_t) {
+    cudaError_t e = cudaMalloc(&w->codes, code_bytes < 16 ? 16 : code_bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(w->codes, codes, code_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && scales_t) {
+        e = cudaMalloc(&w->scales_t, scales_t->size() * 4);
+        if (e == cudaSuccess) e = cudaMemcpy(w->scales_t, scales_t->data(), scales_t->size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess && sz_t) {
+        e = cudaMalloc(&w->sz_t, sz_t->size() * 4);
+        if (e == cudaSuccess) e = cudaMemcpy(w->sz_t, sz_t->data(), sz_t->size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess)
+        return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA, "weight upload: %s",
+                    cudaGetErrorString(e));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_weight_q8(lx2v_ctx *ctx, const int8_t *q, const float *scales, size_t rows,
+                                      size_t cols, size_t group, lx2v_weight **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !q || !scales) return fail(ctx, LX2V_ERR_INVALID, "null codes, scales or output");
+    if ((s = check_shape(ctx, rows, cols, group))) return s;
+    OpScope ps(ctx, "weight_q8");
+    auto *w = new lx2v_weight();
+    w->fmt = LX2V_W_Q8; w->rows = rows; w->cols = cols; w->group = group;
+    auto st = transpose_scales(scales, rows, cols / group);
+    if ((s = upload_codes_scales(ctx, w, q, rows * cols, &st, nullptr))) { weight_release(w); return s; }
+    *out = w;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const float *scales, size_t rows,
+                                       size_t cols, size_t group, lx2v_weight **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !q || !scales) return fail(ctx, LX2V_ERR_INVALID, "null codes, scales or output");
+    if ((s = check_shape(ctx, rows, cols, group))) return s;
+    OpScope ps(ctx, "weight_fp8");
+    auto *w = new lx2v_weight();
+    w->fmt = LX2V_W_FP8; w->rows = rows; w->cols = cols; w->group = group;
+    const size_t G = cols / group;
+    bool fast = true;
+    for (size_t i = 0; i < rows * G; ++i) {
+        const float v = scales[i];
+        if (!(v >= 0x1p-100f && v < 0x1p7f)) fast = false;
+    }
+    w->fp8_fast = fast ? 1 : 0;
+    auto st = transpose_scales(scales, rows, G);
+    if ((s = upload_codes_scales(ctx, w, q, rows * cols, &st, nullptr))) { weight_release(w); return s; }
+    *out = w;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_weight_q4(lx2v_ctx *ctx, const uint8_t *packed, const float *scales,
+                                      const float *zeros, size_t rows, size_t cols, size_t group,
+                                      lx2v_weight **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !packed || !scales || !zeros) return fail(ctx, LX2V_ERR_INVALID, "null codes, scales, zeros or output");
+    if ((s = check_shape(ctx, rows, cols, group))) return s;
+    OpScope ps(ctx, "weight_q4");
+    const size_t G = cols / group;
+    std::vector<uint32_t> sz(rows * G);
+    for (size_t r = 0; r < rows; ++r) {
+        for (size_t g = 0; g < G; ++g) {
+            const float sc = scales[r * G + g], ze = zeros[r * G + g];
+            const __half hs = __float2half_rn(sc), hz = __float2half_rn(ze);
+            const float bs = __half2float(hs), bz = __half2float(hz);
+            const bool same = (bs == sc || (std::isnan(bs) && std::isnan(sc))) &&
+                              (bz == ze || (std::isnan(bz) && std::isnan(ze)));
+            if (!same || (sc == 0.0f && std::signbit(sc) != std::signbit(bs)) ||
+                (ze == 0.0f && std::signbit(ze) != std::signbit(bz)))
+                return fail(ctx, LX2V_ERR_INVALID,
+                            "Q4 scale/zero of row %zu group %zu is not an f16 value (%g, %g)", r, g, sc, ze);
+            uint16_t us, uz;
+            memcpy(&us, &hs, 2);
+            memcpy(&uz, &hz, 2);
+            sz[g * rows + r] = (uint32_t)us | ((uint32_t)uz << 16);
+        }
+    }
+    auto *w = new lx2v_weight();
+    w->fmt = LX2V_W_Q4; w->rows = rows; w->cols = cols; w->group = group;
+    if ((s = upload_codes_scales(ctx, w, packed, (rows * cols + 1) / 2, nullptr, &sz))) { weight_release(w); return s; }
+    *out = w;
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_weight_free(lx2v_ctx *ctx, lx2v_weight *w) {
+    if (!w) return;
+    if (ctx) {
+        cudaSetDevice(ctx->dev);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    weight_release(w);
+}
+
+extern "C" lx2v_status lx2v_weight_info(lx2v_ctx *ctx, const lx2v_weight *w, int *format, size_t *rows,
+                                        size_t *cols, size_t *group) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!w) return fail(ctx, LX2V_ERR_INVALID, "null weight");
+    if (format) *format = w->fmt;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (group) *group = w->group;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_weight_dequant_f32(lx2v_ctx *ctx, const lx2v_weight *w, float *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!w || !out) return fail(ctx, LX2V_ERR_INVALID, "null weight or output");
+    const size_t n = w->rows * w->cols;
+    if ((s = ensure_staging(ctx, n * 4))) return s;
+    CUDA_TRY(ctx, dequant_f32_launch(w->fmt, (const uint8_t *)w->codes, w->scales_t, w->sz_t, w->fp8_fast,
+                                     (int)w->rows, (int)w->cols, (int)w->group, (float *)ctx->staging,
+                                     ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->staging, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return LX2V_OK;
+}
+
+// ---- linear -----------------------------------------------------------------------------
+static lx2v_status make_map(lx2v_ctx *ctx, CUtensorMap *map, const void *base, CUtensorMapDataType dt,
+                            size_t esz, uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+                            CUtensorMapSwizzle sw) {
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * esz};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = ctx->encode(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(ctx, LX2V_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u", (int)r,
+                    (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+    return LX2V_OK;
+}
+
+static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf *x, size_t x_row,
+                               size_t rows, const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                               size_t y_row, const lx2v_buf *mods, size_t gate) {
+    if (!x || !w || !y) return fail(ctx, LX2V_ERR_INVALID, "null x, weight or output");
+    if (act != LX2V_ACT_NONE && act != LX2V_ACT_GELU_TANH) return fail(ctx, LX2V_ERR_INVALID, "bad act %d", act);
+    if (x == y || (x->ptr && x->ptr == y->ptr)) return fail(ctx, LX2V_ERR_INVALID, "output aliases input");
+    const size_t N = w->rows, K = w->cols;
+    if ((x_row + rows) * K > x->len)
+        return fail(ctx, LX2V_ERR_INVALID, "x has %zu elements, rows [%zu, %zu) x %zu need more", x->len, x_row,
+                    x_row + rows, K);
+    if ((y_row + rows) * N > y->len)
+        return fail(ctx, LX2V_ERR_INVALID, "output has %zu elements, rows [%zu, %zu) x %zu need more", y->len,
+                    y_row, y_row + rows, N);
+    if (bias && bias->len < N) return fail(ctx, LX2V_ERR_INVALID, "bias has %zu elements, need %zu", bias->len, N);
+    if (mods && mods->len < (gate + 1) * N)
+        return fail(ctx, LX2V_ERR_INVALID, "mods has %zu elements, gate %zu x %zu needs more", mods->len, gate, N);
+    if (rows == 0) return LX2V_OK;
+    if (rows > (1u << 30)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "too many rows");
+    OpScope ps(ctx, opname);
+
+    const void *gate_ptr = mods ? (const char *)mods->ptr + gate * N * esize(mods->dtype) : nullptr;
+    const bool tc_ok = x->dtype == LX2V_BF16 && K % 16 == 0 &&
+                       unit_path_ok(w->fmt, (int)K, (int)w->group) &&
+                       (N * esize(y->dtype)) % 16 == 0 && rows >= 16;
+    int path = ctx->path;
+    if (path == 0) path = tc_ok ? 1 : 3;
+    if (path == 1 && !tc_ok)
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "the tensor-core kernel does not take this shape/dtype");
+    if (path == 2) return fail(ctx, LX2V_ERR_UNSUPPORTED, "the small-M kernel is not built in this version");
+
+    if (path == 1) {
+        GemmParams p;
+        memset(&p, 0, sizeof p);
+        const int bt = gemm_dq_token_tile((int)rows);
+        lx2v_status s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
+                                 (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (s) return s;
+        s = make_map(ctx, &p.tmap_y, y->ptr,
+                     y->dtype == LX2V_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     esize(y->dtype), N, y_row + rows, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s) return s;
+        p.codes = (const uint8_t *)w->codes;
+        p.scales_t = w->scales_t;
+        p.sz_t = w->sz_t;
+        p.fp8_fast = w->fp8_fast;
+        p.bias = bias ? bias->ptr : nullptr;
+        p.bias_f32 = bias && bias->dtype == LX2V_F32;
+        p.gate = gate_ptr;
+        p.gate_f32 = mods && mods->dtype == LX2V_F32;
+        p.err = ctx->err_dev;
+        p.wait_limit_ns = ctx->wait_limit_ns;
+        p.M = (int)rows; p.N = (int)N; p.K = (int)K; p.group = (int)w->group;
+        p.x_row = (int)x_row; p.y_row = (int)y_row;
+        p.act = act;
+        p.out_f32 = y->dtype == LX2V_F32;
+        p.reduce = mods ? 1 : 0;
+        CUDA_TRY(ctx, gemm_dq_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
+        ctx->launches++;
+        return LX2V_OK;
+    }
+    LinearArgs a;
+    memset(&a, 0, sizeof a);
+    a.fmt = w->fmt; a.codes = (const uint8_t *)w->codes; a.scales_t = w->scales_t; a.sz_t = w->sz_t;
+    a.fp8_fast = w->fp8_fast;
+    a.M = (int)rows; a.N = (int)N; a.K = (int)K; a.group = (int)w->group;
+    a.x = x->ptr; a.x_f32 = x->dtype == LX2V_F32; a.x_row = (int64_t)x_row;
+    a.y = y->ptr; a.y_f32 = y->dtype == LX2V_F32; a.y_row = (int64_t)y_row;
+    a.bias = bias ? bias->ptr : nullptr; a.bias_f32 = bias && bias->dtype == LX2V_F32;
+    a.gate = gate_ptr; a.gate_f32 = mods && mods->dtype == LX2V_F32;
+    a.act = act;
+    CUDA_TRY(ctx, linear_simt_launch(a, ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_linear(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
+                                   const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                                   size_t y_row) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    return linear_impl(ctx, "linear", x, x_row, rows, w, bias, act, y, y_row, nullptr, 0);
+}
+
+extern "C" lx2v_status lx2v_linear_gate_residual(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
+                                                 const lx2v_weight *w, const lx2v_buf *bias, int act,
+                                                 lx2v_buf *h, size_t h_row, const lx2v_buf *mods, size_t gate) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!mods) return fail(ctx, LX2V_ERR_INVALID, "null mods");
+    return linear_impl(ctx, "linear_gate_residual", x, x_row, rows, w, bias, act, h, h_row, mods, gate);
+}
+
+extern "C" lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_buf *a, size_t rows, size_t dim,
+                                          const lx2v_buf *mods, size_t gate) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!h || !a || !mods) return fail(ctx, LX2V_ERR_INVALID, "null buffer");
+    if (rows * dim > h->len || rows * dim > a->len || (gate + 1) * dim > mods->len)
+        return fail(ctx, LX2V_ERR_INVALID, "gate_residual range out of bounds");
+    if (rows * dim == 0) return LX2V_OK;
+    OpScope ps(ctx, "gate_residual");
+    const void *g = (const char *)mods->ptr + gate * dim * esize(mods->dtype);
+    CUDA_TRY(ctx, gate_residual_launch(h->ptr, h->dtype == LX2V_F32, a->ptr, a->dtype == LX2V_F32, g,
+                                       mods->dtype == LX2V_F32, rows, dim, ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}
+
+// ---- profiling / knobs ---------------------------------------------------------------------
+extern "C" lx2v_status lx2v_profile_json(lx2v_ctx *ctx, char *buf, size_t cap, size_t *written) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    resolve_profile(ctx);
+    std::string js = "{";
+    bool first = true;
+    for (auto &kv : ctx->prof) {
+        char tmp[256];
+        snprintf(tmp, sizeof tmp, "%s\"%s\": {\"calls\": %llu, \"ms\": %.6f}", first ? "" : ", ", kv.first.c_str(),
+                 (unsigned long long)kv.second.calls, kv.second.ms);
+        js += tmp;
+        first = false;
+    }
+    js += "}";
+    if (written) *written = js.size() + 1;
+    if (buf && cap) snprintf(buf, cap, "%s", js.c_str());
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_profile_reset(lx2v_ctx *ctx) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    resolve_profile(ctx);
+    ctx->prof.clear();
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (path < 0 || path > 3) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
+    ctx->path = path;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_set_wait_limit_ns(lx2v_ctx *ctx, uint64_t ns) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (ns == 0) return fail(ctx, LX2V_ERR_INVALID, "wait limit must be positive");
+    ctx->wait_limit_ns = ns;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_launch_count(lx2v_ctx *ctx, uint64_t *count) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!count) return fail(ctx, LX2V_ERR_INVALID, "null output");
+    *count = ctx->launches;
+    return LX2V_OK;
+}

@@ -1,0 +1,102 @@
+"""ctypes binding of liblightx2v_cuda.so (the C ABI in include/lightx2v_cuda.h).
+
+This is the reference-side binding a host language would add; the Rust
+version of the same declarations is in INTEGRATION.md. There is no fallback:
+if the shared library is missing, importing the backend raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_NAME = "liblightx2v_cuda.so"
+LIB_PATH = os.path.join(HERE, LIB_NAME)
+
+OK = 0
+ERR_INVALID = 1
+ERR_CUDA = 2
+ERR_OOM = 3
+ERR_UNSUPPORTED = 4
+ERR_NO_DEVICE = 5
+ERR_DEVICE = 6
+STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "NO_DEVICE",
+                6: "DEVICE"}
+
+ACT_NONE = 0
+ACT_GELU_TANH = 1
+BF16 = 0
+F32 = 1
+W_BF16, W_Q8, W_Q4, W_FP8 = 0, 1, 2, 3
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_st = ctypes.c_int
+_pp = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes); mirrors include/lightx2v_cuda.h one to one.
+SIGNATURES = {
+    "lx2v_init": (_st, [ctypes.c_int, _pp]),
+    "lx2v_free_ctx": (None, [_vp]),
+    "lx2v_last_error": (ctypes.c_char_p, [_vp]),
+    "lx2v_name": (_st, [_vp, ctypes.c_char_p, _sz]),
+    "lx2v_sync": (_st, [_vp]),
+    "lx2v_stream": (_vp, [_vp]),
+    "lx2v_buf_alloc": (_st, [_vp, _sz, ctypes.c_int, _pp]),
+    "lx2v_buf_upload_f32": (_st, [_vp, _vp, _sz, ctypes.c_int, _pp]),
+    "lx2v_buf_write_f32": (_st, [_vp, _vp, _vp, _sz]),
+    "lx2v_buf_download_f32": (_st, [_vp, _vp, _vp, _sz]),
+    "lx2v_buf_len": (_st, [_vp, _vp, ctypes.POINTER(_sz)]),
+    "lx2v_buf_info": (_st, [_vp, _vp, ctypes.POINTER(ctypes.c_int), _pp]),
+    "lx2v_buf_copy": (_st, [_vp, _vp, _sz, _vp, _sz, _sz]),
+    "lx2v_buf_free": (None, [_vp, _vp]),
+    "lx2v_weight_f32": (_st, [_vp, _vp, _sz, _sz, _pp]),
+    "lx2v_weight_q8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
+    "lx2v_weight_q4": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _pp]),
+    "lx2v_weight_fp8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
+    "lx2v_weight_free": (None, [_vp, _vp]),
+    "lx2v_weight_info": (_st, [_vp, _vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_sz),
+                               ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
+    "lx2v_weight_dequant_f32": (_st, [_vp, _vp, _vp]),
+    "lx2v_linear": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz]),
+    "lx2v_linear_gate_residual": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz,
+                                        _vp, _sz]),
+    "lx2v_gate_residual": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _sz]),
+    "lx2v_profile_json": (_st, [_vp, ctypes.c_char_p, _sz, ctypes.POINTER(_sz)]),
+    "lx2v_profile_reset": (_st, [_vp]),
+    "lx2v_set_linear_path": (_st, [_vp, ctypes.c_int]),
+    "lx2v_set_wait_limit_ns": (_st, [_vp, ctypes.c_uint64]),
+    "lx2v_launch_count": (_st, [_vp, ctypes.POINTER(ctypes.c_uint64)]),
+}
+
+_lib = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def load(path: str | None = None):
+    """Load the shared library and declare every entry point."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise LibraryMissing(
+            f"{p} is missing: build it with `make -C lightx2v-rs_b200/csrc` "
+            "(or __graft_entry__.build()); there is no CPU fallback")
+    lib = ctypes.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+class Lx2vError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"lx2v status {STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status

@@ -1,0 +1,264 @@
+"""`CudaBackend`: the reference's `Backend` trait (crates/lightx2v-core/src/backend.rs:145-446)
+for the quantized-linear path, over the C ABI of liblightx2v_cuda.so.
+
+Method names, argument order and meaning follow the trait:
+  alloc / upload / write / download / buf_len / copy            backend.rs:160-177
+  weight / weight_q8 / weight_q4 / weight_fp8 / sync             backend.rs:178-190
+  profile_report / profile_reset                                 backend.rs:192-196
+  linear                                                         backend.rs:199-212
+  gate_residual                                                  backend.rs:244-253
+plus `linear_gate_residual`, the fused form of the FFN2 linear followed by
+gate_residual (crates/lightx2v-model/src/dit.rs:748-760).
+
+Like the reference, misuse raises (the reference panics: `assert!` in the
+backends); the availability probe `try_new` returns None when no B200 answers
+(WgpuBackend::try_new, crates/lightx2v-wgpu/src/lib.rs:285-290).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+
+import numpy as np
+
+from . import _lib as L
+from .quant import Fp8E4M3, Q4, Q8
+
+
+class Act:
+    """`Act` (backend.rs:38-43)."""
+    NONE = L.ACT_NONE
+    GELU_TANH = L.ACT_GELU_TANH
+
+
+class Buf:
+    """A flat device buffer of activations (bf16 or f32 elements)."""
+
+    def __init__(self, be: "CudaBackend", handle: int, length: int, dtype: int):
+        self._be = be
+        self.handle = ctypes.c_void_p(handle)
+        self.len = length
+        self.dtype = dtype
+
+    def __del__(self):
+        be = getattr(self, "_be", None)
+        if be is not None and be._ctx and self.handle:
+            be._lib.lx2v_buf_free(be._ctx, self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+    @property
+    def dev_ptr(self) -> int:
+        p = ctypes.c_void_p()
+        self._be._check(self._be._lib.lx2v_buf_info(self._be._ctx, self.handle, None,
+                                                     ctypes.byref(p)))
+        return p.value or 0
+
+
+class Weight:
+    """A `[rows, cols]` matrix (nn.Linear layout `[out, in]`) on the device."""
+
+    def __init__(self, be: "CudaBackend", handle: int, rows: int, cols: int, fmt: int, group: int):
+        self._be = be
+        self.handle = ctypes.c_void_p(handle)
+        self.rows, self.cols, self.format, self.group = rows, cols, fmt, group
+
+    def __del__(self):
+        be = getattr(self, "_be", None)
+        if be is not None and be._ctx and self.handle:
+            be._lib.lx2v_weight_free(be._ctx, self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+
+
+class CudaBackend:
+    """The CUDA backend for one device. Buffers default to bf16, the CUDA
+    backend's activation precision (backend.rs:9-11)."""
+
+    def __init__(self, device: int = 0, lib_path: str | None = None):
+        self._lib = L.load(lib_path)
+        ctx = ctypes.c_void_p()
+        st = self._lib.lx2v_init(device, ctypes.byref(ctx))
+        if st != L.OK:
+            raise L.Lx2vError(st, self._lib.lx2v_last_error(None).decode())
+        self._ctx = ctx
+        self.device = device
+
+    @classmethod
+    def try_new(cls, device: int = 0):
+        """None when no usable B200 answers (the reference's skip-not-fail)."""
+        try:
+            return cls(device)
+        except L.Lx2vError as e:
+            if e.status == L.ERR_NO_DEVICE:
+                return None
+            raise
+
+    def close(self):
+        if getattr(self, "_ctx", None):
+            self._lib.lx2v_free_ctx(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        # Buffers and weights hold a reference to the backend, so the context
+        # outlives them.
+        self.close()
+
+    def _check(self, st: int):
+        if st != L.OK:
+            raise L.Lx2vError(st, self._lib.lx2v_last_error(self._ctx).decode())
+
+    # ---- backend.rs:158 -------------------------------------------------------
+    def name(self) -> str:
+        buf = ctypes.create_string_buffer(320)
+        self._check(self._lib.lx2v_name(self._ctx, buf, 320))
+        return buf.value.decode()
+
+    # ---- memory, backend.rs:160-190 -------------------------------------------
+    def alloc(self, length: int, dtype: int = L.BF16) -> Buf:
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_buf_alloc(self._ctx, length, dtype, ctypes.byref(h)))
+        return Buf(self, h.value, length, dtype)
+
+    def upload(self, data, dtype: int = L.BF16) -> Buf:
+        a = _f32(data)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_buf_upload_f32(self._ctx, a.ctypes.data, a.size, dtype,
+                                                  ctypes.byref(h)))
+        return Buf(self, h.value, a.size, dtype)
+
+    def upload_ptr(self, host_ptr: int, length: int, dtype: int = L.BF16) -> Buf:
+        """upload() from a raw host address of `length` f32 values (e.g. pinned memory)."""
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_buf_upload_f32(self._ctx, host_ptr, length, dtype,
+                                                  ctypes.byref(h)))
+        return Buf(self, h.value, length, dtype)
+
+    def write(self, buf: Buf, data):
+        a = _f32(data)
+        self._check(self._lib.lx2v_buf_write_f32(self._ctx, buf.handle, a.ctypes.data, a.size))
+
+    def write_ptr(self, buf: Buf, host_ptr: int, length: int):
+        self._check(self._lib.lx2v_buf_write_f32(self._ctx, buf.handle, host_ptr, length))
+
+    def download(self, buf: Buf) -> np.ndarray:
+        out = np.empty(buf.len, np.float32)
+        self._check(self._lib.lx2v_buf_download_f32(self._ctx, buf.handle, out.ctypes.data,
+                                                    buf.len))
+        return out
+
+    def download_ptr(self, buf: Buf, host_ptr: int, length: int):
+        self._check(self._lib.lx2v_buf_download_f32(self._ctx, buf.handle, host_ptr, length))
+
+    def buf_len(self, buf: Buf) -> int:
+        n = ctypes.c_size_t()
+        self._check(self._lib.lx2v_buf_len(self._ctx, buf.handle, ctypes.byref(n)))
+        return n.value
+
+    def copy(self, src: Buf, src_off: int, dst: Buf, dst_off: int, length: int):
+        self._check(self._lib.lx2v_buf_copy(self._ctx, src.handle, src_off, dst.handle, dst_off,
+                                            length))
+
+    def weight(self, data, rows: int, cols: int) -> Weight:
+        a = _f32(data)
+        assert a.size == rows * cols, "weight: data length != rows * cols"
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_weight_f32(self._ctx, a.ctypes.data, rows, cols,
+                                              ctypes.byref(h)))
+        return Weight(self, h.value, rows, cols, L.W_BF16, cols)
+
+    def weight_q8(self, q: Q8) -> Weight:
+        codes = np.ascontiguousarray(q.q, np.int8)
+        scales = np.ascontiguousarray(q.scales, np.float32)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_weight_q8(self._ctx, codes.ctypes.data, scales.ctypes.data,
+                                             q.rows, q.cols, q.group, ctypes.byref(h)))
+        return Weight(self, h.value, q.rows, q.cols, L.W_Q8, q.group)
+
+    def weight_q4(self, q: Q4) -> Weight:
+        packed = np.ascontiguousarray(q.packed(), np.uint8)
+        scales = np.ascontiguousarray(q.scales, np.float32)
+        zeros = np.ascontiguousarray(q.zeros, np.float32)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_weight_q4(self._ctx, packed.ctypes.data, scales.ctypes.data,
+                                             zeros.ctypes.data, q.rows, q.cols, q.group,
+                                             ctypes.byref(h)))
+        return Weight(self, h.value, q.rows, q.cols, L.W_Q4, q.group)
+
+    def weight_fp8(self, q: Fp8E4M3) -> Weight:
+        codes = np.ascontiguousarray(q.q, np.uint8)
+        scales = np.ascontiguousarray(q.scales, np.float32)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_weight_fp8(self._ctx, codes.ctypes.data, scales.ctypes.data,
+                                              q.rows, q.cols, q.group, ctypes.byref(h)))
+        return Weight(self, h.value, q.rows, q.cols, L.W_FP8, q.group)
+
+    def weight_dequant_f32(self, w: Weight) -> np.ndarray:
+        """Test hook: the device's decode of `w` as f32 [rows*cols]."""
+        out = np.empty(w.rows * w.cols, np.float32)
+        self._check(self._lib.lx2v_weight_dequant_f32(self._ctx, w.handle, out.ctypes.data))
+        return out
+
+    def sync(self):
+        self._check(self._lib.lx2v_sync(self._ctx))
+
+    def stream(self) -> int:
+        return self._lib.lx2v_stream(self._ctx) or 0
+
+    # ---- profiling, backend.rs:192-196 ------------------------------------------
+    def profile_report(self) -> str | None:
+        prof = self.profile()
+        if not prof:
+            return None
+        total = sum(v["ms"] for v in prof.values()) or 1.0
+        lines = ["cuda profile (LIGHTX2V_PROFILE=1; device time per op):",
+                 "op                     calls      total_ms   mean_us   share"]
+        for name, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"]):
+            lines.append(f"{name:<20} {v['calls']:>8} {v['ms']:>12.3f} "
+                         f"{v['ms'] * 1e3 / max(v['calls'], 1):>9.1f} {v['ms'] / total * 100:>6.1f}%")
+        return "\n".join(lines) + "\n"
+
+    def profile(self) -> dict:
+        n = ctypes.c_size_t()
+        self._check(self._lib.lx2v_profile_json(self._ctx, None, 0, ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(n.value)
+        self._check(self._lib.lx2v_profile_json(self._ctx, buf, n.value, ctypes.byref(n)))
+        return json.loads(buf.value.decode())
+
+    def profile_reset(self):
+        self._check(self._lib.lx2v_profile_reset(self._ctx))
+
+    # ---- transformer, backend.rs:199-253 ------------------------------------------
+    def linear(self, x: Buf, x_row: int, rows: int, w: Weight, bias: Buf | None, act: int,
+               y: Buf, y_row: int):
+        """y[y_row + i, :] = act(x[x_row + i, :] . W^T + b) for i < rows."""
+        self._check(self._lib.lx2v_linear(self._ctx, x.handle, x_row, rows, w.handle,
+                                          bias.handle if bias is not None else None, act,
+                                          y.handle, y_row))
+
+    def linear_gate_residual(self, x: Buf, x_row: int, rows: int, w: Weight, bias: Buf | None,
+                             act: int, h: Buf, h_row: int, mods: Buf, gate: int):
+        """h[h_row + i, j] += act(x[x_row + i, :] . W^T + b)[j] * mods[gate * N + j]."""
+        self._check(self._lib.lx2v_linear_gate_residual(
+            self._ctx, x.handle, x_row, rows, w.handle,
+            bias.handle if bias is not None else None, act, h.handle, h_row, mods.handle, gate))
+
+    def gate_residual(self, h: Buf, a: Buf, rows: int, dim: int, mods: Buf, gate: int):
+        """In place on h: h += a * mods[gate] (backend.rs:244-253)."""
+        self._check(self._lib.lx2v_gate_residual(self._ctx, h.handle, a.handle, rows, dim,
+                                                 mods.handle, gate))
+
+    # ---- knobs ---------------------------------------------------------------------
+    def set_linear_path(self, path: int):
+        """0 automatic, 1 tensor-core GEMM, 2 small-M GEMV, 3 generic CUDA-core kernel."""
+        self._check(self._lib.lx2v_set_linear_path(self._ctx, path))
+
+    def set_wait_limit_ns(self, ns: int):
+        self._check(self._lib.lx2v_set_wait_limit_ns(self._ctx, ns))
+
+    def launch_count(self) -> int:
+        n = ctypes.c_uint64()
+        self._check(self._lib.lx2v_launch_count(self._ctx, ctypes.byref(n)))
+        return n.value

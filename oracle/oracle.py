@@ -1,0 +1,213 @@
+"""ctypes wrapper of the C oracle (lx2v_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA library. Only
+tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs
+import this module. Each function names the reference function it restates
+(path:line inside the lightx2v-rs project).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblx2v_oracle.so")
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_sz = ctypes.c_size_t
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (fast; a no-op when up to date)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.orc_normal.argtypes = [ctypes.c_uint64, _sz, ctypes.c_float, _f32p]
+        L.orc_uniform.argtypes = [ctypes.c_uint64, _sz, ctypes.c_float, _f32p]
+        L.orc_q8_quantize.argtypes = [_f32p, _sz, _sz, _i8p, _f32p]
+        L.orc_q8_quantize.restype = _sz
+        L.orc_q8_dequantize.argtypes = [_i8p, _f32p, _sz, _sz, _f32p]
+        L.orc_q4_quantize.argtypes = [_f32p, _sz, _sz, _sz, ctypes.c_int, _u8p, _f32p, _f32p]
+        L.orc_q4_quantize.restype = _sz
+        L.orc_q4_dequantize.argtypes = [_u8p, _f32p, _f32p, _sz, _sz, _f32p]
+        L.orc_q4_pack.argtypes = [_u8p, _sz, _u8p]
+        L.orc_q4_unpack.argtypes = [_u8p, _sz, _u8p]
+        L.orc_f32_to_e4m3.argtypes = [ctypes.c_float]
+        L.orc_f32_to_e4m3.restype = ctypes.c_uint8
+        L.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        L.orc_e4m3_to_f32.restype = ctypes.c_float
+        L.orc_fp8_quantize.argtypes = [_f32p, _sz, _sz, _u8p, _f32p]
+        L.orc_fp8_quantize.restype = _sz
+        L.orc_fp8_dequantize.argtypes = [_u8p, _f32p, _sz, _sz, _f32p]
+        L.orc_gelu_tanh.argtypes = [ctypes.c_float]
+        L.orc_gelu_tanh.restype = ctypes.c_float
+        L.orc_linear.argtypes = [_f32p, _sz, _sz, _f32p, _sz, _sz, _f32p, ctypes.c_int,
+                                 _f32p, _sz, ctypes.c_int]
+        L.orc_gate_residual.argtypes = [_f32p, _f32p, _sz, _sz, _f32p, _sz]
+        L.orc_openmp_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray, t):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(t)
+
+
+# ---- rng.rs:8-53 --------------------------------------------------------
+def normal(seed: int, n: int, std: float = 1.0) -> np.ndarray:
+    """`std * Rng::new(seed).normal(n)` (rng.rs:39-52)."""
+    out = np.empty(n, np.float32)
+    lib().orc_normal(seed, n, std, _p(out, _f32p))
+    return out
+
+
+def uniform(seed: int, n: int, a: float) -> np.ndarray:
+    """`Rng::new(seed).uniform(n, a)` (rng.rs:34-36)."""
+    out = np.empty(n, np.float32)
+    lib().orc_uniform(seed, n, a, _p(out, _f32p))
+    return out
+
+
+# ---- quant.rs -------------------------------------------------------------
+def q8_quantize(w: np.ndarray, rows: int, cols: int):
+    """Q8::quantize (quant.rs:154-178) -> (codes i8 [rows*cols], scales f32, group)."""
+    w = np.ascontiguousarray(w, np.float32).reshape(-1)
+    group = 128 if cols % 128 == 0 else cols
+    q = np.empty(rows * cols, np.int8)
+    s = np.empty(rows * cols // group, np.float32)
+    g = lib().orc_q8_quantize(_p(w, _f32p), rows, cols, _p(q, _i8p), _p(s, _f32p))
+    assert g == group
+    return q, s, group
+
+
+def q8_dequantize(q, scales, group) -> np.ndarray:
+    """Q8::dequantize (quant.rs:180-186)."""
+    q = np.ascontiguousarray(q, np.int8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    out = np.empty(q.size, np.float32)
+    lib().orc_q8_dequantize(_p(q, _i8p), _p(scales, _f32p), q.size, group, _p(out, _f32p))
+    return out
+
+
+def q4_quantize(w: np.ndarray, rows: int, cols: int, group: int, hqq: bool):
+    """Q4::quantize (quant.rs:226-292) -> (codes u8 one per byte, scales, zeros, group)."""
+    w = np.ascontiguousarray(w, np.float32).reshape(-1)
+    g_used = group if cols % group == 0 else cols
+    q = np.empty(rows * cols, np.uint8)
+    s = np.empty(rows * cols // g_used, np.float32)
+    z = np.empty_like(s)
+    g = lib().orc_q4_quantize(_p(w, _f32p), rows, cols, group, int(hqq), _p(q, _u8p),
+                              _p(s, _f32p), _p(z, _f32p))
+    assert g == g_used
+    return q, s, z, g_used
+
+
+def q4_dequantize(q, scales, zeros, group) -> np.ndarray:
+    """Q4::dequantize (quant.rs:294-303), codes one per byte."""
+    q = np.ascontiguousarray(q, np.uint8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    zeros = np.ascontiguousarray(zeros, np.float32)
+    out = np.empty(q.size, np.float32)
+    lib().orc_q4_dequantize(_p(q, _u8p), _p(scales, _f32p), _p(zeros, _f32p), q.size, group,
+                            _p(out, _f32p))
+    return out
+
+
+def q4_pack(q) -> np.ndarray:
+    """Q4::packed (quant.rs:306-311)."""
+    q = np.ascontiguousarray(q, np.uint8)
+    out = np.empty((q.size + 1) // 2, np.uint8)
+    lib().orc_q4_pack(_p(q, _u8p), q.size, _p(out, _u8p))
+    return out
+
+
+def q4_unpack(packed, n) -> np.ndarray:
+    """Q4::from_packed's code unpacking (quant.rs:324-326)."""
+    packed = np.ascontiguousarray(packed, np.uint8)
+    out = np.empty(n, np.uint8)
+    lib().orc_q4_unpack(_p(packed, _u8p), n, _p(out, _u8p))
+    return out
+
+
+def f32_to_e4m3(v: float) -> int:
+    """f32_to_e4m3 (quant.rs:376-406), defect included."""
+    return int(lib().orc_f32_to_e4m3(v))
+
+
+def e4m3_to_f32(code: int) -> float:
+    """e4m3_to_f32 (quant.rs:409-420)."""
+    return float(lib().orc_e4m3_to_f32(code))
+
+
+def fp8_quantize(w: np.ndarray, rows: int, cols: int):
+    """Fp8E4M3::quantize (quant.rs:423-447) -> (codes u8, scales f32, group)."""
+    w = np.ascontiguousarray(w, np.float32).reshape(-1)
+    group = 128 if cols % 128 == 0 else cols
+    q = np.empty(rows * cols, np.uint8)
+    s = np.empty(rows * cols // group, np.float32)
+    g = lib().orc_fp8_quantize(_p(w, _f32p), rows, cols, _p(q, _u8p), _p(s, _f32p))
+    assert g == group
+    return q, s, group
+
+
+def fp8_dequantize(q, scales, group) -> np.ndarray:
+    """Fp8E4M3::dequantize (quant.rs:449-455)."""
+    q = np.ascontiguousarray(q, np.uint8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    out = np.empty(q.size, np.float32)
+    lib().orc_fp8_dequantize(_p(q, _u8p), _p(scales, _f32p), q.size, group, _p(out, _f32p))
+    return out
+
+
+# ---- crates/lightx2v-cpu/src/lib.rs ----------------------------------------
+def gelu_tanh(x: float) -> float:
+    """gelu_tanh (lib.rs:151-153)."""
+    return float(lib().orc_gelu_tanh(x))
+
+
+def linear(x: np.ndarray, rows: int, w: np.ndarray, n: int, k: int, bias=None, act: int = 0,
+           x_row: int = 0, threads: int = 1) -> np.ndarray:
+    """CpuBackend::linear (lib.rs:296-326) on a dequantized f32 weight `w` [n, k].
+
+    Returns y [rows, n] (the rows the call writes, y_row = 0)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    w = np.ascontiguousarray(w, np.float32).reshape(-1)
+    assert w.size == n * k and x.size >= (x_row + rows) * k
+    y = np.empty(rows * n, np.float32)
+    bp = None
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, np.float32)
+        bp = _p(bias, _f32p)
+    lib().orc_linear(_p(x, _f32p), x_row, rows, _p(w, _f32p), n, k, bp, act, _p(y, _f32p), 0,
+                     threads)
+    return y.reshape(rows, n)
+
+
+def gate_residual(h: np.ndarray, a: np.ndarray, rows: int, dim: int, mods: np.ndarray,
+                  gate: int) -> np.ndarray:
+    """CpuBackend::gate_residual (lib.rs:394-404); returns the updated copy of h."""
+    h = np.array(h, np.float32, copy=True).reshape(-1)
+    a = np.ascontiguousarray(a, np.float32).reshape(-1)
+    mods = np.ascontiguousarray(mods, np.float32).reshape(-1)
+    lib().orc_gate_residual(_p(h, _f32p), _p(a, _f32p), rows, dim, _p(mods, _f32p), gate)
+    return h.reshape(rows, dim)
+
+
+def openmp_threads() -> int:
+    return int(lib().orc_openmp_threads())

@@ -1,0 +1,312 @@
+"""GPU parity of the quantized linear against the C oracle (restating
+CpuBackend::linear, crates/lightx2v-cpu/src/lib.rs:296-326, on weights
+dequantized by quant.rs). All calls go through the C ABI (lightx2v_cuda).
+
+Tolerances: dequantisation bit-exact; GEMM outputs
+rel-L2 <= 1e-2 against the f32 oracle, NaN-aware for FP8 (identical NaN
+masks, rel-L2 over the finite entries).
+"""
+import numpy as np
+import pytest
+
+from lightx2v_cuda import BF16, F32, Act, quant
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-2
+
+
+def rel_l2(got, want):
+    got = np.asarray(got, np.float64).reshape(-1)
+    want = np.asarray(want, np.float64).reshape(-1)
+    nan_g, nan_w = np.isnan(got), np.isnan(want)
+    assert np.array_equal(nan_g, nan_w), f"NaN masks differ: {nan_g.sum()} vs {nan_w.sum()}"
+    fin = ~nan_w
+    d = np.linalg.norm(got[fin] - want[fin])
+    n = np.linalg.norm(want[fin])
+    return d / n if n > 0 else d
+
+
+def make_weight(fmt, rows, cols, seed, std=0.02, group=64, hqq=True, oracle=None):
+    w = oracle.normal(seed, rows * cols, std)
+    if fmt == "q8":
+        q = quant.Q8.quantize(w, rows, cols)
+    elif fmt == "q4":
+        q = quant.Q4.quantize(w, rows, cols, group, hqq)
+    elif fmt == "fp8":
+        q = quant.Fp8E4M3.quantize(w, rows, cols)
+    else:
+        q = None
+    return w, q
+
+
+def oracle_dequant(oracle, fmt, q, w):
+    if fmt == "q8":
+        return oracle.q8_dequantize(q.q, q.scales, q.group)
+    if fmt == "q4":
+        return oracle.q4_dequantize(q.q, q.scales, q.zeros, q.group)
+    if fmt == "fp8":
+        return oracle.fp8_dequantize(q.q, q.scales, q.group)
+    return w
+
+
+def upload_weight(be, fmt, q, w, rows, cols):
+    if fmt == "q8":
+        return be.weight_q8(q)
+    if fmt == "q4":
+        return be.weight_q4(q)
+    if fmt == "fp8":
+        return be.weight_fp8(q)
+    return be.weight(w, rows, cols)
+
+
+# ---- dequantisation: bit-exact -------------------------------------------------
+@pytest.mark.parametrize("fmt,rows,cols,group", [
+    ("q8", 8960, 1536, None), ("q8", 1536, 8960, None), ("q8", 33, 200, None),
+    ("fp8", 4608, 1536, None), ("fp8", 1536, 8960, None), ("fp8", 17, 96, None),
+    ("q4", 8960, 1536, 64), ("q4", 64, 256, 16), ("q4", 9, 200, 64), ("q4", 8, 24, 8),
+])
+def test_dequant_bit_exact(be, oracle, fmt, rows, cols, group):
+    w, q = make_weight(fmt, rows, cols, seed=11 + rows, group=group or 64, hqq=(rows < 4096),
+                       oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, rows, cols)
+    got = be.weight_dequant_f32(dw)
+    want = oracle_dequant(oracle, fmt, q, w)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    fin = ~np.isnan(want)
+    assert np.array_equal(got[fin].view(np.uint32), want[fin].view(np.uint32))
+
+
+def test_fp8_special_codes_bit_exact(be, oracle):
+    # every code byte, including the NaN codes and the exponent-field-0 codes
+    # the reference decodes as m/8 * 2^-9, with fast and slow scales
+    rows, cols = 8, 256
+    codes = np.tile(np.arange(256, dtype=np.uint8), rows * cols // 256)
+    for scales in (np.full(rows * cols // 128, 0.01, np.float32),
+                   np.full(rows * cols // 128, 300.0, np.float32)):
+        q = quant.Fp8E4M3(codes.copy(), scales, rows, cols, 128)
+        got = be.weight_dequant_f32(be.weight_fp8(q))
+        want = oracle.fp8_dequantize(codes, scales, 128)
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        fin = ~np.isnan(want)
+        assert np.array_equal(got[fin].view(np.uint32), want[fin].view(np.uint32))
+
+
+# ---- linear: small shapes against the oracle ------------------------------------------
+@pytest.mark.parametrize("fmt", ["q8", "q4", "fp8", "native"])
+@pytest.mark.parametrize("M", [1, 3, 17, 129, 300])
+def test_linear_small_shapes(be, oracle, fmt, M):
+    N, K = 384, 256
+    w, q = make_weight(fmt, N, K, seed=3, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    x = oracle.normal(1, M * K)
+    b = oracle.normal(2, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b)
+    for act in (Act.NONE, Act.GELU_TANH):
+        for ydt in (BF16, F32):
+            yb = be.alloc(M * N, ydt)
+            be.linear(xb, 0, M, dw, bb, act, yb, 0)
+            got = be.download(yb).reshape(M, N)
+            want = oracle.linear(x, M, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=act,
+                                 threads=8)
+            assert rel_l2(got, want) <= REL_L2, (fmt, M, act, ydt)
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4", "fp8"])
+def test_tensor_core_path_matches_generic_path(be, oracle, fmt):
+    M, N, K = 300, 640, 512
+    w, q = make_weight(fmt, N, K, seed=5, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    xb = be.upload(oracle.normal(6, M * K))
+    bb = be.upload(oracle.normal(7, N, 0.01))
+    outs = []
+    for path in (1, 3):
+        be.set_linear_path(path)
+        yb = be.alloc(M * N, F32)
+        be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
+        outs.append(be.download(yb))
+    be.set_linear_path(0)
+    # same bf16 operands, different f32 summation order
+    assert rel_l2(outs[0], outs[1]) <= 1e-5
+
+
+def test_row_offsets_write_only_their_rows(be, oracle):
+    # linear(x, x_row, rows, ..., y, y_row) as the FFN chunk loop calls it
+    # (crates/lightx2v-model/src/dit.rs:735-759): other rows stay untouched.
+    N, K, M = 256, 256, 200
+    w, q = make_weight("q8", N, K, seed=8, oracle=oracle)
+    dw = be.weight_q8(q)
+    x = oracle.normal(9, M * K)
+    xb = be.upload(x)
+    sentinel = np.full(M * N, 7.0, np.float32)
+    yb = be.upload(sentinel, F32)
+    be.linear(xb, 40, 100, dw, None, Act.NONE, yb, 60)
+    y = be.download(yb).reshape(M, N)
+    assert np.all(y[:60] == 7.0) and np.all(y[160:] == 7.0)
+    want = oracle.linear(x, 100, q.dequantize(), N, K, x_row=40, threads=8)
+    assert rel_l2(y[60:160], want) <= REL_L2
+
+
+# ---- BASELINE shapes: sampled rows against the oracle -------------------------------------
+def sampled_rows(M, n=24):
+    rows = sorted(set(np.linspace(0, M - 1, n).astype(int).tolist() + [M - 1]))
+    return np.array(rows)
+
+
+def test_config1_q8_ffn_up(be, oracle):
+    # Q8, X [1560,1536] ~ N(0,1) seed 1, W [8960,1536] ~ N(0,0.02)
+    # seed 2, bias ~ N(0,0.01) seed 3, f32 output.
+    M, K, N = 1560, 1536, 8960
+    x = oracle.normal(1, M * K)
+    w = oracle.normal(2, N * K, 0.02)
+    b = oracle.normal(3, N, 0.01)
+    q = quant.Q8.quantize(w, N, K)
+    dw = be.weight_q8(q)
+    xb, bb = be.upload(x), be.upload(b)
+    yb = be.alloc(M * N, F32)
+    be.linear(xb, 0, M, dw, bb, Act.NONE, yb, 0)
+    y = be.download(yb).reshape(M, N)
+    rows = sampled_rows(M)
+    want = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, bias=b, x_row=int(r), threads=8)[0]
+                     for r in rows])
+    assert rel_l2(y[rows], want) <= REL_L2
+    assert np.isfinite(y).all()
+
+
+@pytest.mark.parametrize("name,N,K,act", [("qkv", 4608, 1536, Act.NONE), ("out", 1536, 1536, Act.NONE),
+                                          ("ffn1", 8960, 1536, Act.GELU_TANH),
+                                          ("ffn2", 1536, 8960, Act.NONE)])
+def test_config2_fp8_linear_set(be, oracle, name, N, K, act):
+    # FP8 e4m3 weights (the reference's group-128 layout),
+    # bf16 N(0,1) activations, M = 4680.
+    M = 4680
+    x = oracle.normal(21, M * K)
+    w = oracle.normal(22 + N + K, N * K, 0.02)
+    b = oracle.normal(23, N, 0.01)
+    q = quant.Fp8E4M3.quantize(w, N, K)
+    dw = be.weight_fp8(q)
+    xb, bb = be.upload(x), be.upload(b)
+    yb = be.alloc(M * N, BF16)
+    be.linear(xb, 0, M, dw, bb, act, yb, 0)
+    y = be.download(yb).reshape(M, N)
+    rows = sampled_rows(M, 16)
+    deq = q.dequantize()
+    want = np.stack([oracle.linear(x, 1, deq, N, K, bias=b, act=act, x_row=int(r), threads=8)[0]
+                     for r in rows])
+    assert rel_l2(y[rows], want) <= REL_L2
+
+
+def test_fused_gate_residual_matches_reference_sequence(be, oracle):
+    # dit.rs:748-760: FFN2 into tmp, then gate_residual(h += tmp * mods[GATE_FFN]).
+    M, N, K = 777, 1536, 1024
+    w, q = make_weight("fp8", N, K, seed=31, oracle=oracle)
+    dw = be.weight_fp8(q)
+    x = oracle.normal(32, M * K)
+    h0 = oracle.normal(33, M * N)
+    mods = oracle.normal(34, 6 * N, 0.5)
+    b = oracle.normal(35, N, 0.01)
+    xb, bb, mb = be.upload(x), be.upload(b), be.upload(mods, F32)
+    want = oracle.gate_residual(h0, oracle.linear(x, M, q.dequantize(), N, K, bias=b, threads=8),
+                                M, N, mods, 5)
+    h0m = h0.reshape(M, N)
+    for hdt in (F32, BF16):
+        # an f32 residual stream resolves the update itself; a bf16 one only
+        # to its own rounding, so it is compared as a whole
+        check = (lambda g: rel_l2(g - h0m, want - h0m)) if hdt == F32 else (lambda g: rel_l2(g, want))
+        hb = be.upload(h0, hdt)
+        be.linear_gate_residual(xb, 0, M, dw, bb, Act.NONE, hb, 0, mb, 5)
+        assert check(be.download(hb).reshape(M, N)) <= REL_L2, hdt
+        # the unfused sequence through the trait ops gives the same result
+        hb2 = be.upload(h0, hdt)
+        tmp = be.alloc(M * N, F32)
+        be.linear(xb, 0, M, dw, bb, Act.NONE, tmp, 0)
+        be.gate_residual(hb2, tmp, M, N, mb, 5)
+        assert check(be.download(hb2).reshape(M, N)) <= REL_L2, hdt
+
+
+# ---- the reference's conformance case and edge cases ----------------------------------------
+def test_check_linear_hand_case(be):
+    # crates/lightx2v-model/src/check.rs:74-103, tolerance 1e-6
+    x = np.array([1, 2, 3, 4, 5, 6], np.float32)
+    w = np.array([1, 0, -1, 0.5, 1, 0.5, 2, -1, 0, 0, 1, 2], np.float32)
+    b = np.array([0.5, -0.5, 1.0, 0.0], np.float32)
+    xb, yb, wb, bb = be.upload(x), be.alloc(8), be.weight(w, 4, 3), be.upload(b)
+    be.linear(xb, 0, 2, wb, bb, Act.NONE, yb, 0)
+    got = be.download(yb)
+    want = [b[o] + sum(x[r * 3 + i] * w[o * 3 + i] for i in range(3)) for r in range(2) for o in range(4)]
+    assert np.abs(got - np.array(want, np.float32)).max() <= 1e-6
+
+
+def test_zero_rows_and_empty_is_noop(be, oracle):
+    w, q = make_weight("q8", 128, 128, seed=1, oracle=oracle)
+    dw = be.weight_q8(q)
+    xb = be.upload(np.ones(128, np.float32))
+    yb = be.upload(np.full(128, 3.0, np.float32))
+    be.linear(xb, 0, 0, dw, None, Act.NONE, yb, 0)
+    assert np.all(be.download(yb) == 3.0)
+
+
+def test_errors_are_reported(be, oracle):
+    from lightx2v_cuda import _lib as L
+    w, q = make_weight("q8", 128, 128, seed=1, oracle=oracle)
+    dw = be.weight_q8(q)
+    xb = be.upload(np.ones(10 * 128, np.float32))
+    yb = be.alloc(10 * 128)
+    with pytest.raises(L.Lx2vError) as e:
+        be.linear(xb, 5, 10, dw, None, Act.NONE, yb, 0)  # x too short
+    assert e.value.status == L.ERR_INVALID
+    with pytest.raises(L.Lx2vError) as e:
+        be.linear(xb, 0, 10, dw, None, Act.NONE, xb, 0)  # output aliases input
+    assert e.value.status == L.ERR_INVALID
+    with pytest.raises(L.Lx2vError) as e:
+        be.linear(xb, 0, 10, dw, None, 7, yb, 0)
+    assert e.value.status == L.ERR_INVALID
+    with pytest.raises(L.Lx2vError):
+        be.weight_q4(quant.Q4(np.zeros(256, np.uint8), np.array([0.1], np.float32),
+                              np.array([0.0], np.float32), 1, 256, 256))  # 0.1 is not an f16 value
+
+
+def test_profile_report_lists_linear(be, oracle):
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path.insert(0, 'lightx2v-rs_b200');"
+        "import numpy as np; from lightx2v_cuda import CudaBackend, Act, quant;"
+        "be = CudaBackend(0); q = quant.Q8.quantize(np.ones(256*256, np.float32), 256, 256);"
+        "w = be.weight_q8(q); x = be.upload(np.ones(64*256, np.float32)); y = be.alloc(64*256);"
+        "be.linear(x, 0, 64, w, None, Act.NONE, y, 0); be.sync();"
+        "p = be.profile(); assert p['linear']['calls'] == 1 and p['linear']['ms'] > 0, p;"
+        "print(be.profile_report())")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
+                       env={**os.environ, "LIGHTX2V_PROFILE": "1"}, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "linear" in r.stdout
+
+
+def test_expired_wait_is_reported_and_context_survives(be, oracle):
+    """A pipeline wait that runs out stops the kernel with an error status
+    the host reads (no trap, no hang); the context stays usable."""
+    from lightx2v_cuda import _lib as L
+    M, N, K = 2048, 2048, 1536
+    w, q = make_weight("q8", N, K, seed=41, oracle=oracle)
+    dw = be.weight_q8(q)
+    x = oracle.normal(42, M * K)
+    xb = be.upload(x)
+    yb = be.alloc(M * N, F32)
+    be.sync()
+    be.set_wait_limit_ns(1)  # every wait that does not succeed at once expires
+    try:
+        be.linear(xb, 0, M, dw, None, Act.NONE, yb, 0)
+        with pytest.raises(L.Lx2vError) as e:
+            be.sync()
+        assert e.value.status == L.ERR_DEVICE
+    finally:
+        be.set_wait_limit_ns(2_000_000_000)
+    be.sync()  # error word was cleared
+    be.linear(xb, 0, M, dw, None, Act.NONE, yb, 0)
+    y = be.download(yb).reshape(M, N)
+    rows = sampled_rows(M, 8)
+    want = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, x_row=int(r), threads=8)[0] for r in rows])
+    assert rel_l2(y[rows], want) <= REL_L2

@@ -1,0 +1,87 @@
+"""The host-side mirror of lightx2v-core::quant / Rng (lightx2v_cuda.quant, .rng)
+against the C oracle, bit for bit, on BASELINE-sized matrices."""
+import numpy as np
+import pytest
+
+from lightx2v_cuda import quant, rng
+
+
+def test_rng_u64_stream_and_uniform_exact(oracle):
+    # rng.rs:20-36: the integer stream and uniform() are exact.
+    for seed in (0, 1, 17, 2 ** 63 + 5):
+        assert np.array_equal(rng.uniform(seed, 4097, 1.0), oracle.uniform(seed, 4097, 1.0))
+
+
+def test_rng_normal_within_four_ulp(oracle):
+    a = oracle.normal(3, 200001)
+    b = rng.normal(3, 200001)
+    ulp = np.spacing(np.maximum(np.abs(a), np.abs(b)).astype(np.float32))
+    # r and cos/sin can each be one ulp off glibc, so the product a few ulp
+    assert np.all(np.abs(a - b) <= 4 * ulp)
+    assert (a == b).mean() > 0.97
+
+
+@pytest.mark.parametrize("rows,cols", [(8960, 1536), (1536, 8960), (7, 200), (3, 128)])
+def test_q8_exact(oracle, rows, cols):
+    w = oracle.normal(2, rows * cols, 0.02)
+    m = quant.Q8.quantize(w, rows, cols)
+    q, s, g = oracle.q8_quantize(w, rows, cols)
+    assert m.group == g and np.array_equal(m.q, q) and np.array_equal(m.scales, s)
+    assert np.array_equal(m.dequantize().view(np.uint32), oracle.q8_dequantize(q, s, g).view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,cols", [(8960, 1536), (4608, 1536), (7, 200), (5, 384)])
+def test_fp8_exact(oracle, rows, cols):
+    w = oracle.normal(4, rows * cols, 0.02)
+    m = quant.Fp8E4M3.quantize(w, rows, cols)
+    q, s, g = oracle.fp8_quantize(w, rows, cols)
+    assert m.group == g and np.array_equal(m.q, q) and np.array_equal(m.scales, s)
+    d = oracle.fp8_dequantize(q, s, g)
+    md = m.dequantize()
+    assert np.array_equal(np.isnan(md), np.isnan(d))
+    fin = ~np.isnan(d)
+    assert np.array_equal(md[fin].view(np.uint32), d[fin].view(np.uint32))
+
+
+def test_fp8_encoder_edge_values(oracle):
+    vals = np.array([0.0, -0.0, 1.0, -1.0, 448.0, 464.0, 463.99, 1e-3, 2.0 ** -9, 2.0 ** -8,
+                     2.0 ** -7, 2.0 ** -10, 2.0 ** -12, 3e-5, 1e-8, np.inf, -np.inf, np.nan,
+                     255.9, 0.0078125 * 1.875, 0.0039, -0.005], np.float32)
+    got = quant.f32_to_e4m3(vals)
+    want = np.array([oracle.f32_to_e4m3(float(v)) for v in vals], np.uint8)
+    assert np.array_equal(got, want)
+    # every decode of the table equals the oracle's decode
+    t = quant.e4m3_decode_table()
+    for c in range(256):
+        o = oracle.e4m3_to_f32(c)
+        assert (np.isnan(t[c]) and np.isnan(o)) or t[c] == o
+
+
+@pytest.mark.parametrize("hqq", [False, True])
+@pytest.mark.parametrize("rows,cols,group", [(512, 1536, 64), (96, 8960, 64), (16, 256, 16),
+                                             (8, 200, 64)])
+def test_q4_exact(oracle, rows, cols, group, hqq):
+    w = oracle.normal(5, rows * cols, 0.02)
+    m = quant.Q4.quantize(w, rows, cols, group, hqq)
+    q, s, z, g = oracle.q4_quantize(w, rows, cols, group, hqq)
+    assert m.group == g
+    assert np.array_equal(m.q, q)
+    assert np.array_equal(m.scales, s) and np.array_equal(m.zeros, z)
+    assert np.array_equal(m.packed(), oracle.q4_pack(q))
+    assert np.array_equal(quant.Q4.from_packed(m.packed(), s, z, rows, cols).q, q)
+
+
+def test_weight_quant_parse_and_for_key():
+    # quant.rs:45-132 and the parse cases of quant.rs:513-525
+    WQ = quant.WeightQuant
+    assert WQ.parse("int4-hqq-g32") == WQ("int4", 32, True, False)
+    assert WQ.parse("fp8") == WQ("fp8")
+    assert WQ.parse("int4-hqq-g64-ffn").attn() == WQ("int8")
+    assert str(WQ.parse("int4-hqq-g64")) == "int4-hqq-g64"
+    with pytest.raises(ValueError):
+        WQ.parse("int4-g12")
+    q = WQ.parse("int4-hqq-g64-ffn")
+    assert q.for_key("blocks.3.ffn.net.0.proj") == q
+    assert q.for_key("blocks.3.attn1.to_q") == WQ("int8")
+    assert q.for_key("blocks.3.norm2") == WQ("native")
+    assert q.for_key("proj_out") == WQ("native")
