@@ -167,6 +167,9 @@ LX2V_API lx2v_status lx2v_profile_reset(lx2v_ctx *ctx);
  * 2 = small-M GEMV, 3 = generic CUDA-core kernel. A forced choice that cannot
  * run the shape returns LX2V_ERR_UNSUPPORTED. */
 LX2V_API lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path);
+/* Token tile of the tensor-core kernel: 0 = automatic, else 128, 192 or 256
+ * tokens per tile (each tile is 128 output features wide). */
+LX2V_API lx2v_status lx2v_set_token_tile(lx2v_ctx *ctx, int tokens);
 /* Bounded-wait limit of the pipelined kernels, in nanoseconds (default 2e9).
  * A wait that expires makes the kernel stop and record an error that the
  * next lx2v_sync returns as LX2V_ERR_DEVICE. */

@@ -7,19 +7,28 @@
 //   Q8   q as f32 * s                      crates/lightx2v-core/src/quant.rs:180-186
 //   Q4   (c as f32 - z) * s                quant.rs:294-303
 //   FP8  e4m3_to_f32(code) * s             quant.rs:409-420, 449-455
-// The GEMM rounds these to bf16 (round-to-nearest-even) for the tensor cores;
-// the lx2v_weight_dequant_f32 hook writes them out unrounded, so the hook's
-// bit-exact test also covers the arithmetic the GEMM uses.
+// The GEMM rounds each product to bf16 (round-to-nearest-even) for the tensor
+// cores; the lx2v_weight_dequant_f32 hook runs the same decode functions and
+// writes the products unrounded, so its bit-exact test covers the GEMM's
+// arithmetic too.
+//
+// Products are formed two at a time with the sm_100 packed f32 multiply
+// (__fmul2_rn: two independent IEEE round-to-nearest multiplies).
 //
 // Device layout of a weight (written once at upload, runtime.cu):
 //   codes    the reference's own flat code array: Q8 i8 [N*K], FP8 u8 [N*K],
 //            Q4 packed nibbles [(N*K+1)/2] (element 2i in the low nibble),
 //            native bf16 [N*K];
-//   scales   transposed to [G][N] (G = K/group) so that the scales a CTA
-//            needs for one k-block are contiguous: f32 for Q8/FP8, and
-//            (scale, zero) as a half2 word (low half = scale) for Q4.
+//   scales   transposed to [G][N] (G = K/group) so that the scales of one
+//            k-block are contiguous across rows: f32 for Q8/FP8, and
+//            (scale, zero) as a half2 word (low half = scale) for Q4;
+//   flags    FP8 only, one byte per (row, 32-column block): nonzero when the
+//            block holds a code that the fast decode does not cover (an
+//            exponent-field-0 code, a NaN code 0x7F/0xFF) or a scale outside
+//            [2^-100, 2^7). Those blocks take the reference formula.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -33,88 +42,113 @@ struct WeightView {
     const uint8_t *codes;
     const float *scales_t;  // Q8 / FP8: [G][N]
     const uint32_t *sz_t;   // Q4: [G][N], half2 bits (lo = scale, hi = zero)
-    int fp8_fast;           // every FP8 scale s satisfies 2^-100 <= s < 2^7
+    const uint8_t *flags;   // FP8: [N][ceil(K/32)]
 };
+
+__host__ __device__ inline int fp8_flag_cols(int k) { return (k + 31) / 32; }
 
 // e4m3_to_f32 as the reference defines it (quant.rs:409-420): exponent-field-0
 // codes are m/8 * 2^-9 (not the OCP m/8 * 2^-6), 0x7F / 0xFF are NaN.
-__device__ __forceinline__ float e4m3_ref(uint32_t code) {
+__host__ __device__ inline float e4m3_ref(uint32_t code) {
     const float sign = (code & 0x80u) ? -1.0f : 1.0f;
     const uint32_t e = (code >> 3) & 0xFu, m = code & 7u;
     if (e == 0) return sign * ((float)m / 8.0f) * 0x1p-9f;
-    if (e == 0xF && m == 7) return __int_as_float(0x7FC00000);
-    return sign * (1.0f + (float)m / 8.0f) * __int_as_float((int)((e + 120u) << 23));
+    if (e == 0xF && m == 7) {
+        const uint32_t nan_bits = 0x7FC00000u;
+        float f;
+        memcpy(&f, &nan_bits, 4);
+        return f;
+    }
+    uint32_t bits = (e + 120u) << 23;
+    float p2;
+    memcpy(&p2, &bits, 4);
+    return sign * (1.0f + (float)m / 8.0f) * p2;
 }
 
-// Nonzero when some byte of w is zero.
-__device__ __forceinline__ uint32_t has_zero_byte(uint32_t w) {
-    return (w - 0x01010101u) & ~w & 0x80808080u;
+// Whether a code needs the reference formula (exponent field 0 or NaN).
+__host__ __device__ inline bool fp8_code_special(uint32_t c) {
+    return ((c & 0x78u) == 0) || ((c & 0x7Fu) == 0x7Fu);
 }
+__host__ __device__ inline bool fp8_scale_fast(float s) { return s >= 0x1p-100f && s < 0x1p7f; }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float2 v) { return pack_bf16x2(v.x, v.y); }
 
 // ---- Q8 -----------------------------------------------------------------
-// 16 int8 codes (one uint4) times scale s. The code is turned into an exact
-// f32 with the 2^23 magic number: bits 0x4B0000xx = 2^23 + xx, xx = q + 128.
-__device__ __forceinline__ void dq_q8_unit(const uint4 raw, float s, float (&out)[16]) {
+// 16 int8 codes (one uint4) times scale s: p[i] = (q_{2i} * s, q_{2i+1} * s).
+// A code becomes an exact f32 with the 2^23 magic number: the bit pattern
+// 0x4B0000xx is 2^23 + xx, and xx = q + 128.
+__device__ __forceinline__ void q8_products(const uint4 raw, float s, float2 (&p)[8]) {
     const uint32_t w[4] = {raw.x ^ 0x80808080u, raw.y ^ 0x80808080u, raw.z ^ 0x80808080u,
                            raw.w ^ 0x80808080u};
+    const float2 off = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    const float2 s2 = make_float2(s, s);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float q = __int_as_float((int)__byte_perm(w[j], 0x4B000000u, 0x7440u + i)) -
-                            8388736.0f;  // 2^23 + 128
-            out[4 * j + i] = q * s;
+        for (int h = 0; h < 2; ++h) {
+            float2 q;
+            q.x = __int_as_float((int)__byte_perm(w[j], 0x4B000000u, 0x7440u + 2 * h));
+            q.y = __int_as_float((int)__byte_perm(w[j], 0x4B000000u, 0x7441u + 2 * h));
+            p[2 * j + h] = __fmul2_rn(__fadd2_rn(q, off), s2);
         }
     }
 }
 
 // ---- FP8 (reference e4m3) -----------------------------------------------
-// Fast path for a unit without exponent-field-0 or NaN codes and with a
-// scale in the fast range: a code's low 7 bits shifted to bit 20 are the
-// f32 bit pattern of |value| * 2^-120, so |value| * s = that float *
-// (s * 2^120), one correctly rounded multiply of the same real product.
-// The sign is then copied in from the code's bit 7.
-__device__ __forceinline__ void dq_fp8_unit(const uint4 raw, float s, bool fast_scale,
-                                            float (&out)[16]) {
+// Fast path, for a unit without special codes and with a fast-range scale: a
+// code's low 7 bits shifted to bit 20 are the f32 bit pattern of
+// |value| * 2^-120, so |value| * s = that float * (s * 2^120), one correctly
+// rounded multiply of the same real product. Returns the magnitudes; the
+// signs (code bit 7) are applied after rounding, which commutes with it.
+__device__ __forceinline__ void fp8_magnitudes(const uint4 raw, float s, float2 (&p)[8]) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t special = 0;
+    const float s120 = s * 0x1p120f;
+    const float2 s2 = make_float2(s120, s120);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        special |= has_zero_byte(w[j] & 0x78787878u);      // exponent field 0
-        special |= has_zero_byte(~w[j] & 0x7F7F7F7Fu);     // 0x7F / 0xFF (NaN)
+        float2 a, b;
+        a.x = __uint_as_float((w[j] << 20) & 0x07F00000u);
+        a.y = __uint_as_float((w[j] << 12) & 0x07F00000u);
+        b.x = __uint_as_float((w[j] << 4) & 0x07F00000u);
+        b.y = __uint_as_float((w[j] >> 4) & 0x07F00000u);
+        p[2 * j] = __fmul2_rn(a, s2);
+        p[2 * j + 1] = __fmul2_rn(b, s2);
     }
-    if (special == 0 && fast_scale) {
-        const float s120 = s * 0x1p120f;
+}
+// Sign bits of codes 2i, 2i+1 placed at bits 15 and 31 (a bf16x2 sign mask).
+__device__ __forceinline__ uint32_t fp8_sign_pair_bf16(const uint4 raw, int i) {
+    const uint32_t w = (i < 2) ? raw.x : (i < 4) ? raw.y : (i < 6) ? raw.z : raw.w;
+    return __byte_perm(w, 0u, (i & 1) ? 0x3424u : 0x1404u) & 0x80008000u;
+}
+// Reference-formula path: signed products.
+__device__ __forceinline__ void fp8_products_slow(const uint4 raw, float s, float2 (&p)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t c = (w[j] >> (8 * i)) & 0xFFu;
-                const float mag = __int_as_float((int)((c & 0x7Fu) << 20)) * s120;
-                out[4 * j + i] = __int_as_float(__float_as_int(mag) ^ (int)((c & 0x80u) << 24));
-            }
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) out[4 * j + i] = e4m3_ref((w[j] >> (8 * i)) & 0xFFu) * s;
-        }
+    for (int j = 0; j < 4; ++j) {
+        p[2 * j] = make_float2(e4m3_ref(w[j] & 0xFFu) * s, e4m3_ref((w[j] >> 8) & 0xFFu) * s);
+        p[2 * j + 1] = make_float2(e4m3_ref((w[j] >> 16) & 0xFFu) * s, e4m3_ref(w[j] >> 24) * s);
     }
 }
 
 // ---- Q4 -----------------------------------------------------------------
 // 16 nibbles (one uint2; element 2i in the low nibble) with f16-exact scale
-// s and zero z: (c - z) * s, two roundings as the reference does them.
-__device__ __forceinline__ void dq_q4_unit(const uint2 raw, float s, float z, float (&out)[16]) {
+// s and zero z: (c - z) * s with the reference's two roundings.
+__device__ __forceinline__ void q4_products(const uint2 raw, float s, float z, float2 (&p)[8]) {
     const uint32_t w[2] = {raw.x, raw.y};
+    const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
+    const float2 nz = make_float2(-z, -z), s2 = make_float2(s, s);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t c = (w[j] >> (4 * i)) & 0xFu;
-            const float cf = __int_as_float((int)(0x4B000000u | c)) - 8388608.0f;
-            out[8 * j + i] = (cf - z) * s;
+        for (int i = 0; i < 4; ++i) {
+            float2 c;
+            c.x = __uint_as_float(((w[j] >> (8 * i)) & 0xFu) | 0x4B000000u);
+            c.y = __uint_as_float(((w[j] >> (8 * i + 4)) & 0xFu) | 0x4B000000u);
+            p[4 * j + i] = __fmul2_rn(__fadd2_rn(__fadd2_rn(c, m23), nz), s2);
         }
     }
 }
@@ -125,8 +159,63 @@ __device__ __forceinline__ void q4_scale_zero(uint32_t sz, float &s, float &z) {
     z = __high2float(h);
 }
 
+// ---- one unit, f32 out (hook) or bf16x2 out (GEMM) ---------------------------
+// `raw` holds the unit's codes: 16 bytes (Q8/FP8), 8 bytes in .x/.y (Q4),
+// or 32 bytes of bf16 split over raw/raw2 (native).
+template <int FMT>
+__device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, float s, float z,
+                                             bool fp8_slow, uint32_t (&out)[8]) {
+    if (FMT == FMT_BF16) {
+        out[0] = raw.x; out[1] = raw.y; out[2] = raw.z; out[3] = raw.w;
+        out[4] = raw2.x; out[5] = raw2.y; out[6] = raw2.z; out[7] = raw2.w;
+        return;
+    }
+    float2 p[8];
+    if (FMT == FMT_Q8) {
+        q8_products(raw, s, p);
+    } else if (FMT == FMT_Q4) {
+        q4_products(make_uint2(raw.x, raw.y), s, z, p);
+    } else {
+        if (!fp8_slow) {
+            fp8_magnitudes(raw, s, p);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]) ^ fp8_sign_pair_bf16(raw, i);
+            return;
+        }
+        fp8_products_slow(raw, s, p);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]);
+}
+
+template <int FMT>
+__device__ __forceinline__ void unit_to_f32(const uint4 raw, float s, float z, bool fp8_slow,
+                                            float (&out)[16]) {
+    float2 p[8];
+    if (FMT == FMT_Q8) {
+        q8_products(raw, s, p);
+    } else if (FMT == FMT_Q4) {
+        q4_products(make_uint2(raw.x, raw.y), s, z, p);
+    } else {
+        if (!fp8_slow) {
+            fp8_magnitudes(raw, s, p);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t sign = ((w[i >> 2] >> (8 * (i & 3))) & 0x80u) << 24;
+                const float mag = (i & 1) ? p[i >> 1].y : p[i >> 1].x;
+                out[i] = __uint_as_float(__float_as_uint(mag) ^ sign);
+            }
+            return;
+        }
+        fp8_products_slow(raw, s, p);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { out[2 * i] = p[i].x; out[2 * i + 1] = p[i].y; }
+}
+
 // ---- generic element access (any shape) ---------------------------------
-// Flat element i = n*K + k of the reference's code array; group index is
+// Flat element i = n*K + k of the reference's code array; the group index is
 // i / group over the flat array, which equals n * (K/group) + k/group.
 __device__ __forceinline__ float dq_elem(const WeightView &w, int64_t n, int64_t k) {
     const int64_t i = n * (int64_t)w.k + k;
@@ -147,8 +236,8 @@ __device__ __forceinline__ float dq_elem(const WeightView &w, int64_t n, int64_t
     }
 }
 
-// Whether the 16-value unit path applies: rows start 16-byte aligned, units
-// never straddle a group.
+// Whether the 16-value unit path applies: rows start 16-byte aligned and a
+// unit never straddles a group.
 __host__ __device__ inline bool unit_path_ok(int fmt, int k, int group) {
     if (group % 16 != 0) return false;
     switch (fmt) {
@@ -157,41 +246,6 @@ __host__ __device__ inline bool unit_path_ok(int fmt, int k, int group) {
         case FMT_Q4: return k % 32 == 0;
         default: return k % 8 == 0;
     }
-}
-
-// Decode the unit of row n starting at column k0 (k0 % 16 == 0, k0 < K).
-__device__ __forceinline__ void dq_unit(const WeightView &w, int n, int k0, float (&out)[16]) {
-    const int64_t base = (int64_t)n * w.k + k0;
-    const int64_t g = k0 / w.group;
-    switch (w.fmt) {
-        case FMT_Q8: {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(w.codes + base);
-            dq_q8_unit(raw, w.scales_t[g * w.n + n], out);
-            break;
-        }
-        case FMT_FP8: {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(w.codes + base);
-            dq_fp8_unit(raw, w.scales_t[g * w.n + n], w.fp8_fast != 0, out);
-            break;
-        }
-        case FMT_Q4: {
-            const uint2 raw = *reinterpret_cast<const uint2 *>(w.codes + base / 2);
-            float s, z;
-            q4_scale_zero(w.sz_t[g * w.n + n], s, z);
-            dq_q4_unit(raw, s, z, out);
-            break;
-        }
-        default: {
-            const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(w.codes) + base;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) out[i] = __bfloat162float(p[i]);
-        }
-    }
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t *>(&v);
 }
 
 }  // namespace lx2v

@@ -9,10 +9,12 @@ namespace lx2v {
 // Everything one linear launch needs; passed by value as a __grid_constant__.
 struct alignas(64) GemmParams {
     CUtensorMap tmap_x;  // x: bf16 [x_row + M, K], box {64, BT}, 128-byte swizzle
+    CUtensorMap tmap_w;  // weight codes [N rows], box {one 64-wide k-block, 128 rows}
     CUtensorMap tmap_y;  // y (or h): bf16/f32 [y_row + M, N], box {128, 32}
     const uint8_t *codes;     // weight codes in the reference layout (dequant.cuh)
     const float *scales_t;    // Q8/FP8 scales, [G][N]
     const uint32_t *sz_t;     // Q4 (scale, zero) half2 words, [G][N]
+    const uint8_t *flags;     // FP8 slow-block flags, [N][ceil(K/32)]
     const void *bias;         // [N] or null
     const void *gate;         // [N] (mods + gate * N) or null
     int *err;                 // error word (ptx.cuh error codes)
@@ -23,12 +25,11 @@ struct alignas(64) GemmParams {
     int out_f32;              // y element type: 1 f32, 0 bf16
     int reduce;               // 1: reduce-add into y (gated residual)
     int bias_f32, gate_f32;   // element types of bias / gate
-    int fp8_fast;
 };
 
 // Tensor-core (tcgen05) dequant GEMM. `bt` = token tile (128, 192 or 256).
 cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
-int gemm_dq_token_tile(int M);
+int gemm_dq_token_tile(int M, int N, int num_sms);
 
 // Small-M path and the generic CUDA-core path (kernels.cu); they take plain
 // pointers instead of tensor maps.
@@ -37,7 +38,7 @@ struct LinearArgs {
     const uint8_t *codes;
     const float *scales_t;
     const uint32_t *sz_t;
-    int fp8_fast;
+    const uint8_t *flags;
     int M, N, K, group;
     const void *x; int x_f32; int64_t x_row;
     void *y; int y_f32; int64_t y_row;
@@ -55,7 +56,7 @@ cudaError_t convert_launch(const void *src, int src_f32, void *dst, int dst_f32,
 cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, const void *gate,
                                  int gate_f32, size_t rows, size_t dim, cudaStream_t st);
 cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,
-                               const uint32_t *sz_t, int fp8_fast, int N, int K, int group,
+                               const uint32_t *sz_t, const uint8_t *flags, int N, int K, int group,
                                float *out, cudaStream_t st);
 
 }  // namespace lx2v

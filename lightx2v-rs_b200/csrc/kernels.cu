@@ -63,15 +63,33 @@ cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, c
 }
 
 // ---- dequant hook ------------------------------------------------------------
-// Unit path: the same decode functions the GEMM's dequant warps run.
+// Unit path: the same decode functions the GEMM's dequant warps run, with
+// the same fast/reference split for FP8.
+template <int FMT>
 __global__ void dequant_units_kernel(WeightView w, float *out) {
     const int units_per_row = w.k / 16;
+    const int ku = fp8_flag_cols(w.k);
     const int64_t total = (int64_t)w.n * units_per_row;
     for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
         const int n = (int)(u / units_per_row), k0 = (int)(u % units_per_row) * 16;
+        const int64_t base = (int64_t)n * w.k + k0;
+        const int64_t g = k0 / w.group;
         float v[16];
-        dq_unit(w, n, k0, v);
-        float4 *o = reinterpret_cast<float4 *>(out + (int64_t)n * w.k + k0);
+        if (FMT == FMT_Q4) {
+            const uint2 raw = *reinterpret_cast<const uint2 *>(w.codes + base / 2);
+            float s, z;
+            q4_scale_zero(w.sz_t[g * w.n + n], s, z);
+            unit_to_f32<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), s, z, false, v);
+        } else if (FMT == FMT_BF16) {
+            const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(w.codes) + base;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(p[i]);
+        } else {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(w.codes + base);
+            const bool slow = FMT == FMT_FP8 && w.flags[(int64_t)n * ku + k0 / 32] != 0;
+            unit_to_f32<FMT>(raw, w.scales_t[g * w.n + n], 0.0f, slow, v);
+        }
+        float4 *o = reinterpret_cast<float4 *>(out + base);
 #pragma unroll
         for (int i = 0; i < 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
@@ -84,12 +102,18 @@ __global__ void dequant_elems_kernel(WeightView w, float *out) {
 }
 
 cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,
-                               const uint32_t *sz_t, int fp8_fast, int N, int K, int group,
+                               const uint32_t *sz_t, const uint8_t *flags, int N, int K, int group,
                                float *out, cudaStream_t st) {
-    WeightView w{fmt, N, K, group, codes, scales_t, sz_t, fp8_fast};
+    WeightView w{fmt, N, K, group, codes, scales_t, sz_t, flags};
     if ((size_t)N * K == 0) return cudaSuccess;
     if (unit_path_ok(fmt, K, group)) {
-        dequant_units_kernel<<<grid_for((size_t)N * K / 16, 256), 256, 0, st>>>(w, out);
+        const int g = grid_for((size_t)N * K / 16, 256);
+        switch (fmt) {
+            case FMT_Q8: dequant_units_kernel<FMT_Q8><<<g, 256, 0, st>>>(w, out); break;
+            case FMT_Q4: dequant_units_kernel<FMT_Q4><<<g, 256, 0, st>>>(w, out); break;
+            case FMT_FP8: dequant_units_kernel<FMT_FP8><<<g, 256, 0, st>>>(w, out); break;
+            default: dequant_units_kernel<FMT_BF16><<<g, 256, 0, st>>>(w, out); break;
+        }
     } else {
         dequant_elems_kernel<<<grid_for((size_t)N * K, 256), 256, 0, st>>>(w, out);
     }
@@ -105,7 +129,7 @@ __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(_
 __global__ void __launch_bounds__(256) linear_simt_kernel(LinearArgs a) {
     __shared__ float xs[16][65];
     __shared__ float ws[16][65];
-    WeightView w{a.fmt, a.N, a.K, a.group, a.codes, a.scales_t, a.sz_t, a.fp8_fast};
+    WeightView w{a.fmt, a.N, a.K, a.group, a.codes, a.scales_t, a.sz_t, a.flags};
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
     float acc[4][4] = {};

@@ -39,6 +39,7 @@ struct lx2v_ctx {
     int *err_dev = nullptr;
     uint64_t wait_limit_ns = 2000000000ull;
     int path = 0;
+    int token_tile = 0;
     uint64_t launches = 0;
     bool profile = false;
     std::map<std::string, ProfEntry> prof;
@@ -62,7 +63,7 @@ struct lx2v_weight {
     void *codes = nullptr;
     float *scales_t = nullptr;
     uint32_t *sz_t = nullptr;
-    int fp8_fast = 0;
+    uint8_t *flags = nullptr;  // FP8: [rows][ceil(cols/32)] blocks that need the reference formula
 };
 
 static thread_local std::string g_init_err;
@@ -388,6 +389,7 @@ static void weight_release(lx2v_weight *w) {
     if (w->codes) cudaFree(w->codes);
     if (w->scales_t) cudaFree(w->scales_t);
     if (w->sz_t) cudaFree(w->sz_t);
+    if (w->flags) cudaFree(w->flags);
     delete w;
 }
 
@@ -473,14 +475,25 @@ extern "C" lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const fl
     auto *w = new lx2v_weight();
     w->fmt = LX2V_W_FP8; w->rows = rows; w->cols = cols; w->group = group;
     const size_t G = cols / group;
-    bool fast = true;
-    for (size_t i = 0; i < rows * G; ++i) {
-        const float v = scales[i];
-        if (!(v >= 0x1p-100f && v < 0x1p7f)) fast = false;
+    // One flag byte per (row, 32-column block): the block holds a code the
+    // fast decode does not cover, or a scale outside its range.
+    const size_t ku = (size_t)fp8_flag_cols((int)cols);
+    std::vector<uint8_t> flags(rows * ku, 0);
+    for (size_t r = 0; r < rows; ++r) {
+        for (size_t c = 0; c < cols; ++c) {
+            const bool bad = fp8_code_special(q[r * cols + c]) || !fp8_scale_fast(scales[r * G + c / group]);
+            if (bad) flags[r * ku + c / 32] = 1;
+        }
     }
-    w->fp8_fast = fast ? 1 : 0;
     auto st = transpose_scales(scales, rows, G);
     if ((s = upload_codes_scales(ctx, w, q, rows * cols, &st, nullptr))) { weight_release(w); return s; }
+    cudaError_t e = cudaMalloc(&w->flags, flags.size());
+    if (e == cudaSuccess) e = cudaMemcpy(w->flags, flags.data(), flags.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        weight_release(w);
+        return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA, "weight upload: %s",
+                    cudaGetErrorString(e));
+    }
     *out = w;
     return LX2V_OK;
 }
@@ -545,7 +558,7 @@ extern "C" lx2v_status lx2v_weight_dequant_f32(lx2v_ctx *ctx, const lx2v_weight 
     if (!w || !out) return fail(ctx, LX2V_ERR_INVALID, "null weight or output");
     const size_t n = w->rows * w->cols;
     if ((s = ensure_staging(ctx, n * 4))) return s;
-    CUDA_TRY(ctx, dequant_f32_launch(w->fmt, (const uint8_t *)w->codes, w->scales_t, w->sz_t, w->fp8_fast,
+    CUDA_TRY(ctx, dequant_f32_launch(w->fmt, (const uint8_t *)w->codes, w->scales_t, w->sz_t, w->flags,
                                      (int)w->rows, (int)w->cols, (int)w->group, (float *)ctx->staging,
                                      ctx->stream));
     ctx->launches++;
@@ -604,9 +617,21 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     if (path == 1) {
         GemmParams p;
         memset(&p, 0, sizeof p);
-        const int bt = gemm_dq_token_tile((int)rows);
+        const int bt = ctx->token_tile ? ctx->token_tile : gemm_dq_token_tile((int)rows, (int)N, ctx->num_sms);
         lx2v_status s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
                                  (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (s) return s;
+        // Code tile of one stage: 128 weight rows x one 64-wide k-block, with
+        // the swizzle that makes the dequant threads' row reads conflict free.
+        if (w->fmt == LX2V_W_Q4)
+            s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 32, 128,
+                         CU_TENSOR_MAP_SWIZZLE_32B);
+        else if (w->fmt == LX2V_W_BF16)
+            s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+        else
+            s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
         if (s) return s;
         s = make_map(ctx, &p.tmap_y, y->ptr,
                      y->dtype == LX2V_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
@@ -615,7 +640,7 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         p.codes = (const uint8_t *)w->codes;
         p.scales_t = w->scales_t;
         p.sz_t = w->sz_t;
-        p.fp8_fast = w->fp8_fast;
+        p.flags = w->flags;
         p.bias = bias ? bias->ptr : nullptr;
         p.bias_f32 = bias && bias->dtype == LX2V_F32;
         p.gate = gate_ptr;
@@ -634,7 +659,7 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     LinearArgs a;
     memset(&a, 0, sizeof a);
     a.fmt = w->fmt; a.codes = (const uint8_t *)w->codes; a.scales_t = w->scales_t; a.sz_t = w->sz_t;
-    a.fp8_fast = w->fp8_fast;
+    a.flags = w->flags;
     a.M = (int)rows; a.N = (int)N; a.K = (int)K; a.group = (int)w->group;
     a.x = x->ptr; a.x_f32 = x->dtype == LX2V_F32; a.x_row = (int64_t)x_row;
     a.y = y->ptr; a.y_f32 = y->dtype == LX2V_F32; a.y_row = (int64_t)y_row;
@@ -711,6 +736,14 @@ extern "C" lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path) {
     if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
     if (path < 0 || path > 3) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
     ctx->path = path;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_set_token_tile(lx2v_ctx *ctx, int tokens) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (tokens != 0 && tokens != 128 && tokens != 192 && tokens != 256)
+        return fail(ctx, LX2V_ERR_INVALID, "token tile must be 0 (automatic), 128, 192 or 256, got %d", tokens);
+    ctx->token_tile = tokens;
     return LX2V_OK;
 }
 

@@ -255,6 +255,10 @@ class CudaBackend:
         """0 automatic, 1 tensor-core GEMM, 2 small-M GEMV, 3 generic CUDA-core kernel."""
         self._check(self._lib.lx2v_set_linear_path(self._ctx, path))
 
+    def set_token_tile(self, tokens: int):
+        """Tokens per tensor-core tile: 0 automatic, or 128 / 192 / 256."""
+        self._check(self._lib.lx2v_set_token_tile(self._ctx, tokens))
+
     def set_wait_limit_ns(self, ns: int):
         self._check(self._lib.lx2v_set_wait_limit_ns(self._ctx, ns))
 
