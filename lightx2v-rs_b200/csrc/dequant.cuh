@@ -22,10 +22,12 @@
 //   scales   transposed to [G][N] (G = K/group) so that the scales of one
 //            k-block are contiguous across rows: f32 for Q8/FP8, and
 //            (scale, zero) as a half2 word (low half = scale) for Q4;
-//   flags    FP8 only, one byte per (row, 32-column block): nonzero when the
-//            block holds a code that the fast decode does not cover (an
-//            exponent-field-0 code, a NaN code 0x7F/0xFF) or a scale outside
-//            [2^-100, 2^7). Those blocks take the reference formula.
+//   flags    FP8 only, one byte per (32-column block, row), stored [K/32][N]
+//            so one k-block's flags are contiguous across rows: 0 = fast decode;
+//            1 = the block holds a code the fast decode does not cover (an
+//            exponent-field-0 code, a NaN code 0x7F/0xFF) and takes the fast
+//            decode plus an exact fix-up; 2 = a scale outside [2^-100, 2^7),
+//            the block takes the reference formula.
 #pragma once
 #include <cstdint>
 #include <cstring>
@@ -42,7 +44,7 @@ struct WeightView {
     const uint8_t *codes;
     const float *scales_t;  // Q8 / FP8: [G][N]
     const uint32_t *sz_t;   // Q4: [G][N], half2 bits (lo = scale, hi = zero)
-    const uint8_t *flags;   // FP8: [N][ceil(K/32)]
+    const uint8_t *flags;   // FP8: [ceil(K/32)][N]
 };
 
 __host__ __device__ inline int fp8_flag_cols(int k) { return (k + 31) / 32; }
@@ -124,6 +126,24 @@ __device__ __forceinline__ uint32_t fp8_sign_pair_bf16(const uint4 raw, int i) {
     const uint32_t w = (i < 2) ? raw.x : (i < 4) ? raw.y : (i < 6) ? raw.z : raw.w;
     return __byte_perm(w, 0u, (i & 1) ? 0x3424u : 0x1404u) & 0x80008000u;
 }
+// Fix-up of fast-path magnitudes for a block that holds special codes (its
+// scale is in the fast range): an exponent-field-0 code m decodes to
+// m/8 * 2^-9 (quant.rs:413-414) but the fast formula gives m * 2^-9, so the
+// product is scaled by 2^-3 (exact: the fast product is at least 2^-109);
+// the NaN codes 0x7F / 0xFF become NaN.
+__device__ __forceinline__ void fp8_fixup(const uint4 raw, float2 (&p)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const float qnan = __uint_as_float(0x7FC00000u);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const uint32_t c = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        float v = (i & 1) ? p[i >> 1].y : p[i >> 1].x;
+        v = ((c & 0x78u) == 0) ? v * 0.125f : v;
+        v = ((c & 0x7Fu) == 0x7Fu) ? qnan : v;
+        if (i & 1) p[i >> 1].y = v; else p[i >> 1].x = v;
+    }
+}
+
 // Reference-formula path: signed products.
 __device__ __forceinline__ void fp8_products_slow(const uint4 raw, float s, float2 (&p)[8]) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -162,9 +182,10 @@ __device__ __forceinline__ void q4_scale_zero(uint32_t sz, float &s, float &z) {
 // ---- one unit, f32 out (hook) or bf16x2 out (GEMM) ---------------------------
 // `raw` holds the unit's codes: 16 bytes (Q8/FP8), 8 bytes in .x/.y (Q4),
 // or 32 bytes of bf16 split over raw/raw2 (native).
+// fp8_mode: 0 fast, 1 fast + special-code fix-up, 2 reference formula.
 template <int FMT>
 __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, float s, float z,
-                                             bool fp8_slow, uint32_t (&out)[8]) {
+                                             int fp8_mode, uint32_t (&out)[8]) {
     if (FMT == FMT_BF16) {
         out[0] = raw.x; out[1] = raw.y; out[2] = raw.z; out[3] = raw.w;
         out[4] = raw2.x; out[5] = raw2.y; out[6] = raw2.z; out[7] = raw2.w;
@@ -176,8 +197,9 @@ __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, 
     } else if (FMT == FMT_Q4) {
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
     } else {
-        if (!fp8_slow) {
+        if (fp8_mode != 2) {
             fp8_magnitudes(raw, s, p);
+            if (fp8_mode == 1) fp8_fixup(raw, p);
 #pragma unroll
             for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]) ^ fp8_sign_pair_bf16(raw, i);
             return;
@@ -189,7 +211,7 @@ __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, 
 }
 
 template <int FMT>
-__device__ __forceinline__ void unit_to_f32(const uint4 raw, float s, float z, bool fp8_slow,
+__device__ __forceinline__ void unit_to_f32(const uint4 raw, float s, float z, int fp8_mode,
                                             float (&out)[16]) {
     float2 p[8];
     if (FMT == FMT_Q8) {
@@ -197,8 +219,9 @@ __device__ __forceinline__ void unit_to_f32(const uint4 raw, float s, float z, b
     } else if (FMT == FMT_Q4) {
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
     } else {
-        if (!fp8_slow) {
+        if (fp8_mode != 2) {
             fp8_magnitudes(raw, s, p);
+            if (fp8_mode == 1) fp8_fixup(raw, p);
             const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
             for (int i = 0; i < 16; ++i) {

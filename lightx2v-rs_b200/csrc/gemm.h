@@ -10,11 +10,12 @@ namespace lx2v {
 struct alignas(64) GemmParams {
     CUtensorMap tmap_x;  // x: bf16 [x_row + M, K], box {64, BT}, 128-byte swizzle
     CUtensorMap tmap_w;  // weight codes [N rows], box {one 64-wide k-block, 128 rows}
-    CUtensorMap tmap_y;  // y (or h): bf16/f32 [y_row + M, N], box {128, 32}
+    CUtensorMap tmap_s;  // scale words [G][N] (4 bytes each), box {128 rows, sgrp groups}
+    CUtensorMap tmap_f;  // FP8 block flags [ceil(K/32)][N] bytes, box {128 rows, 2}
+    void *y;                  // output (or h for the gated residual)
     const uint8_t *codes;     // weight codes in the reference layout (dequant.cuh)
     const float *scales_t;    // Q8/FP8 scales, [G][N]
     const uint32_t *sz_t;     // Q4 (scale, zero) half2 words, [G][N]
-    const uint8_t *flags;     // FP8 slow-block flags, [N][ceil(K/32)]
     const void *bias;         // [N] or null
     const void *gate;         // [N] (mods + gate * N) or null
     int *err;                 // error word (ptx.cuh error codes)
@@ -25,6 +26,7 @@ struct alignas(64) GemmParams {
     int out_f32;              // y element type: 1 f32, 0 bf16
     int reduce;               // 1: reduce-add into y (gated residual)
     int bias_f32, gate_f32;   // element types of bias / gate
+    int sgrp;                 // scale groups per k-block box (1, 2 or 4)
 };
 
 // Tensor-core (tcgen05) dequant GEMM. `bt` = token tile (128, 192 or 256).
@@ -38,7 +40,7 @@ struct LinearArgs {
     const uint8_t *codes;
     const float *scales_t;
     const uint32_t *sz_t;
-    const uint8_t *flags;
+    const uint8_t *flags;     // FP8 block flags, [ceil(K/32)][N]
     int M, N, K, group;
     const void *x; int x_f32; int64_t x_row;
     void *y; int y_f32; int64_t y_row;

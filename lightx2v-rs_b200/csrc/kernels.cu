@@ -68,7 +68,6 @@ cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, c
 template <int FMT>
 __global__ void dequant_units_kernel(WeightView w, float *out) {
     const int units_per_row = w.k / 16;
-    const int ku = fp8_flag_cols(w.k);
     const int64_t total = (int64_t)w.n * units_per_row;
     for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
         const int n = (int)(u / units_per_row), k0 = (int)(u % units_per_row) * 16;
@@ -79,15 +78,15 @@ __global__ void dequant_units_kernel(WeightView w, float *out) {
             const uint2 raw = *reinterpret_cast<const uint2 *>(w.codes + base / 2);
             float s, z;
             q4_scale_zero(w.sz_t[g * w.n + n], s, z);
-            unit_to_f32<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), s, z, false, v);
+            unit_to_f32<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), s, z, 0, v);
         } else if (FMT == FMT_BF16) {
             const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(w.codes) + base;
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(p[i]);
         } else {
             const uint4 raw = *reinterpret_cast<const uint4 *>(w.codes + base);
-            const bool slow = FMT == FMT_FP8 && w.flags[(int64_t)n * ku + k0 / 32] != 0;
-            unit_to_f32<FMT>(raw, w.scales_t[g * w.n + n], 0.0f, slow, v);
+            const int mode = FMT == FMT_FP8 ? w.flags[(int64_t)(k0 / 32) * w.n + n] : 0;
+            unit_to_f32<FMT>(raw, w.scales_t[g * w.n + n], 0.0f, mode, v);
         }
         float4 *o = reinterpret_cast<float4 *>(out + base);
 #pragma unroll

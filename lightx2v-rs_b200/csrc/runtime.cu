@@ -63,7 +63,7 @@ struct lx2v_weight {
     void *codes = nullptr;
     float *scales_t = nullptr;
     uint32_t *sz_t = nullptr;
-    uint8_t *flags = nullptr;  // FP8: [rows][ceil(cols/32)] blocks that need the reference formula
+    uint8_t *flags = nullptr;  // FP8: [ceil(cols/32)][rows] blocks needing the fix-up / reference formula
 };
 
 static thread_local std::string g_init_err;
@@ -475,19 +475,21 @@ extern "C" lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const fl
     auto *w = new lx2v_weight();
     w->fmt = LX2V_W_FP8; w->rows = rows; w->cols = cols; w->group = group;
     const size_t G = cols / group;
-    // One flag byte per (row, 32-column block): the block holds a code the
-    // fast decode does not cover, or a scale outside its range.
+    // One flag byte per (row, 32-column block): 1 = the block holds a code
+    // the fast decode does not cover (fixed up exactly), 2 = a scale outside
+    // the fast range (reference formula).
     const size_t ku = (size_t)fp8_flag_cols((int)cols);
     std::vector<uint8_t> flags(rows * ku, 0);
     for (size_t r = 0; r < rows; ++r) {
         for (size_t c = 0; c < cols; ++c) {
-            const bool bad = fp8_code_special(q[r * cols + c]) || !fp8_scale_fast(scales[r * G + c / group]);
-            if (bad) flags[r * ku + c / 32] = 1;
+            uint8_t &f = flags[(c / 32) * rows + r];
+            if (!fp8_scale_fast(scales[r * G + c / group])) f = 2;
+            else if (fp8_code_special(q[r * cols + c]) && f == 0) f = 1;
         }
     }
     auto st = transpose_scales(scales, rows, G);
     if ((s = upload_codes_scales(ctx, w, q, rows * cols, &st, nullptr))) { weight_release(w); return s; }
-    cudaError_t e = cudaMalloc(&w->flags, flags.size());
+    cudaError_t e = cudaMalloc(&w->flags, flags.size() < 16 ? 16 : flags.size());
     if (e == cudaSuccess) e = cudaMemcpy(w->flags, flags.data(), flags.size(), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         weight_release(w);
@@ -605,9 +607,13 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     OpScope ps(ctx, opname);
 
     const void *gate_ptr = mods ? (const char *)mods->ptr + gate * N * esize(mods->dtype) : nullptr;
-    const bool tc_ok = x->dtype == LX2V_BF16 && K % 16 == 0 &&
-                       unit_path_ok(w->fmt, (int)K, (int)w->group) &&
-                       (N * esize(y->dtype)) % 16 == 0 && rows >= 16;
+    // Tensor-core kernel: 16-byte aligned rows for every TMA map and store,
+    // and at most 4 quantization groups per 64-wide k-block.
+    const size_t grp = w->group;
+    const bool groups_ok = w->fmt == LX2V_W_BF16 || grp % 64 == 0 ||
+                           (w->fmt == LX2V_W_Q4 && grp >= 16 && 64 % grp == 0);
+    const bool tc_ok = x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 && groups_ok &&
+                       unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16;
     int path = ctx->path;
     if (path == 0) path = tc_ok ? 1 : 3;
     if (path == 1 && !tc_ok)
@@ -633,14 +639,23 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
             s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, 64, 128,
                          CU_TENSOR_MAP_SWIZZLE_64B);
         if (s) return s;
-        s = make_map(ctx, &p.tmap_y, y->ptr,
-                     y->dtype == LX2V_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                     esize(y->dtype), N, y_row + rows, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (s) return s;
+        if (w->fmt != LX2V_W_BF16) {
+            const int sgrp = grp % 64 == 0 ? 1 : (int)(64 / grp);
+            p.sgrp = sgrp;
+            s = make_map(ctx, &p.tmap_s, w->fmt == LX2V_W_Q4 ? (void *)w->sz_t : (void *)w->scales_t,
+                         CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, N, K / grp, 128, (uint32_t)sgrp,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (s) return s;
+        }
+        if (w->fmt == LX2V_W_FP8) {
+            s = make_map(ctx, &p.tmap_f, w->flags, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N,
+                         (size_t)fp8_flag_cols((int)K), 128, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (s) return s;
+        }
+        p.y = y->ptr;
         p.codes = (const uint8_t *)w->codes;
         p.scales_t = w->scales_t;
         p.sz_t = w->sz_t;
-        p.flags = w->flags;
         p.bias = bias ? bias->ptr : nullptr;
         p.bias_f32 = bias && bias->dtype == LX2V_F32;
         p.gate = gate_ptr;
