@@ -163,8 +163,9 @@ LX2V_API lx2v_status lx2v_profile_json(lx2v_ctx *ctx, char *buf, size_t cap, siz
 LX2V_API lx2v_status lx2v_profile_reset(lx2v_ctx *ctx);
 
 /* ---- knobs for tests and benchmarks -------------------------------------- */
-/* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05),
- * 2 = small-M GEMV, 3 = generic CUDA-core kernel. A forced choice that cannot
+/* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05, one
+ * CTA per tile), 2 = small-M GEMV, 3 = generic CUDA-core kernel, 4 = tensor-
+ * core GEMM on CTA pairs (tcgen05 cta_group::2). A forced choice that cannot
  * run the shape returns LX2V_ERR_UNSUPPORTED. */
 LX2V_API lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path);
 /* Token tile of the tensor-core kernel: 0 = automatic, else 128, 192 or 256

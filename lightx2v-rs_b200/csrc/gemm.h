@@ -27,11 +27,15 @@ struct alignas(64) GemmParams {
     int reduce;               // 1: reduce-add into y (gated residual)
     int bias_f32, gate_f32;   // element types of bias / gate
     int sgrp;                 // scale groups per k-block box (1, 2 or 4)
+    int gshift;               // log2(group) when group < 64, else 6
 };
 
 // Tensor-core (tcgen05) dequant GEMM. `bt` = token tile (128, 192 or 256).
 cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
 int gemm_dq_token_tile(int M, int N, int num_sms);
+// The same GEMM on CTA pairs (cta_group::2): pair tile = 256 features x bt
+// tokens; tmap_x's box must be {64, bt/2}.
+cudaError_t gemm_pair_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
 
 // Small-M path and the generic CUDA-core path (kernels.cu); they take plain
 // pointers instead of tensor maps.

@@ -1,0 +1,201 @@
+// gemm_common.cuh — pieces shared by the single-CTA and the CTA-pair
+// tensor-core linear kernels: stage layout of the weight codes, the per-item
+// decode (smem codes -> bf16 pairs for tcgen05.st), the GELU epilogue math and
+// the epilogue tile writer (TMEM -> registers -> smem staging -> coalesced
+// global stores or vector reductions).
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include "dequant.cuh"
+#include "gemm.h"
+#include "ptx.cuh"
+
+namespace lx2v {
+
+constexpr int BK = 64;          // k columns per pipeline stage
+constexpr int STG_ROWS = 16;    // tokens per epilogue staging chunk
+constexpr int STG_COLS = 128;   // features per staging chunk (one CTA's rows)
+constexpr int STG_BYTES = STG_ROWS * STG_COLS * 4;
+constexpr int EPI_THREADS = 128;
+constexpr int TMEM_COLS = 512;
+
+// Bytes of one stage's code tile (128 weight rows x 64 k) and of its side
+// data: scales (Q8/FP8 f32, Q4 (scale, zero) words) for up to SGRP groups,
+// and the FP8 block flags of the two 32-column halves.
+template <int FMT>
+struct WTile {
+    static constexpr int ROW_BYTES = FMT == FMT_Q4 ? 32 : FMT == FMT_BF16 ? 128 : 64;
+    static constexpr int BYTES = 128 * ROW_BYTES;
+    static constexpr int SGRP = FMT == FMT_Q4 ? 4 : FMT == FMT_BF16 ? 0 : 1;
+    static constexpr int S_BYTES = 128 * 4 * SGRP;
+    static constexpr int F_BYTES = FMT == FMT_FP8 ? 2 * 128 : 0;
+};
+
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// GELU-tanh (crates/lightx2v-cpu/src/lib.rs:151-153) on a pair:
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float2 gelu2(float2 x) {
+    const float2 c1 = make_float2(0.044715f, 0.044715f);
+    const float2 one = make_float2(1.0f, 1.0f);
+    const float2 k0 = make_float2(0.7978845608028654f, 0.7978845608028654f);
+    const float2 half = make_float2(0.5f, 0.5f);
+    const float2 x2 = __fmul2_rn(x, x);
+    const float2 inner = __fmul2_rn(__fmul2_rn(x, k0), __ffma2_rn(x2, c1, one));
+    const float2 t = make_float2(tanh_approx(inner.x), tanh_approx(inner.y));
+    const float2 hx = __fmul2_rn(x, half);
+    return __ffma2_rn(hx, t, hx);
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) {
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+// A ring position (stage, phase), advanced per item without divisions.
+struct Ring {
+    int s = 0, ph = 0;
+    template <int N>
+    __device__ __forceinline__ void next() {
+        if (++s == N) { s = 0; ph ^= 1; }
+    }
+};
+
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) {
+    return *reinterpret_cast<const uint2 *>(p);
+}
+
+// Decode UNITS consecutive 16-value units of weight row `r` of one stage,
+// starting at unit `u0` (columns 16*u0 ..) of k-block `kb`, from the stage's
+// code tile `wstage`, scale words `sstage` and FP8 flags `fstage` in shared
+// memory. Output: 8 bf16x2 words per unit, columns (2i, 2i+1) -> word i.
+// Scale-group index of a unit inside the stage's scale box: the box starts
+// at the k-block's first group; groups are >= 16 columns and either divide
+// 64 (p.gshift = log2(group)) or are multiples of 64 (p.gshift = 6).
+template <int FMT, int UNITS>
+__device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t *wstage, const uint8_t *sstage,
+                                             const uint8_t *fstage, int r, int u0, uint32_t (&packed)[8 * UNITS]) {
+    const uint8_t *wt = wstage + r * WTile<FMT>::ROW_BYTES;
+#pragma unroll
+    for (int u = 0; u < UNITS; ++u) {
+        const int ui = u0 + u;
+        uint32_t *out = packed + 8 * u;
+        uint32_t o[8];
+        if (FMT == FMT_BF16) {
+            // 128-byte rows, 128B swizzle: 16-byte chunk ^= row & 7; a unit is 2 chunks
+            const uint4 a = lds128(wt + (((2 * ui) ^ (r & 7)) << 4));
+            const uint4 b = lds128(wt + (((2 * ui + 1) ^ (r & 7)) << 4));
+            o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+            o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+        } else {
+            const uint32_t *sw = reinterpret_cast<const uint32_t *>(sstage);
+            const int gi = (ui * 16) >> p.gshift;
+            if (FMT == FMT_Q4) {
+                // 32-byte rows, 32B swizzle: chunk ^= (row >> 2) & 1; a unit is half a chunk
+                const uint2 raw = lds64(wt + (((ui >> 1) ^ ((r >> 2) & 1)) << 4) + (ui & 1) * 8);
+                float s, z;
+                q4_scale_zero(sw[gi * 128 + r], s, z);
+                unit_to_bf16<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), make_uint4(0, 0, 0, 0), s, z, 0, o);
+            } else {
+                // 64-byte rows, 64B swizzle: chunk ^= (row >> 1) & 3; a unit is one chunk
+                const uint4 raw = lds128(wt + ((ui ^ ((r >> 1) & 3)) << 4));
+                const float s = __uint_as_float(sw[r]);
+                const int mode = FMT == FMT_FP8 ? fstage[(ui >> 1) * 128 + r] : 0;
+                unit_to_bf16<FMT>(raw, raw, s, 0.0f, mode, o);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = o[i];
+    }
+}
+
+// Epilogue of one accumulator tile held in this CTA's TMEM: 128 features
+// (lanes; this thread = feature f_base + 32*q + lane) x `ntok` tokens
+// (columns from `acc_addr`, tokens m0 .. m0 + ntok). Bias, GELU and gate are
+// applied in f32; rows go through a [16 tokens][128 features] smem staging
+// tile to 16-byte coalesced global stores, or to vector reductions into h
+// for the gated residual. `release` runs once the last TMEM load of the tile
+// has completed (the accumulator can be reused from then on).
+template <typename Release>
+__device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_addr, int ntok, int f_base,
+                                              int m0, int q, int lane, uint8_t *stg_base, int &chunk_ctr,
+                                              Release release) {
+    const int et = q * 32 + lane;  // 0..127
+    const bool out_f32 = p.out_f32 != 0;
+    const int esz = out_f32 ? 4 : 2;
+    const int row_bytes = STG_COLS * esz;
+    const int cpr = row_bytes / 16;  // 16-byte chunks per staged row
+    const int f = f_base + et;
+    float bias_f = 0.0f, gate_f = 1.0f;
+    if (f < p.N) {
+        if (p.bias) bias_f = p.bias_f32 ? reinterpret_cast<const float *>(p.bias)[f]
+                                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.bias)[f]);
+        if (p.gate) gate_f = p.gate_f32 ? reinterpret_cast<const float *>(p.gate)[f]
+                                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.gate)[f]);
+    }
+    const float2 bias2 = make_float2(bias_f, bias_f), gate2 = make_float2(gate_f, gate_f);
+    const int nld = min(ntok / 32, (p.M - m0 + 31) / 32);
+    for (int c = 0; c < nld; ++c) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(acc_addr + (uint32_t)(c * 32), acc);
+        tmem_wait_ld();
+        if (c == nld - 1) release();
+        float2 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float2 t = __fadd2_rn(make_float2(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1])), bias2);
+            if (p.act == 1) t = gelu2(t);
+            v[i] = p.gate ? __fmul2_rn(t, gate2) : t;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row0 = m0 + c * 32 + h * STG_ROWS;
+            if (row0 >= p.M) break;
+            uint8_t *stg = stg_base + (chunk_ctr & 1) * STG_BYTES;
+            ++chunk_ctr;
+            if (out_f32) {
+                float *s32 = reinterpret_cast<float *>(stg) + et;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    s32[(2 * i) * STG_COLS] = v[h * 8 + i].x;
+                    s32[(2 * i + 1) * STG_COLS] = v[h * 8 + i].y;
+                }
+            } else {
+                unsigned short *s16 = reinterpret_cast<unsigned short *>(stg) + et;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t pk = pack_bf16x2(v[h * 8 + i]);
+                    s16[(2 * i) * STG_COLS] = (unsigned short)(pk & 0xFFFFu);
+                    s16[(2 * i + 1) * STG_COLS] = (unsigned short)(pk >> 16);
+                }
+            }
+            named_bar_sync(1, EPI_THREADS);
+            const int vals = 16 / esz;  // elements per 16-byte chunk
+            for (int id = et; id < STG_ROWS * cpr; id += EPI_THREADS) {
+                const int row = id / cpr, cc = id - row * cpr;
+                const int token = row0 + row;
+                const int f0 = f_base + cc * vals;
+                if (token >= p.M || f0 >= p.N) continue;
+                const uint4 u = *reinterpret_cast<const uint4 *>(stg + row * row_bytes + cc * 16);
+                char *dst = reinterpret_cast<char *>(p.y) + (((int64_t)p.y_row + token) * p.N + f0) * esz;
+                if (!p.reduce) {
+                    *reinterpret_cast<uint4 *>(dst) = u;
+                } else if (out_f32) {
+                    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                                 "f"(__uint_as_float(u.x)), "f"(__uint_as_float(u.y)),
+                                 "f"(__uint_as_float(u.z)), "f"(__uint_as_float(u.w))
+                                 : "memory");
+                } else {
+                    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                                 "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
+                                 : "memory");
+                }
+            }
+        }
+    }
+}
+
+}  // namespace lx2v

@@ -1,0 +1,312 @@
+// gemm_pair_sm100.cu — the quantized linear on a CTA pair (cta_group::2).
+//
+// Same computation as gemm_sm100.cu (Backend::linear and the fused gated
+// residual, crates/lightx2v-core/src/backend.rs:199-212, 244-253), with the
+// tile spread over a cluster of two CTAs on two SMs:
+//   pair tile = 256 output features x BT tokens;
+//   CTA r decodes weight rows [128 r, 128 r + 128) of the tile into its own
+//   TMEM (A operand, 128 lanes per CTA) and TMA-loads tokens
+//   [BT/2 r, BT/2 r + BT/2) of x into its own shared memory (B operand);
+//   the leader CTA (rank 0) issues tcgen05.mma.cta_group::2 with M = 256,
+//   N = BT, which reads A from both TMEMs and B from both shared memories and
+//   leaves D = 128 features x BT tokens in each CTA's TMEM.
+// Each SM thus loads half of the x tile per k-block: 24 KB of x + codes per
+// 4.2 MFLOP instead of 40 KB, which is what lets the ring hold 8 stages and
+// keep the tensor pipe fed from L2.
+//
+// Synchronisation (all waits bounded, ptx.cuh):
+//   xb_full[s]  leader; both CTAs' x halves complete_tx on it (TMA
+//               .cta_group::2, no multicast)
+//   w_full[s]   each CTA; its own code / scale / flag tiles
+//   x_empty[s]  each CTA; multicast tcgen05.commit from the leader's MMA
+//   a_full[a]   leader; 32 arrivals (16 dequant warps x 2 CTAs, remote for
+//               the peer)
+//   a_empty[a], acc_full[b]  each CTA; multicast commits
+//   acc_empty[b] leader; 8 arrivals (4 epilogue warps x 2 CTAs)
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include "gemm_common.cuh"
+
+namespace lx2v {
+
+
+template <int FMT, int BT, int ACC, int SS, int AS>
+struct PairCfg {
+    static constexpr int A_COL0 = ACC * BT;
+    static_assert(A_COL0 + AS * (BK / 2) <= TMEM_COLS, "TMEM budget");
+    static_assert(BT % 64 == 0 && BT <= 256, "pair token tile");
+    static constexpr int XH_BYTES = (BT / 2) * BK * 2;  // this CTA's half of the x tile
+    static constexpr int W_BYTES = WTile<FMT>::BYTES;
+    static constexpr int S_BYTES = WTile<FMT>::S_BYTES;
+    static constexpr int F_BYTES = WTile<FMT>::F_BYTES;
+    static constexpr int OFF_W = SS * XH_BYTES;
+    static constexpr int OFF_S = OFF_W + SS * W_BYTES;
+    static constexpr int OFF_F = OFF_S + SS * S_BYTES;
+    static constexpr int OFF_STG = (OFF_F + SS * F_BYTES + 127) & ~127;
+    static constexpr int OFF_BAR = OFF_STG + 2 * STG_BYTES;
+    static constexpr int NUM_BARS = 3 * SS + 2 * AS + 2 * ACC + 1;
+    static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
+    static_assert(XH_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "swizzle atoms");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct PairCtl {
+    uint32_t tmem_base;
+    int epi_ok;
+};
+
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
+__global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+    using C = PairCfg<FMT, BT, ACC, SS, AS>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
+    uint64_t *xb_full = bars;               // [SS]  leader: both x halves
+    uint64_t *w_full = xb_full + SS;        // [SS]  own codes + side data
+    uint64_t *x_empty = w_full + SS;        // [SS]  multicast commit
+    uint64_t *a_full = x_empty + SS;        // [AS]  leader: dequant warps of both CTAs
+    uint64_t *a_empty = a_full + AS;        // [AS]  multicast commit
+    uint64_t *acc_full = a_empty + AS;      // [ACC] multicast commit
+    uint64_t *acc_empty = acc_full + ACC;   // [ACC] leader: 8 epilogue warps
+    uint64_t *drain = acc_empty + ACC;      // [1]   leader: final MMA drain
+    PairCtl *ctl = reinterpret_cast<PairCtl *>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool lead = rank == 0;
+    const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+    const int n_mt = (p.M + BT - 1) / BT;
+    const int n_ft = (p.N + 255) / 256;
+    const int n_tiles = n_mt * n_ft;
+    const int KB = (p.K + BK - 1) / BK;
+    const int my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+    int *err = p.err;
+    const uint64_t lim = p.wait_limit_ns;
+    const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SS; ++s) {
+            mbar_init(&xb_full[s], 1);
+            mbar_init(&w_full[s], 1);
+            mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < AS; ++s) {
+            mbar_init(&a_full[s], 8 * DQW);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int b = 0; b < ACC; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&p.tmap_x);
+        tma_prefetch_desc(&p.tmap_w);
+        if (FMT != FMT_BF16) tma_prefetch_desc(&p.tmap_s);
+        if (FMT == FMT_FP8) tma_prefetch_desc(&p.tmap_f);
+    }
+    if (warp == 1) tmem_alloc_pair(&ctl->tmem_base, TMEM_COLS);
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            int last_phase[SS];
+            for (int s = 0; s < SS; ++s) last_phase[s] = -1;
+            const int wk_div = FMT == FMT_Q4 ? 2 : 1;
+            const uint32_t w_tx = C::W_BYTES + (FMT != FMT_BF16 ? 128 * 4 * p.sgrp : 0) + C::F_BYTES;
+            Ring xs;
+            bool ok = true;
+            for (int j = 0; j < my_tiles && ok; ++j) {
+                const int tile = pair + j * npairs;
+                const int mt = tile % n_mt, ft = tile / n_mt;
+                const int row0 = ft * 256 + (int)rank * 128;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_cluster_bounded(&x_empty[xs.s], xs.ph ^ 1, err, lim)) { ok = false; break; }
+                    if (lead) mbar_arrive_expect_tx(&xb_full[xs.s], 2 * C::XH_BYTES);
+                    mbar_arrive_expect_tx(&w_full[xs.s], w_tx);
+                    tma_load_2d_pair(smem + xs.s * C::XH_BYTES, &p.tmap_x, mapa_shared(smem_u32(&xb_full[xs.s]), 0),
+                                     kb * BK, p.x_row + mt * BT + (int)rank * (BT / 2));
+                    tma_load_2d(smem + C::OFF_W + xs.s * C::W_BYTES, &p.tmap_w, &w_full[xs.s], kb * BK / wk_div, row0);
+                    if (FMT != FMT_BF16)
+                        tma_load_2d(smem + C::OFF_S + xs.s * C::S_BYTES, &p.tmap_s, &w_full[xs.s], row0,
+                                    (kb * BK) / p.group);
+                    if (FMT == FMT_FP8)
+                        tma_load_2d(smem + C::OFF_F + xs.s * C::F_BYTES, &p.tmap_f, &w_full[xs.s], row0, kb * 2);
+                    last_phase[xs.s] = xs.ph;
+                    xs.next<SS>();
+                }
+            }
+            // Drain: a stage's loads have landed once its own codes arrived and
+            // the leader's MMA released it (x halves are counted on the leader).
+            for (int s = 0; s < SS; ++s)
+                if (last_phase[s] >= 0) {
+                    mbar_wait_bounded(&w_full[s], (uint32_t)last_phase[s], nullptr, drain_lim);
+                    mbar_wait_cluster_bounded(&x_empty[s], (uint32_t)last_phase[s], nullptr, drain_lim);
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader CTA) ----------------
+        if (lane == 0 && lead) {
+            const uint32_t idesc = idesc_bf16_f32(256, BT);
+            bool ok = true;
+            Ring xs, as, ab;
+            for (int j = 0; j < my_tiles && ok; ++j) {
+                if (!mbar_wait_cluster_bounded(&acc_empty[ab.s], ab.ph ^ 1, err, lim)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim) ||
+                        !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
+                    const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                    mma_commit_pair(&x_empty[xs.s], 0x3);
+                    mma_commit_pair(&a_empty[as.s], 0x3);
+                    xs.next<SS>();
+                    as.next<AS>();
+                }
+                if (!ok) break;
+                mma_commit_pair(&acc_full[ab.s], 0x3);
+                ab.next<ACC>();
+            }
+            mma_commit_pair(drain, 0x1);
+            mbar_wait_bounded(drain, 0, nullptr, drain_lim);
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- epilogue (both CTAs) ----------------
+        const int q = warp - 4;
+        const bool leader_thread = threadIdx.x == 128;
+        int chunk_ctr = 0;
+        Ring ab;
+        for (int j = 0; j < my_tiles; ++j) {
+            const int tile = pair + j * npairs;
+            const int mt = tile % n_mt, ft = tile / n_mt;
+            if (leader_thread) ctl->epi_ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+            named_bar_sync(1, EPI_THREADS);
+            if (!ctl->epi_ok) break;
+            tc_fence_after();
+            const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
+            const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
+            epilogue_tile(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
+                          chunk_ctr, [&] {
+                              tc_fence_before();
+                              __syncwarp();
+                              if (lane == 0) mbar_arrive_cluster(rel);
+                          });
+            ab.next<ACC>();
+        }
+    } else if (warp >= 8) {
+        // ---------------- dequant (both CTAs) ----------------
+        constexpr int U = 4 / DQW;
+        const int q = warp & 3;
+        const int u0 = ((warp - 8) >> 2) * U;
+        const int r = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        Ring xs, as;
+        bool ok = true;
+        for (int j = 0; j < my_tiles && ok; ++j) {
+            for (int kb = 0; kb < KB; ++kb) {
+                int w = 1;
+                if (lane == 0) w = mbar_wait_bounded(&w_full[xs.s], xs.ph, err, lim) ? 1 : 0;
+                w = __shfl_sync(0xFFFFFFFFu, w, 0);
+                if (!w) { ok = false; break; }
+                uint32_t packed[8 * U];
+                decode_units<FMT, U>(p, smem + C::OFF_W + xs.s * C::W_BYTES, smem + C::OFF_S + xs.s * C::S_BYTES,
+                                     smem + C::OFF_F + xs.s * C::F_BYTES, r, u0, packed);
+                if (lane == 0) w = mbar_wait_cluster_bounded(&a_empty[as.s], as.ph ^ 1, err, lim) ? 1 : 0;
+                w = __shfl_sync(0xFFFFFFFFu, w, 0);
+                if (!w) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ta = tmem + lane_addr + (uint32_t)(C::A_COL0 + as.s * (BK / 2) + u0 * 8);
+#pragma unroll
+                for (int u = 0; u < U; ++u) tmem_st_32x32b_x8(ta + u * 8, packed + 8 * u);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[as.s]), 0));
+                xs.next<SS>();
+                as.next<AS>();
+            }
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // the leader's MMAs and both epilogues are done with both TMEMs
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
+}
+
+// ---- host launcher --------------------------------------------------------
+constexpr int pair_stages(int fmt, int bt) {
+    const int budget = 227 * 1024 - 1024 - 2 * STG_BYTES - 512;
+    const int w = 128 * (fmt == FMT_Q4 ? 32 : fmt == FMT_BF16 ? 128 : 64);
+    const int side = fmt == FMT_Q4 ? 128 * 16 : fmt == FMT_BF16 ? 0 : 512 + (fmt == FMT_FP8 ? 256 : 0);
+    const int stage = (bt / 2) * BK * 2 + w + side;
+    return budget / stage > 10 ? 10 : budget / stage;
+}
+
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW = 4>
+static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
+    using C = PairCfg<FMT, BT, ACC, SS, AS>;
+    auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW>;
+    constexpr int PAIR_THREADS = 32 * (8 + 4 * DQW);
+    static int max_pairs = 0;
+    const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(PAIR_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_pairs == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3(2 * (num_sms / 2));
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        max_pairs = clusters > 0 ? clusters : 1;
+    }
+    const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
+    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    cfg.gridDim = dim3(2 * pairs);
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int FMT>
+static cudaError_t pair_launch_fmt(int bt, const GemmParams &p, int num_sms, cudaStream_t st) {
+    switch (bt) {
+        case 128: return pair_launch_t<FMT, 128, 2, pair_stages(FMT, 128), 8>(p, num_sms, st);
+        case 192: return pair_launch_t<FMT, 192, 2, pair_stages(FMT, 192), 4>(p, num_sms, st);
+        case 256: return pair_launch_t<FMT, 256, 1, pair_stages(FMT, 256), 8>(p, num_sms, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t gemm_pair_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st) {
+    switch (fmt) {
+        case FMT_Q8: return pair_launch_fmt<FMT_Q8>(bt, p, num_sms, st);
+        case FMT_Q4: return pair_launch_fmt<FMT_Q4>(bt, p, num_sms, st);
+        case FMT_FP8: return pair_launch_fmt<FMT_FP8>(bt, p, num_sms, st);
+        default: return pair_launch_fmt<FMT_BF16>(bt, p, num_sms, st);
+    }
+}
+
+}  // namespace lx2v

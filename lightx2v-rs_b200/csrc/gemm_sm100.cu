@@ -20,13 +20,13 @@
 // code tile of the 128 weight rows (64-, 32- or 128-byte swizzle so that the
 // dequant threads' row reads are bank-conflict free).
 //
-// Warp roles (16 warps, one persistent CTA per SM):
+// Warp roles (24 warps, one persistent CTA per SM):
 //   warp 0      TMA producer (x tile + code tile per stage)
 //   warp 1      TMEM allocator and MMA issuer (one thread)
 //   warps 4-7   epilogue: TMEM -> registers -> bias/GELU/gate -> smem staging
 //               -> TMA store (or TMA reduce-add for the gated residual)
-//   warps 8-15  dequant: two warpgroups, each owns 32 of the 64 columns of a
-//               k-block; thread = one weight row (TMEM lane)
+//   warps 8+    dequant: four warpgroups, each owns 16 of the 64 columns of
+//               a k-block; thread = one weight row (TMEM lane)
 // ACC accumulators (1 or 2) let the epilogue of tile j overlap the mainloop
 // of tile j+1. Every mbarrier wait is bounded (ptx.cuh); on expiry the kernel
 // records an error word, drains its own in-flight copies and MMAs, frees
@@ -35,30 +35,10 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstring>
-#include "dequant.cuh"
-#include "gemm.h"
-#include "ptx.cuh"
+#include "gemm_common.cuh"
 
 namespace lx2v {
 
-constexpr int BK = 64;
-constexpr int NUM_THREADS = 512;
-constexpr int EPI_THREADS = 128;
-constexpr int STG_ROWS = 16;    // tokens per epilogue staging chunk (half a 32-column TMEM load)
-constexpr int STG_COLS = 128;   // features per staging chunk
-constexpr int TMEM_COLS = 512;
-
-// Bytes of one stage's code tile (128 weight rows x 64 k) and of its side
-// data: scales (Q8/FP8 f32, Q4 (scale, zero) words) for up to SGRP groups,
-// and the FP8 block flags of the two 32-column halves.
-template <int FMT>
-struct WTile {
-    static constexpr int ROW_BYTES = FMT == FMT_Q4 ? 32 : FMT == FMT_BF16 ? 128 : 64;
-    static constexpr int BYTES = 128 * ROW_BYTES;
-    static constexpr int SGRP = FMT == FMT_Q4 ? 4 : FMT == FMT_BF16 ? 0 : 1;
-    static constexpr int S_BYTES = 128 * 4 * SGRP;
-    static constexpr int F_BYTES = FMT == FMT_FP8 ? 2 * 128 : 0;
-};
 
 // SS = shared-memory stages (x tile + code tile), AS = TMEM stages of the
 // decoded A operand, ACC = accumulators of BT columns each.
@@ -70,7 +50,6 @@ struct Cfg {
     static constexpr int W_STAGE_BYTES = WTile<FMT>::BYTES;
     static constexpr int S_STAGE_BYTES = WTile<FMT>::S_BYTES;
     static constexpr int F_STAGE_BYTES = WTile<FMT>::F_BYTES;
-    static constexpr int STG_BYTES = STG_ROWS * STG_COLS * 4;
     static constexpr int OFF_W = SS * X_STAGE_BYTES;
     static constexpr int OFF_S = OFF_W + SS * W_STAGE_BYTES;
     static constexpr int OFF_F = OFF_S + SS * S_STAGE_BYTES;
@@ -87,48 +66,17 @@ struct SmemCtl {
     int epi_ok;
 };
 
-__device__ __forceinline__ float tanh_approx(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// GELU-tanh (crates/lightx2v-cpu/src/lib.rs:151-153) on a pair:
-// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
-__device__ __forceinline__ float2 gelu2(float2 x) {
-    const float2 c1 = make_float2(0.044715f, 0.044715f);
-    const float2 one = make_float2(1.0f, 1.0f);
-    const float2 k0 = make_float2(0.7978845608028654f, 0.7978845608028654f);
-    const float2 half = make_float2(0.5f, 0.5f);
-    const float2 x2 = __fmul2_rn(x, x);
-    const float2 inner = __fmul2_rn(__fmul2_rn(x, k0), __ffma2_rn(x2, c1, one));
-    const float2 t = make_float2(tanh_approx(inner.x), tanh_approx(inner.y));
-    const float2 hx = __fmul2_rn(x, half);
-    return __ffma2_rn(hx, t, hx);
-}
-
-__device__ __forceinline__ uint4 lds128(const uint8_t *p) {
-    return *reinterpret_cast<const uint4 *>(p);
-}
-
-// A ring position (stage, phase) advanced per item without divisions.
-struct Ring {
-    int s = 0, ph = 0;
-    template <int N>
-    __device__ __forceinline__ void next() {
-        if (++s == N) { s = 0; ph ^= 1; }
-    }
-};
-
-// Dequant warps: thread = one weight row (TMEM lane) of the 128-row tile;
-// warpgroup `half` owns columns [32*half, 32*half + 32) of each k-block.
-template <int FMT, int BT, int ACC, int SS, int AS>
+// Dequant warps: DQW warpgroups; thread = one weight row (TMEM lane) of the
+// 128-row tile; warpgroup wg owns units [wg*U, wg*U + U) (16 columns each,
+// U = 4/DQW) of every 64-wide k-block.
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
 __device__ __forceinline__ void dequant_role(const GemmParams &p, uint8_t *smem, uint32_t tmem,
                                              uint64_t *x_full, uint64_t *a_full, uint64_t *a_empty,
                                              int warp, int lane, int KB, int my_tiles) {
     using C = Cfg<FMT, BT, ACC, SS, AS>;
+    constexpr int U = 4 / DQW;
     const int q = warp & 3;
-    const int half = (warp - 8) >> 2;
+    const int u0 = ((warp - 8) >> 2) * U;
     const int r = q * 32 + lane;  // row within the 128-row tile
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     Ring xs, as;
@@ -138,62 +86,17 @@ __device__ __forceinline__ void dequant_role(const GemmParams &p, uint8_t *smem,
             if (lane == 0) ok = mbar_wait_bounded(&x_full[xs.s], xs.ph, p.err, p.wait_limit_ns) ? 1 : 0;
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             if (!ok) return;
-
-            const uint8_t *wt = smem + C::OFF_W + xs.s * C::W_STAGE_BYTES + r * WTile<FMT>::ROW_BYTES;
-            // Side data of this row from the stage: scale word(s) of the
-            // groups of the two 16-column units, and the FP8 block flag.
-            float s0 = 0.0f, s1 = 0.0f, z0 = 0.0f, z1 = 0.0f;
-            int mode = 0;
-            if (FMT != FMT_BF16) {
-                const uint32_t *sw = reinterpret_cast<const uint32_t *>(smem + C::OFF_S + xs.s * C::S_STAGE_BYTES);
-                const int kbase = kb * BK + half * 32;
-                const int gbase = (kb * BK) / p.group;
-                const int gi0 = kbase / p.group - gbase, gi1 = (kbase + 16) / p.group - gbase;
-                const int i0 = gi0 < WTile<FMT>::SGRP ? gi0 : 0, i1 = gi1 < WTile<FMT>::SGRP ? gi1 : 0;
-                if (FMT == FMT_Q4) {
-                    q4_scale_zero(sw[i0 * 128 + r], s0, z0);
-                    q4_scale_zero(sw[i1 * 128 + r], s1, z1);
-                } else {
-                    s0 = __uint_as_float(sw[i0 * 128 + r]);
-                    s1 = __uint_as_float(sw[i1 * 128 + r]);
-                }
-                if (FMT == FMT_FP8) mode = (smem + C::OFF_F + xs.s * C::F_STAGE_BYTES)[half * 128 + r];
-            }
-            uint32_t packed[16];
-            if (FMT == FMT_Q4) {
-                // 32-byte rows, 32B swizzle: chunk ^= (row >> 2) & 1
-                const uint4 raw = lds128(wt + ((half ^ ((r >> 2) & 1)) << 4));
-                uint32_t o0[8], o1[8];
-                unit_to_bf16<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), raw, s0, z0, 0, o0);
-                unit_to_bf16<FMT_Q4>(make_uint4(raw.z, raw.w, 0, 0), raw, s1, z1, 0, o1);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) { packed[i] = o0[i]; packed[8 + i] = o1[i]; }
-            } else if (FMT == FMT_BF16) {
-                // 128-byte rows, 128B swizzle: chunk ^= row & 7
-                const int c0 = half * 4;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 v = lds128(wt + (((c0 + i) ^ (r & 7)) << 4));
-                    packed[4 * i] = v.x; packed[4 * i + 1] = v.y;
-                    packed[4 * i + 2] = v.z; packed[4 * i + 3] = v.w;
-                }
-            } else {
-                // 64-byte rows, 64B swizzle: chunk ^= (row >> 1) & 3
-                const int sw = (r >> 1) & 3;
-                const uint4 a = lds128(wt + (((half * 2) ^ sw) << 4));
-                const uint4 b = lds128(wt + (((half * 2 + 1) ^ sw) << 4));
-                uint32_t o0[8], o1[8];
-                unit_to_bf16<FMT>(a, a, s0, 0.0f, mode, o0);
-                unit_to_bf16<FMT>(b, b, s1, 0.0f, mode, o1);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) { packed[i] = o0[i]; packed[8 + i] = o1[i]; }
-            }
+            uint32_t packed[8 * U];
+            decode_units<FMT, U>(p, smem + C::OFF_W + xs.s * C::W_STAGE_BYTES, smem + C::OFF_S + xs.s * C::S_STAGE_BYTES,
+                                 smem + C::OFF_F + xs.s * C::F_STAGE_BYTES, r, u0, packed);
             // The decoded values are in registers; now wait for the TMEM stage.
             if (lane == 0) ok = mbar_wait_bounded(&a_empty[as.s], as.ph ^ 1, p.err, p.wait_limit_ns) ? 1 : 0;
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             if (!ok) return;
             tc_fence_after();
-            tmem_st_32x32b_x16(tmem + lane_addr + (uint32_t)(C::A_COL0 + as.s * (BK / 2) + half * 16), packed);
+            const uint32_t ta = tmem + lane_addr + (uint32_t)(C::A_COL0 + as.s * (BK / 2) + u0 * 8);
+#pragma unroll
+            for (int u = 0; u < U; ++u) tmem_st_32x32b_x8(ta + u * 8, packed + 8 * u);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -204,8 +107,8 @@ __device__ __forceinline__ void dequant_role(const GemmParams &p, uint8_t *smem,
     }
 }
 
-template <int FMT, int BT, int ACC, int SS, int AS>
-__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_dq_kernel(const __grid_constant__ GemmParams p) {
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
+__global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_dq_kernel(const __grid_constant__ GemmParams p) {
     using C = Cfg<FMT, BT, ACC, SS, AS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -238,7 +141,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_dq_kernel(const __grid_co
             mbar_init(&x_empty[s], 1);
         }
         for (int s = 0; s < AS; ++s) {
-            mbar_init(&a_full[s], 8);
+            mbar_init(&a_full[s], 4 * DQW);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < ACC; ++b) {
@@ -329,19 +232,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_dq_kernel(const __grid_co
         __syncwarp();
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue ----------------
-        // TMEM (thread = feature, 32 tokens) -> bias/GELU/gate -> smem staging
-        // [32 tokens][128 features] -> 16-byte coalesced global stores, or
-        // vector reductions (red.global.add) for the gated residual. Plain
-        // stores keep the epilogue off the TMA queue, where the pipeline's
-        // loads are waiting.
         const int q = warp - 4;
-        const int et = threadIdx.x - 128;  // 0..127
-        const bool leader = et == 0;
+        const bool leader = threadIdx.x == 128;
         int chunk_ctr = 0;
-        const bool out_f32 = p.out_f32 != 0;
-        const int esz = out_f32 ? 4 : 2;
-        const int row_bytes = STG_COLS * esz;
-        const int cpr = row_bytes / 16;  // 16-byte chunks per staged row
         Ring ab;
         for (int j = 0; j < my_tiles; ++j) {
             const int tile = (int)blockIdx.x + j * (int)gridDim.x;
@@ -350,84 +243,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_dq_kernel(const __grid_co
             named_bar_sync(1, EPI_THREADS);
             if (!ctl->epi_ok) break;
             tc_fence_after();
-            const int f = ft * 128 + q * 32 + lane;
-            float bias_f = 0.0f, gate_f = 1.0f;
-            if (f < p.N) {
-                if (p.bias) bias_f = p.bias_f32 ? reinterpret_cast<const float *>(p.bias)[f]
-                                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.bias)[f]);
-                if (p.gate) gate_f = p.gate_f32 ? reinterpret_cast<const float *>(p.gate)[f]
-                                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.gate)[f]);
-            }
-            const float2 bias2 = make_float2(bias_f, bias_f), gate2 = make_float2(gate_f, gate_f);
-            const int m0 = mt * BT;
-            const int nld = min(BT / 32, (p.M - m0 + 31) / 32);
             const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
-            for (int c = 0; c < nld; ++c) {
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(acc_addr + (uint32_t)(c * 32), acc);
-                tmem_wait_ld();
-                if (c == nld - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[ab.s]);
-                }
-                float2 v[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float2 t = __fadd2_rn(make_float2(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1])), bias2);
-                    if (p.act == 1) t = gelu2(t);
-                    v[i] = p.gate ? __fmul2_rn(t, gate2) : t;
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row0 = m0 + c * 32 + h * STG_ROWS;
-                    if (row0 >= p.M) break;
-                    uint8_t *stg = smem + C::OFF_STG + (chunk_ctr & 1) * C::STG_BYTES;
-                    ++chunk_ctr;
-                    if (out_f32) {
-                        float *s32 = reinterpret_cast<float *>(stg) + q * 32 + lane;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            s32[(2 * i) * STG_COLS] = v[h * 8 + i].x;
-                            s32[(2 * i + 1) * STG_COLS] = v[h * 8 + i].y;
-                        }
-                    } else {
-                        unsigned short *s16 = reinterpret_cast<unsigned short *>(stg) + q * 32 + lane;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const uint32_t pk = pack_bf16x2(v[h * 8 + i]);
-                            s16[(2 * i) * STG_COLS] = (unsigned short)(pk & 0xFFFFu);
-                            s16[(2 * i + 1) * STG_COLS] = (unsigned short)(pk >> 16);
-                        }
-                    }
-                    named_bar_sync(1, EPI_THREADS);
-                    const int vals = 16 / esz;  // elements per 16-byte chunk
-                    for (int id = et; id < STG_ROWS * cpr; id += EPI_THREADS) {
-                        const int row = id / cpr, cc = id - row * cpr;
-                        const int token = row0 + row;
-                        const int f0 = ft * 128 + cc * vals;
-                        if (token >= p.M || f0 >= p.N) continue;
-                        const uint4 u = *reinterpret_cast<const uint4 *>(stg + row * row_bytes + cc * 16);
-                        char *dst = reinterpret_cast<char *>(p.y) + (((int64_t)p.y_row + token) * p.N + f0) * esz;
-                        if (!p.reduce) {
-                            *reinterpret_cast<uint4 *>(dst) = u;
-                        } else if (out_f32) {
-                            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-                                         "f"(__uint_as_float(u.x)), "f"(__uint_as_float(u.y)),
-                                         "f"(__uint_as_float(u.z)), "f"(__uint_as_float(u.w))
-                                         : "memory");
-                        } else {
-                            asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-                                         "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
-                                         : "memory");
-                        }
-                    }
-                }
-            }
+            uint64_t *rel_bar = &acc_empty[ab.s];
+            epilogue_tile(p, acc_addr, BT, ft * 128, mt * BT, q, lane, smem + C::OFF_STG, chunk_ctr, [&] {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(rel_bar);
+            });
             ab.next<ACC>();
         }
     } else if (warp >= 8) {
-        dequant_role<FMT, BT, ACC, SS, AS>(p, smem, tmem, x_full, a_full, a_empty, warp, lane, KB, my_tiles);
+        dequant_role<FMT, BT, ACC, SS, AS, DQW>(p, smem, tmem, x_full, a_full, a_empty, warp, lane, KB, my_tiles);
     }
 
     tc_fence_before();
@@ -437,22 +263,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_dq_kernel(const __grid_co
 }
 
 // ---- host launcher --------------------------------------------------------
-template <int FMT, int BT, int ACC, int SS, int AS>
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW = 4>
 static cudaError_t launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = Cfg<FMT, BT, ACC, SS, AS>;
+    constexpr int NUM_THREADS = 32 * (8 + 4 * DQW);
     static bool attr_set = false;
     // Keep the footprint large enough that only one CTA fits per SM: each
     // CTA allocates all 512 TMEM columns.
     const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_dq_kernel<FMT, BT, ACC, SS, AS>,
+        cudaError_t e = cudaFuncSetAttribute(gemm_dq_kernel<FMT, BT, ACC, SS, AS, DQW>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 127) / 128);
     const int grid = n_tiles < num_sms ? n_tiles : num_sms;
-    gemm_dq_kernel<FMT, BT, ACC, SS, AS><<<grid, NUM_THREADS, smem, st>>>(p);
+    gemm_dq_kernel<FMT, BT, ACC, SS, AS, DQW><<<grid, NUM_THREADS, smem, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -611,21 +611,22 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     // and at most 4 quantization groups per 64-wide k-block.
     const size_t grp = w->group;
     const bool groups_ok = w->fmt == LX2V_W_BF16 || grp % 64 == 0 ||
-                           (w->fmt == LX2V_W_Q4 && grp >= 16 && 64 % grp == 0);
+                           (w->fmt == LX2V_W_Q4 && (grp == 16 || grp == 32));
     const bool tc_ok = x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 && groups_ok &&
                        unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16;
     int path = ctx->path;
-    if (path == 0) path = tc_ok ? 1 : 3;
-    if (path == 1 && !tc_ok)
+    if (path == 0) path = tc_ok ? (rows >= 512 && N >= 256 ? 4 : 1) : 3;
+    if ((path == 1 || path == 4) && !tc_ok)
         return fail(ctx, LX2V_ERR_UNSUPPORTED, "the tensor-core kernel does not take this shape/dtype");
     if (path == 2) return fail(ctx, LX2V_ERR_UNSUPPORTED, "the small-M kernel is not built in this version");
 
-    if (path == 1) {
+    if (path == 1 || path == 4) {
+        const bool pair = path == 4;
         GemmParams p;
         memset(&p, 0, sizeof p);
         const int bt = ctx->token_tile ? ctx->token_tile : gemm_dq_token_tile((int)rows, (int)N, ctx->num_sms);
         lx2v_status s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
-                                 (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B);
+                                 (uint32_t)(pair ? bt / 2 : bt), CU_TENSOR_MAP_SWIZZLE_128B);
         if (s) return s;
         // Code tile of one stage: 128 weight rows x one 64-wide k-block, with
         // the swizzle that makes the dequant threads' row reads conflict free.
@@ -642,6 +643,7 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         if (w->fmt != LX2V_W_BF16) {
             const int sgrp = grp % 64 == 0 ? 1 : (int)(64 / grp);
             p.sgrp = sgrp;
+            p.gshift = grp % 64 == 0 ? 6 : (grp == 16 ? 4 : 5);
             s = make_map(ctx, &p.tmap_s, w->fmt == LX2V_W_Q4 ? (void *)w->sz_t : (void *)w->scales_t,
                          CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, N, K / grp, 128, (uint32_t)sgrp,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -667,7 +669,8 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         p.act = act;
         p.out_f32 = y->dtype == LX2V_F32;
         p.reduce = mods ? 1 : 0;
-        CUDA_TRY(ctx, gemm_dq_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
+        if (pair) CUDA_TRY(ctx, gemm_pair_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
+        else CUDA_TRY(ctx, gemm_dq_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
         ctx->launches++;
         return LX2V_OK;
     }
@@ -749,7 +752,7 @@ extern "C" lx2v_status lx2v_profile_reset(lx2v_ctx *ctx) {
 
 extern "C" lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path) {
     if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
-    if (path < 0 || path > 3) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
+    if (path < 0 || path > 4) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
     ctx->path = path;
     return LX2V_OK;
 }

@@ -310,3 +310,52 @@ def test_expired_wait_is_reported_and_context_survives(be, oracle):
     rows = sampled_rows(M, 8)
     want = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, x_row=int(r), threads=8)[0] for r in rows])
     assert rel_l2(y[rows], want) <= REL_L2
+
+
+# ---- the CTA-pair (cta_group::2) tensor-core kernel ---------------------------------------
+@pytest.mark.parametrize("fmt", ["fp8", "q8", "q4", "native"])
+@pytest.mark.parametrize("M,N,K,bt", [(512, 256, 128, 256), (700, 640, 448, 192), (1000, 384, 1024, 128),
+                                      (257, 1536, 256, 256)])
+def test_pair_kernel_matches_oracle_and_single_cta(be, oracle, fmt, M, N, K, bt):
+    w, q = make_weight(fmt, N, K, seed=51 + M, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    x = oracle.normal(52, M * K)
+    b = oracle.normal(53, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b)
+    outs = {}
+    try:
+        be.set_token_tile(bt)
+        for path in (4, 1):
+            be.set_linear_path(path)
+            yb = be.alloc(M * N, F32)
+            be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
+            outs[path] = be.download(yb).reshape(M, N)
+    finally:
+        be.set_linear_path(0)
+        be.set_token_tile(0)
+    want = oracle.linear(x, M, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=1, threads=8)
+    assert rel_l2(outs[4], want) <= REL_L2
+    # same bf16 operands, different summation order
+    assert rel_l2(outs[4], outs[1]) <= 1e-5
+
+
+def test_pair_kernel_gated_residual_and_offsets(be, oracle):
+    M, N, K = 900, 768, 512
+    w, q = make_weight("fp8", N, K, seed=61, oracle=oracle)
+    dw = be.weight_fp8(q)
+    x = oracle.normal(62, (M + 40) * K)
+    h0 = oracle.normal(63, (M + 7) * N)
+    mods = oracle.normal(64, 6 * N, 0.5)
+    xb, mb = be.upload(x), be.upload(mods, F32)
+    hb = be.upload(h0, F32)
+    try:
+        be.set_linear_path(4)
+        be.linear_gate_residual(xb, 40, M, dw, None, Act.NONE, hb, 7, mb, 5)
+    finally:
+        be.set_linear_path(0)
+    got = be.download(hb).reshape(M + 7, N)
+    lin = oracle.linear(x, M, q.dequantize(), N, K, x_row=40, threads=8)
+    want = h0.reshape(M + 7, N).copy()
+    want[7:] = oracle.gate_residual(h0.reshape(M + 7, N)[7:], lin, M, N, mods, 5)
+    assert np.array_equal(got[:7], h0.reshape(M + 7, N)[:7])
+    assert rel_l2(got[7:] - h0.reshape(M + 7, N)[7:], want[7:] - h0.reshape(M + 7, N)[7:]) <= REL_L2
