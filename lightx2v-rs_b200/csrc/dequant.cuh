@@ -126,11 +126,12 @@ __device__ __forceinline__ uint32_t fp8_sign_pair_bf16(const uint4 raw, int i) {
     const uint32_t w = (i < 2) ? raw.x : (i < 4) ? raw.y : (i < 6) ? raw.z : raw.w;
     return __byte_perm(w, 0u, (i & 1) ? 0x3424u : 0x1404u) & 0x80008000u;
 }
-// Fix-up of fast-path magnitudes for a block that holds special codes (its
-// scale is in the fast range): an exponent-field-0 code m decodes to
-// m/8 * 2^-9 (quant.rs:413-414) but the fast formula gives m * 2^-9, so the
-// product is scaled by 2^-3 (exact: the fast product is at least 2^-109);
-// the NaN codes 0x7F / 0xFF become NaN.
+// Fix-up of fast-path products (fp8_magnitudes or fp8_products_hw) for a
+// block that holds special codes (its scale is in the fast range): an
+// exponent-field-0 code m decodes to m/8 * 2^-9 (quant.rs:413-414) but both
+// fast decoders give m * 2^-9, so the product is scaled by 2^-3 (exact: the
+// fast product is at least 2^-109 in magnitude or zero); the NaN codes
+// 0x7F / 0xFF become NaN.
 __device__ __forceinline__ void fp8_fixup(const uint4 raw, float2 (&p)[8]) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
     const float qnan = __uint_as_float(0x7FC00000u);
@@ -141,6 +142,32 @@ __device__ __forceinline__ void fp8_fixup(const uint4 raw, float2 (&p)[8]) {
         v = ((c & 0x78u) == 0) ? v * 0.125f : v;
         v = ((c & 0x7Fu) == 0x7Fu) ? qnan : v;
         if (i & 1) p[i >> 1].y = v; else p[i >> 1].x = v;
+    }
+}
+
+// Signed products with the hardware e4m3 converter: cvt.rn.f16x2.e4m3x2
+// gives the exact IEEE-style e4m3 value as f16 (f16 holds every e4m3 value,
+// subnormals included), the f16 -> f32 widening is exact, and one f32
+// multiply rounds decode(c) * s exactly as the reference does
+// (quant.rs:400-420). IEEE-style decoding differs from the reference only on
+// exponent-field-0 codes (2^3 larger) and on 0x7F / 0xFF, which fp8_fixup
+// corrects in blocks the upload flagged; it needs no restriction on s.
+__device__ __forceinline__ void fp8_products_hw(const uint4 raw, float s, float2 (&p)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t h0, h1;
+        asm("{\n\t.reg .b16 lo, hi;\n\t"
+            "mov.b32 {lo, hi}, %2;\n\t"
+            "cvt.rn.f16x2.e4m3x2 %0, lo;\n\t"
+            "cvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+            : "=r"(h0), "=r"(h1)
+            : "r"(w[j]));
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1));
+        p[2 * j] = __fmul2_rn(f0, s2);
+        p[2 * j + 1] = __fmul2_rn(f1, s2);
     }
 }
 
@@ -198,13 +225,11 @@ __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, 
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
     } else {
         if (fp8_mode != 2) {
-            fp8_magnitudes(raw, s, p);
+            fp8_products_hw(raw, s, p);
             if (fp8_mode == 1) fp8_fixup(raw, p);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]) ^ fp8_sign_pair_bf16(raw, i);
-            return;
+        } else {
+            fp8_products_slow(raw, s, p);
         }
-        fp8_products_slow(raw, s, p);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]);

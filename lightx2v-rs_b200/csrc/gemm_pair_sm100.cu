@@ -18,10 +18,13 @@
 //   xb_full[s]  leader; both CTAs' x halves complete_tx on it (TMA
 //               .cta_group::2, no multicast)
 //   w_full[s]   each CTA; its own code / scale / flag tiles
-//   x_empty[s]  each CTA; multicast tcgen05.commit from the leader's MMA
-//   a_full[a]   leader; 32 arrivals (16 dequant warps x 2 CTAs, remote for
-//               the peer)
-//   a_empty[a], acc_full[b]  each CTA; multicast commits
+//   x_empty[s]  each CTA; multicast tcgen05.commit from the leader once the
+//               MMAs of the stage's k-block completed. It frees the smem
+//               stage for the producer and, AS k-blocks later, the TMEM A
+//               stage for the dequant warps (one commit per k-block).
+//   a_full[a]   leader; 8 arrivals (the 4 warps of the dequant warpgroup that
+//               owns the k-block, in both CTAs; remote for the peer)
+//   acc_full[b] each CTA; multicast commit
 //   acc_empty[b] leader; 8 arrivals (4 epilogue warps x 2 CTAs)
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -46,7 +49,7 @@ struct PairCfg {
     static constexpr int OFF_F = OFF_S + SS * S_BYTES;
     static constexpr int OFF_STG = (OFF_F + SS * F_BYTES + 127) & ~127;
     static constexpr int OFF_BAR = OFF_STG + 2 * STG_BYTES;
-    static constexpr int NUM_BARS = 3 * SS + 2 * AS + 2 * ACC + 1;
+    static constexpr int NUM_BARS = 3 * SS + AS + 2 * ACC + 1;
     static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
     static_assert(XH_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "swizzle atoms");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -60,15 +63,15 @@ struct PairCtl {
 template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
 __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
+    static_assert(SS >= AS, "an A stage is released through the x ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
     uint64_t *xb_full = bars;               // [SS]  leader: both x halves
     uint64_t *w_full = xb_full + SS;        // [SS]  own codes + side data
-    uint64_t *x_empty = w_full + SS;        // [SS]  multicast commit
+    uint64_t *x_empty = w_full + SS;        // [SS]  multicast commit: MMA of the stage done
     uint64_t *a_full = x_empty + SS;        // [AS]  leader: dequant warps of both CTAs
-    uint64_t *a_empty = a_full + AS;        // [AS]  multicast commit
-    uint64_t *acc_full = a_empty + AS;      // [ACC] multicast commit
+    uint64_t *acc_full = a_full + AS;       // [ACC] multicast commit
     uint64_t *acc_empty = acc_full + ACC;   // [ACC] leader: 8 epilogue warps
     uint64_t *drain = acc_empty + ACC;      // [1]   leader: final MMA drain
     PairCtl *ctl = reinterpret_cast<PairCtl *>(drain + 1);
@@ -82,6 +85,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     const int n_tiles = n_mt * n_ft;
     const int KB = (p.K + BK - 1) / BK;
     const int my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+    const int total_kb = my_tiles * KB;  // k-blocks this pair runs, over all its tiles
     int *err = p.err;
     const uint64_t lim = p.wait_limit_ns;
     const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
@@ -92,10 +96,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             mbar_init(&w_full[s], 1);
             mbar_init(&x_empty[s], 1);
         }
-        for (int s = 0; s < AS; ++s) {
-            mbar_init(&a_full[s], 8 * DQW);
-            mbar_init(&a_empty[s], 1);
-        }
+        for (int s = 0; s < AS; ++s) mbar_init(&a_full[s], 8);
         for (int b = 0; b < ACC; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 8);
@@ -126,12 +127,13 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 const int tile = pair + j * npairs;
                 const int mt = tile % n_mt, ft = tile / n_mt;
                 const int row0 = ft * 256 + (int)rank * 128;
+                const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait_cluster_bounded(&x_empty[xs.s], xs.ph ^ 1, err, lim)) { ok = false; break; }
                     if (lead) mbar_arrive_expect_tx(&xb_full[xs.s], 2 * C::XH_BYTES);
                     mbar_arrive_expect_tx(&w_full[xs.s], w_tx);
                     tma_load_2d_pair(smem + xs.s * C::XH_BYTES, &p.tmap_x, mapa_shared(smem_u32(&xb_full[xs.s]), 0),
-                                     kb * BK, p.x_row + mt * BT + (int)rank * (BT / 2));
+                                     kb * BK, xrow);
                     tma_load_2d(smem + C::OFF_W + xs.s * C::W_BYTES, &p.tmap_w, &w_full[xs.s], kb * BK / wk_div, row0);
                     if (FMT != FMT_BF16)
                         tma_load_2d(smem + C::OFF_S + xs.s * C::S_BYTES, &p.tmap_s, &w_full[xs.s], row0,
@@ -153,17 +155,29 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA) ----------------
+        // The readiness of stage i + 1 is tested (without blocking) before the
+        // MMAs of stage i are issued, so the barrier round trip overlaps the
+        // tensor pipe's work instead of idling it between k-blocks.
         if (lane == 0 && lead) {
             const uint32_t idesc = idesc_bf16_f32(256, BT);
             bool ok = true;
             Ring xs, as, ab;
+            bool x_ready = total_kb > 0 && mbar_wait_cluster_bounded(&xb_full[0], 0, err, lim);
+            bool a_ready = x_ready && mbar_wait_cluster_bounded(&a_full[0], 0, err, lim);
+            ok = total_kb == 0 || (x_ready && a_ready);
+            int i = 0;
             for (int j = 0; j < my_tiles && ok; ++j) {
                 if (!mbar_wait_cluster_bounded(&acc_empty[ab.s], ab.ph ^ 1, err, lim)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
-                for (int kb = 0; kb < KB; ++kb) {
-                    if (!mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim) ||
-                        !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim)) { ok = false; break; }
+                for (int kb = 0; kb < KB; ++kb, ++i) {
+                    // stage i is ready; look ahead at stage i + 1
+                    Ring xn = xs, an = as;
+                    xn.next<SS>();
+                    an.next<AS>();
+                    const bool more = i + 1 < total_kb;
+                    bool xr = more ? mbar_test_wait(&xb_full[xn.s], xn.ph) : true;
+                    bool ar = more ? mbar_test_wait(&a_full[an.s], an.ph) : true;
                     tc_fence_after();
                     const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
@@ -171,12 +185,13 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                     for (int kk = 0; kk < BK / 16; ++kk)
                         mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
                     mma_commit_pair(&x_empty[xs.s], 0x3);
-                    mma_commit_pair(&a_empty[as.s], 0x3);
-                    xs.next<SS>();
-                    as.next<AS>();
+                    if (kb == KB - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
+                    xs = xn;
+                    as = an;
+                    if (!xr) xr = mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim);
+                    if (xr && !ar) ar = mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim);
+                    if (!xr || !ar) { ok = false; break; }
                 }
-                if (!ok) break;
-                mma_commit_pair(&acc_full[ab.s], 0x3);
                 ab.next<ACC>();
             }
             mma_commit_pair(drain, 0x1);
@@ -208,36 +223,44 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         }
     } else if (warp >= 8) {
         // ---------------- dequant (both CTAs) ----------------
-        constexpr int U = 4 / DQW;
+        // Warpgroup g takes whole k-blocks i = g, g + DQW, ... of the pair's
+        // sequence; thread r decodes weight row r (64 values) and writes them
+        // to A stage i % AS of its CTA's TMEM. The A stage is free once the
+        // MMA of k-block i - AS has completed, which the x ring's empty
+        // barrier of that k-block records.
+        const int g = (warp - 8) >> 2;
         const int q = warp & 3;
-        const int u0 = ((warp - 8) >> 2) * U;
         const int r = q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-        Ring xs, as;
-        bool ok = true;
-        for (int j = 0; j < my_tiles && ok; ++j) {
-            for (int kb = 0; kb < KB; ++kb) {
-                int w = 1;
-                if (lane == 0) w = mbar_wait_bounded(&w_full[xs.s], xs.ph, err, lim) ? 1 : 0;
-                w = __shfl_sync(0xFFFFFFFFu, w, 0);
-                if (!w) { ok = false; break; }
-                uint32_t packed[8 * U];
-                decode_units<FMT, U>(p, smem + C::OFF_W + xs.s * C::W_BYTES, smem + C::OFF_S + xs.s * C::S_BYTES,
-                                     smem + C::OFF_F + xs.s * C::F_BYTES, r, u0, packed);
-                if (lane == 0) w = mbar_wait_cluster_bounded(&a_empty[as.s], as.ph ^ 1, err, lim) ? 1 : 0;
-                w = __shfl_sync(0xFFFFFFFFu, w, 0);
-                if (!w) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t ta = tmem + lane_addr + (uint32_t)(C::A_COL0 + as.s * (BK / 2) + u0 * 8);
-#pragma unroll
-                for (int u = 0; u < U; ++u) tmem_st_32x32b_x8(ta + u * 8, packed + 8 * u);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[as.s]), 0));
-                xs.next<SS>();
-                as.next<AS>();
+        for (int i = g; i < total_kb; i += DQW) {
+            const int s = i % SS;
+            const uint32_t ph = (uint32_t)(i / SS) & 1u;
+            const int a = i % AS;
+            int w = 1;
+            if (lane == 0) {
+                w = mbar_wait_bounded(&w_full[s], ph, err, lim) ? 1 : 0;
+                if (w && i >= AS) {
+                    const int e = i - AS;
+                    w = mbar_wait_cluster_bounded(&x_empty[e % SS], (uint32_t)(e / SS) & 1u, err, lim) ? 1 : 0;
+                }
             }
+            w = __shfl_sync(0xFFFFFFFFu, w, 0);
+            if (!w) break;
+            tc_fence_after();
+            const uint32_t ta = tmem + lane_addr + (uint32_t)(C::A_COL0 + a * (BK / 2));
+            const uint8_t *wst = smem + C::OFF_W + s * C::W_BYTES;
+            const uint8_t *sst = smem + C::OFF_S + s * C::S_BYTES;
+            const uint8_t *fst = smem + C::OFF_F + s * C::F_BYTES;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t packed[16];
+                decode_units<FMT, 2>(p, wst, sst, fst, r, 2 * h, packed);
+                tmem_st_32x32b_x16(ta + (uint32_t)(h * 16), packed);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[a]), 0));
         }
     }
 
@@ -248,6 +271,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
 }
 
 // ---- host launcher --------------------------------------------------------
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
+
 constexpr int pair_stages(int fmt, int bt) {
     const int budget = 227 * 1024 - 1024 - 2 * STG_BYTES - 512;
     const int w = 128 * (fmt == FMT_Q4 ? 32 : fmt == FMT_BF16 ? 128 : 64);
@@ -293,9 +318,9 @@ static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t 
 template <int FMT>
 static cudaError_t pair_launch_fmt(int bt, const GemmParams &p, int num_sms, cudaStream_t st) {
     switch (bt) {
-        case 128: return pair_launch_t<FMT, 128, 2, pair_stages(FMT, 128), 8>(p, num_sms, st);
-        case 192: return pair_launch_t<FMT, 192, 2, pair_stages(FMT, 192), 4>(p, num_sms, st);
-        case 256: return pair_launch_t<FMT, 256, 1, pair_stages(FMT, 256), 8>(p, num_sms, st);
+        case 128: return pair_launch_t<FMT, 128, 2, pair_stages(FMT, 128), cmin(8, pair_stages(FMT, 128))>(p, num_sms, st);
+        case 192: return pair_launch_t<FMT, 192, 2, pair_stages(FMT, 192), cmin(4, pair_stages(FMT, 192))>(p, num_sms, st);
+        case 256: return pair_launch_t<FMT, 256, 1, pair_stages(FMT, 256), cmin(8, pair_stages(FMT, 256))>(p, num_sms, st);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -55,6 +55,33 @@ __device__ __forceinline__ void raise_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// Non-blocking test of a phase (never suspends the thread); used to look
+// ahead at the next stage while the current one is being issued.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// try_wait with an explicit suspend-time hint: the thread sleeps until the
+// phase completes or the hint expires, instead of polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the phase of `bar` with the given parity, for at most `limit_ns`
 // nanoseconds. Returns false (and records ERR_WAIT_TIMEOUT) when the limit
 // expires or when another role of the kernel has already recorded an error.
@@ -62,14 +89,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
                                                   uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t spin = 1;; ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 63) == 0) {
-            if (err && *(volatile int *)err != 0) return false;
-            if (globaltimer_ns() - t0 > limit_ns) {
-                raise_error(err, ERR_WAIT_TIMEOUT);
-                return false;
-            }
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (err && *(volatile int *)err != 0) return false;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            raise_error(err, ERR_WAIT_TIMEOUT);
+            return false;
         }
     }
 }

@@ -359,3 +359,62 @@ def test_pair_kernel_gated_residual_and_offsets(be, oracle):
     want[7:] = oracle.gate_residual(h0.reshape(M + 7, N)[7:], lin, M, N, mods, 5)
     assert np.array_equal(got[:7], h0.reshape(M + 7, N)[:7])
     assert rel_l2(got[7:] - h0.reshape(M + 7, N)[7:], want[7:] - h0.reshape(M + 7, N)[7:]) <= REL_L2
+
+
+# ---- GEMM operand decode: bit-exact through a one-hot activation --------------------------
+def bf16_round(v):
+    """f32 -> bf16 round-to-nearest-even, returned as f32 (NaN kept NaN)."""
+    b = np.asarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    out = r.astype(np.uint32).view(np.float32).copy()
+    out[np.isnan(v)] = np.nan
+    return out
+
+
+def fp8_all_codes_weight(N, K, seed):
+    """Codes cover all 256 bytes; rows >= N - 16 keep the NaN codes, the
+    others have them replaced; scales mix the fast range with values far
+    outside it (which take the reference-formula path)."""
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0, 256, N * K, dtype=np.uint8).reshape(N, K)
+    codes[: N - 16][(codes[: N - 16] & 0x7F) == 0x7F] ^= 0x01
+    codes[: N - 16, :64] = np.arange(256, dtype=np.uint8).reshape(4, 64).repeat((N - 16) // 4 + 1, 0)[: N - 16] & 0xFE
+    groups = N * K // 128
+    scales = rng.choice(np.array([0.01, 3e-4, 1.5, 300.0, 1e-33, 2.0 ** -101, 2.0 ** 7], np.float32), groups)
+    return quant.Fp8E4M3(codes.reshape(-1).copy(), scales.astype(np.float32), N, K, 128)
+
+
+@pytest.mark.parametrize("fmt", ["fp8_all", "fp8", "q8", "q4", "native"])
+@pytest.mark.parametrize("path", [1, 4, 3])
+def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
+    # x = identity (K tokens, one-hot): y[m][n] = operand(w[n][m]) exactly,
+    # since every other product is 0 * w. Rows holding a NaN code are NaN.
+    N, K = 512, 256
+    if fmt == "fp8_all":
+        q = fp8_all_codes_weight(N, K, 7)
+        dw = be.weight_fp8(q)
+        deq = oracle.fp8_dequantize(q.q, q.scales, q.group).reshape(N, K)
+    else:
+        w, q = make_weight(fmt, N, K, seed=71, group=64, oracle=oracle)
+        dw = upload_weight(be, fmt, q, w, N, K)
+        deq = oracle_dequant(oracle, fmt, q, w).reshape(N, K)
+    x = np.eye(K, dtype=np.float32).reshape(-1)
+    xb = be.upload(x)
+    yb = be.alloc(K * N, F32)
+    try:
+        be.set_linear_path(path)
+        be.linear(xb, 0, K, dw, None, Act.NONE, yb, 0)
+        got = be.download(yb).reshape(K, N)
+    finally:
+        be.set_linear_path(0)
+    want = bf16_round(deq.reshape(-1)).reshape(N, K).T.copy()
+    nan_rows = np.isnan(deq).any(axis=1)
+    want[:, nan_rows] = np.nan
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    # values below the f32 normal range may be flushed inside the tensor
+    # core; everything else must match to the bit
+    tiny = ~np.isnan(want) & (np.abs(np.nan_to_num(want)) < 2.0 ** -126)
+    fin = ~np.isnan(want) & ~tiny
+    bad = np.flatnonzero(got[fin] != want[fin])
+    assert bad.size == 0, (fmt, path, bad.size, got[fin][bad[:4]], want[fin][bad[:4]])
+    assert np.all(np.abs(got[tiny]) <= 2.0 ** -126)
