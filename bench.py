@@ -361,7 +361,7 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": f"bf16 dense burst, {peak_src}",
                          "traffic": profile_traffic(),
-                         "kernel": "gemm_dq_kernel<FP8> (tcgen05, A=weights from TMEM)",
+                         "kernel": "gemm_pair_kernel<FP8> (tcgen05.mma cta_group::2, dequantised weights in TMEM)",
                          "per_linear": per_kernel},
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
