@@ -32,7 +32,7 @@ struct alignas(64) GemmParams {
 
 // Tensor-core (tcgen05) dequant GEMM. `bt` = token tile (128, 192 or 256).
 cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
-int gemm_dq_token_tile(int M, int N, int num_sms);
+int gemm_dq_token_tile(int M, int N, int K, int units, int feat_tile);
 // The same GEMM on CTA pairs (cta_group::2): pair tile = 256 features x bt
 // tokens; tmap_x's box must be {64, bt/2}.
 cudaError_t gemm_pair_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);

@@ -64,6 +64,7 @@ template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
 __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
     static_assert(SS >= AS, "an A stage is released through the x ring");
+    static_assert(SS % DQW == 0, "each smem slot is read by one dequant warpgroup");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
@@ -278,7 +279,11 @@ constexpr int pair_stages(int fmt, int bt) {
     const int w = 128 * (fmt == FMT_Q4 ? 32 : fmt == FMT_BF16 ? 128 : 64);
     const int side = fmt == FMT_Q4 ? 128 * 16 : fmt == FMT_BF16 ? 0 : 512 + (fmt == FMT_FP8 ? 256 : 0);
     const int stage = (bt / 2) * BK * 2 + w + side;
-    return budget / stage > 10 ? 10 : budget / stage;
+    // A multiple of the four dequant warpgroups: each ring slot is then read
+    // by one warpgroup only, which has waited out the slot's previous phase
+    // itself (a parity wait must never run a whole phase ahead).
+    const int n = budget / stage > 8 ? 8 : budget / stage;
+    return n - n % 4;
 }
 
 template <int FMT, int BT, int ACC, int SS, int AS, int DQW = 4>

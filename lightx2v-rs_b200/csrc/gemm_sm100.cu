@@ -313,15 +313,32 @@ cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cu
     }
 }
 
-int gemm_dq_token_tile(int M, int N, int num_sms) {
-    // Measured on B200 (FP8 linears of the Wan2.1-1.3B chunk, M = 4680): the
-    // widest token tile is fastest once there are enough tokens to fill it;
-    // each decoded weight then feeds the most MMA columns.
-    (void)N;
-    (void)num_sms;
-    if (M >= 1024) return 256;
-    if (M >= 384) return 192;
-    return 128;
+int gemm_dq_token_tile(int M, int N, int K, int units, int feat_tile) {
+    // Wave model of the persistent grid: `units` CTAs (or CTA pairs) each run
+    // whole tiles of feat_tile features x bt tokens, so a launch takes
+    // ceil(tiles / units) rounds of bt * K MMA columns. The 256-token tile
+    // has a single TMEM accumulator, so its epilogue is not hidden behind the
+    // next tile's k-loop; measured on B200 that costs about as much as 192
+    // more k-columns per tile. A 128-token tile moves more bytes per FLOP and
+    // pays the per-k-block handoffs on fewer columns: measured ~1.65x the
+    // time per column of the wider tiles. The cheapest tile wins; ties go to
+    // the wider tile. (FP8 set of the Wan2.1-1.3B chunk, M = 4680: QKV,
+    // FFN1 -> 192; out -> 256 (tie); FFN2 -> 256.)
+    const int cand[3] = {256, 192, 128};
+    int best = 128;
+    double best_cost = 0.0;
+    for (int c = 0; c < 3; ++c) {
+        const int bt = cand[c];
+        if (c > 0 && M < bt / 2) continue;
+        const long long tiles = (long long)((M + bt - 1) / bt) * ((N + feat_tile - 1) / feat_tile);
+        const long long waves = (tiles + units - 1) / units;
+        const double cost = (double)waves * bt * (K + (bt == 256 ? 192 : 0)) * (bt == 128 ? 1.65 : 1.0);
+        if (c == 0 || cost < best_cost) {
+            best = bt;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 
 }  // namespace lx2v

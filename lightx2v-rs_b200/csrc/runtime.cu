@@ -624,7 +624,9 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         const bool pair = path == 4;
         GemmParams p;
         memset(&p, 0, sizeof p);
-        const int bt = ctx->token_tile ? ctx->token_tile : gemm_dq_token_tile((int)rows, (int)N, ctx->num_sms);
+        const int bt = ctx->token_tile ? ctx->token_tile
+                                       : gemm_dq_token_tile((int)rows, (int)N, (int)K, pair ? ctx->num_sms / 2 : ctx->num_sms,
+                                                            pair ? 256 : 128);
         lx2v_status s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
                                  (uint32_t)(pair ? bt / 2 : bt), CU_TENSOR_MAP_SWIZZLE_128B);
         if (s) return s;

@@ -418,3 +418,4 @@ def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
     bad = np.flatnonzero(got[fin] != want[fin])
     assert bad.size == 0, (fmt, path, bad.size, got[fin][bad[:4]], want[fin][bad[:4]])
     assert np.all(np.abs(got[tiny]) <= 2.0 ** -126)
+
