@@ -112,17 +112,27 @@ __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t 
     }
 }
 
+// Partial-tile traffic of a stream-K epilogue (see GemmParams::streamk).
+struct PartialIO {
+    float *write = nullptr;        // non-null: store the raw accumulator here, nothing else
+    const float *add = nullptr;    // non-null: add n_add partial tiles from here before the epilogue
+    int n_add = 0;
+    int64_t add_stride = 0;        // floats between consecutive partial tiles
+};
+
 // Epilogue of one accumulator tile held in this CTA's TMEM: 128 features
 // (lanes; this thread = feature f_base + 32*q + lane) x `ntok` tokens
 // (columns from `acc_addr`, tokens m0 .. m0 + ntok). Bias, GELU and gate are
 // applied in f32; rows go through a [16 tokens][128 features] smem staging
 // tile to 16-byte coalesced global stores, or to vector reductions into h
 // for the gated residual. `release` runs once the last TMEM load of the tile
-// has completed (the accumulator can be reused from then on).
-template <typename Release>
+// has completed (the accumulator can be reused from then on). Partial tiles
+// (`io`) are stored token-major, [token][128 features] f32, so a warp's
+// accesses for one token are 128 contiguous bytes.
+template <bool PARTIAL = false, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_addr, int ntok, int f_base,
                                               int m0, int q, int lane, uint8_t *stg_base, int &chunk_ctr,
-                                              Release release) {
+                                              Release release, const PartialIO &io = PartialIO()) {
     const int et = q * 32 + lane;  // 0..127
     const bool out_f32 = p.out_f32 != 0;
     const int esz = out_f32 ? 4 : 2;
@@ -143,6 +153,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
         tmem_ld_32x32b_x32(acc_addr + (uint32_t)(c * 32), acc);
         tmem_wait_ld();
         if (c == nld - 1) release();
+        if (PARTIAL) {
+            if (io.write) {
+                float *dst = io.write + (int64_t)(c * 32) * 128 + et;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) __stcg(dst + i * 128, __uint_as_float(acc[i]));
+                continue;
+            }
+            for (int part = 0; part < io.n_add; ++part) {
+                const float *src = io.add + part * io.add_stride + (int64_t)(c * 32) * 128 + et;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    acc[i] = __float_as_uint(__uint_as_float(acc[i]) + __ldcg(src + i * 128));
+            }
+        }
         float2 v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -194,6 +218,31 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
                                  : "memory");
                 }
             }
+        }
+    }
+}
+
+// Flag publication between CTAs of one launch (stream-K partial tiles).
+__device__ __forceinline__ void flag_publish(int *flag, int value) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
+}
+__device__ __forceinline__ int flag_read(const int *flag) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+}
+// Wait until *flag == value, for at most limit_ns; false (and the error word
+// set) when the limit expires or another role already failed.
+__device__ __forceinline__ bool flag_wait_bounded(const int *flag, int value, int *err, uint64_t limit_ns) {
+    if (flag_read(flag) == value) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(64);
+        if (flag_read(flag) == value) return true;
+        if (err && *(volatile int *)err != 0) return false;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            raise_error(err, ERR_WAIT_TIMEOUT);
+            return false;
         }
     }
 }

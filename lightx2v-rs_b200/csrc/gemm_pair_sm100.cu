@@ -60,7 +60,36 @@ struct PairCtl {
     int epi_ok;
 };
 
-template <int FMT, int BT, int ACC, int SS, int AS, int DQW>
+// The work of one CTA pair as a list of segments: k-blocks [kb0, kb1) of a
+// tile. Whole tiles: tiles pair, pair + npairs, ... Stream-K: the
+// n_tiles * KB k-blocks split into npairs equal contiguous ranges; a range
+// may start and end inside a tile.
+struct PairWork {
+    long long lo = 0, hi = 0;  // stream-K k-block range
+    int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
+    bool sk = false;
+    __device__ __forceinline__ int count() const {
+        if (!sk) return my_tiles;
+        return hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0;
+    }
+    __device__ __forceinline__ long long total_kb() const { return sk ? hi - lo : (long long)my_tiles * KB; }
+    __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
+        if (!sk) {
+            tile = pair + idx * npairs;
+            kb0 = 0;
+            kb1 = KB;
+            return;
+        }
+        const long long t = lo / KB + idx;
+        const long long start = lo > t * KB ? lo : t * KB;
+        const long long end = hi < (t + 1) * KB ? hi : (t + 1) * KB;
+        tile = (int)t;
+        kb0 = (int)(start - t * KB);
+        kb1 = (int)(end - t * KB);
+    }
+};
+
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW, bool SK>
 __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
     static_assert(SS >= AS, "an A stage is released through the x ring");
@@ -85,8 +114,17 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     const int n_ft = (p.N + 255) / 256;
     const int n_tiles = n_mt * n_ft;
     const int KB = (p.K + BK - 1) / BK;
-    const int my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
-    const int total_kb = my_tiles * KB;  // k-blocks this pair runs, over all its tiles
+    PairWork work;
+    work.KB = KB;
+    work.pair = pair;
+    work.npairs = npairs;
+    work.my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+    work.sk = SK;
+    const long long units = (long long)n_tiles * KB;
+    work.lo = units * pair / npairs;
+    work.hi = units * (pair + 1) / npairs;
+    const int n_seg = work.count();
+    const int total_kb = (int)work.total_kb();  // k-blocks this pair runs, over all its segments
     int *err = p.err;
     const uint64_t lim = p.wait_limit_ns;
     const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
@@ -124,12 +162,13 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             const uint32_t w_tx = C::W_BYTES + (FMT != FMT_BF16 ? 128 * 4 * p.sgrp : 0) + C::F_BYTES;
             Ring xs;
             bool ok = true;
-            for (int j = 0; j < my_tiles && ok; ++j) {
-                const int tile = pair + j * npairs;
+            for (int j = 0; j < n_seg && ok; ++j) {
+                int tile, kb0, kb1;
+                work.seg(j, tile, kb0, kb1);
                 const int mt = tile % n_mt, ft = tile / n_mt;
                 const int row0 = ft * 256 + (int)rank * 128;
                 const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
-                for (int kb = 0; kb < KB; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_cluster_bounded(&x_empty[xs.s], xs.ph ^ 1, err, lim)) { ok = false; break; }
                     if (lead) mbar_arrive_expect_tx(&xb_full[xs.s], 2 * C::XH_BYTES);
                     mbar_arrive_expect_tx(&w_full[xs.s], w_tx);
@@ -167,11 +206,13 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             bool a_ready = x_ready && mbar_wait_cluster_bounded(&a_full[0], 0, err, lim);
             ok = total_kb == 0 || (x_ready && a_ready);
             int i = 0;
-            for (int j = 0; j < my_tiles && ok; ++j) {
+            for (int j = 0; j < n_seg && ok; ++j) {
+                int tile, kb0, kb1;
+                work.seg(j, tile, kb0, kb1);
                 if (!mbar_wait_cluster_bounded(&acc_empty[ab.s], ab.ph ^ 1, err, lim)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
-                for (int kb = 0; kb < KB; ++kb, ++i) {
+                for (int kb = kb0; kb < kb1; ++kb, ++i) {
                     // stage i is ready; look ahead at stage i + 1
                     Ring xn = xs, an = as;
                     xn.next<SS>();
@@ -184,9 +225,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                        mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc,
+                                        (kb != kb0 || kk != 0) ? 1u : 0u);
                     mma_commit_pair(&x_empty[xs.s], 0x3);
-                    if (kb == KB - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
+                    if (kb == kb1 - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
                     xs = xn;
                     as = an;
                     if (!xr) xr = mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim);
@@ -205,21 +247,50 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         const bool leader_thread = threadIdx.x == 128;
         int chunk_ctr = 0;
         Ring ab;
-        for (int j = 0; j < my_tiles; ++j) {
-            const int tile = pair + j * npairs;
+        const int64_t part_floats = (int64_t)128 * BT;  // one CTA's partial tile
+        for (int j = 0; j < n_seg; ++j) {
+            int tile, kb0, kb1;
+            work.seg(j, tile, kb0, kb1);
             const int mt = tile % n_mt, ft = tile / n_mt;
-            if (leader_thread) ctl->epi_ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+            PartialIO io;
+            int n_add = 0;
+            if (!SK) {
+            } else if (kb0 > 0) {
+                // the tail of a split tile: its owner adds it later
+                io.write = p.partials + (int64_t)(pair * 2 + (int)rank) * part_floats;
+            } else if (kb1 < KB) {
+                // the head of a split tile: the pairs after this one hold the rest
+                const long long tile_end = (long long)(tile + 1) * KB;
+                while (pair + 1 + n_add < npairs && units * (pair + 1 + n_add) / npairs < tile_end) ++n_add;
+            }
+            if (leader_thread) {
+                bool ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim);
+                for (int a = 0; SK && a < n_add && ok; ++a)
+                    ok = flag_wait_bounded(p.flags + (pair + 1 + a) * 2 + (int)rank, p.epoch, err, lim);
+                ctl->epi_ok = ok ? 1 : 0;
+            }
             named_bar_sync(1, EPI_THREADS);
             if (!ctl->epi_ok) break;
             tc_fence_after();
+            if (SK && n_add > 0) {
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                io.add = p.partials + (int64_t)((pair + 1) * 2 + (int)rank) * part_floats;
+                io.n_add = n_add;
+                io.add_stride = 2 * part_floats;
+            }
             const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
             const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
-            epilogue_tile(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
+            epilogue_tile<SK>(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
                           chunk_ctr, [&] {
                               tc_fence_before();
                               __syncwarp();
                               if (lane == 0) mbar_arrive_cluster(rel);
-                          });
+                          }, io);
+            if (SK && io.write) {
+                __threadfence();
+                named_bar_sync(1, EPI_THREADS);
+                if (leader_thread) flag_publish(p.flags + pair * 2 + (int)rank, p.epoch);
+            }
             ab.next<ACC>();
         }
     } else if (warp >= 8) {
@@ -286,10 +357,10 @@ constexpr int pair_stages(int fmt, int bt) {
     return n - n % 4;
 }
 
-template <int FMT, int BT, int ACC, int SS, int AS, int DQW = 4>
-static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
+template <int FMT, int BT, int ACC, int SS, int AS, bool SK, int DQW = 4>
+static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
-    auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW>;
+    auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW, SK>;
     constexpr int PAIR_THREADS = 32 * (8 + 4 * DQW);
     static int max_pairs = 0;
     const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
@@ -315,9 +386,18 @@ static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t 
         max_pairs = clusters > 0 ? clusters : 1;
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
-    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    // stream-K: every pair gets at least one k-block (the host checked
+    // n_tiles * KB >= pairs)
+    const long long work = SK ? (long long)n_tiles * ((p.K + BK - 1) / BK) : n_tiles;
+    const int pairs = work < max_pairs ? (int)work : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int FMT, int BT, int ACC, int SS, int AS>
+static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
+    return p.streamk ? pair_launch_sk<FMT, BT, ACC, SS, AS, true>(p, num_sms, st)
+                     : pair_launch_sk<FMT, BT, ACC, SS, AS, false>(p, num_sms, st);
 }
 
 template <int FMT>

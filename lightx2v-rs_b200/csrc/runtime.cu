@@ -40,6 +40,10 @@ struct lx2v_ctx {
     uint64_t wait_limit_ns = 2000000000ull;
     int path = 0;
     int token_tile = 0;
+    int split_mode = 0;          // 0 automatic, 1 whole tiles, 2 stream-K
+    void *sk_ws = nullptr;       // stream-K workspace: partial tiles + flags
+    size_t sk_ws_bytes = 0;
+    int sk_epoch = 0;
     uint64_t launches = 0;
     bool profile = false;
     std::map<std::string, ProfEntry> prof;
@@ -139,6 +143,31 @@ static void resolve_profile(lx2v_ctx *ctx) {
     ctx->pending.clear();
 }
 
+// Stream-K workspace: `pairs` x 2 partial tiles of 128 x bt f32, then the
+// pairs x 2 publication flags (zeroed when the workspace is allocated; they
+// hold launch epochs, so they never need clearing afterwards).
+static lx2v_status ensure_sk_workspace(lx2v_ctx *ctx, int pairs, int bt, float **partials, int **flags) {
+    const size_t flag_bytes = (size_t)ctx->num_sms * 2 * sizeof(int);  // >= pairs x 2 flags
+    const size_t part_bytes = (size_t)pairs * 2 * 128 * bt * sizeof(float);
+    if (ctx->sk_ws_bytes < part_bytes + flag_bytes) {
+        if (ctx->sk_ws) {
+            CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+            cudaFree(ctx->sk_ws);
+            ctx->sk_ws = nullptr;
+            ctx->sk_ws_bytes = 0;
+        }
+        // sized for the largest tile (256 tokens) on every SM pair at once
+        const size_t dflt = (size_t)((ctx->num_sms + 1) / 2) * 2 * 128 * 256 * sizeof(float);
+        const size_t bytes = (dflt > part_bytes ? dflt : part_bytes) + flag_bytes;
+        CUDA_TRY(ctx, cudaMalloc(&ctx->sk_ws, bytes));
+        CUDA_TRY(ctx, cudaMemsetAsync(ctx->sk_ws, 0, bytes, ctx->stream));
+        ctx->sk_ws_bytes = bytes;
+    }
+    *partials = (float *)ctx->sk_ws;
+    *flags = (int *)((char *)ctx->sk_ws + (ctx->sk_ws_bytes - flag_bytes));
+    return LX2V_OK;
+}
+
 static lx2v_status ensure_staging(lx2v_ctx *ctx, size_t bytes) {
     if (ctx->staging_bytes >= bytes) return LX2V_OK;
     if (ctx->staging) {
@@ -205,6 +234,7 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     }
     for (auto e : ctx->event_pool) cudaEventDestroy(e);
     if (ctx->staging) cudaFree(ctx->staging);
+    if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -586,6 +616,25 @@ static lx2v_status make_map(lx2v_ctx *ctx, CUtensorMap *map, const void *base, C
     return LX2V_OK;
 }
 
+// Stream-K pays when whole tiles leave most CTA pairs idle (a grid of fewer
+// tiles than pairs, e.g. a few hundred tokens against a long K): it spreads
+// the k-blocks over all pairs at the price of one partial tile written and
+// read per pair. With several waves of tiles it measured slower than whole
+// tiles on B200 (FFN2 of the 1.3B chunk: 762 vs 804 TFLOP/s), so it is only
+// taken when it at least shortens the critical path by 40%.
+static bool use_streamk(const lx2v_ctx *ctx, int M, int N, int K, int bt) {
+    if (ctx->split_mode == 1) return false;
+    const int pairs = ctx->num_sms / 2;
+    const long long tiles = (long long)((M + bt - 1) / bt) * ((N + 255) / 256);
+    const long long kb = (K + 63) / 64;
+    if (tiles * kb < pairs) return false;  // every pair needs at least one k-block
+    if (ctx->split_mode == 2) return true;
+    const long long waves = (tiles + pairs - 1) / pairs;
+    const double whole = (double)waves * kb;                       // k-blocks on the critical path
+    const double split = (double)tiles * kb / pairs + 16.0;        // + the partial tile's traffic
+    return split < 0.6 * whole;
+}
+
 static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf *x, size_t x_row,
                                size_t rows, const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
                                size_t y_row, const lx2v_buf *mods, size_t gate) {
@@ -671,6 +720,14 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         p.act = act;
         p.out_f32 = y->dtype == LX2V_F32;
         p.reduce = mods ? 1 : 0;
+        if (pair && use_streamk(ctx, (int)rows, (int)N, (int)K, bt)) {
+            const int pairs = ctx->num_sms / 2;
+            s = ensure_sk_workspace(ctx, pairs, bt, &p.partials, &p.flags);
+            if (s) return s;
+            p.streamk = 1;
+            if (++ctx->sk_epoch <= 0) ctx->sk_epoch = 1;
+            p.epoch = ctx->sk_epoch;
+        }
         if (pair) CUDA_TRY(ctx, gemm_pair_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
         else CUDA_TRY(ctx, gemm_dq_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
         ctx->launches++;
@@ -756,6 +813,13 @@ extern "C" lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path) {
     if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
     if (path < 0 || path > 4) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
     ctx->path = path;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_set_split_mode(lx2v_ctx *ctx, int mode) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (mode < 0 || mode > 2) return fail(ctx, LX2V_ERR_INVALID, "bad split mode %d", mode);
+    ctx->split_mode = mode;
     return LX2V_OK;
 }
 

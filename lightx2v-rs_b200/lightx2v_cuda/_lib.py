@@ -66,6 +66,7 @@ SIGNATURES = {
     "lx2v_profile_reset": (_st, [_vp]),
     "lx2v_set_linear_path": (_st, [_vp, ctypes.c_int]),
     "lx2v_set_token_tile": (_st, [_vp, ctypes.c_int]),
+    "lx2v_set_split_mode": (_st, [_vp, ctypes.c_int]),
     "lx2v_set_wait_limit_ns": (_st, [_vp, ctypes.c_uint64]),
     "lx2v_launch_count": (_st, [_vp, ctypes.POINTER(ctypes.c_uint64)]),
 }

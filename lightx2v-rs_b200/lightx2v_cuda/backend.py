@@ -259,6 +259,10 @@ class CudaBackend:
         """Tokens per tensor-core tile: 0 automatic, or 128 / 192 / 256."""
         self._check(self._lib.lx2v_set_token_tile(self._ctx, tokens))
 
+    def set_split_mode(self, mode: int):
+        """Work split of the CTA-pair kernel: 0 automatic, 1 whole tiles, 2 stream-K."""
+        self._check(self._lib.lx2v_set_split_mode(self._ctx, mode))
+
     def set_wait_limit_ns(self, ns: int):
         self._check(self._lib.lx2v_set_wait_limit_ns(self._ctx, ns))
 

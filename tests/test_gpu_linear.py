@@ -419,3 +419,62 @@ def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
     assert bad.size == 0, (fmt, path, bad.size, got[fin][bad[:4]], want[fin][bad[:4]])
     assert np.all(np.abs(got[tiny]) <= 2.0 ** -126)
 
+
+
+# ---- stream-K work split of the CTA-pair kernel ------------------------------------------
+@pytest.mark.parametrize("fmt", ["fp8", "q8", "q4", "native"])
+@pytest.mark.parametrize("M,N,K,bt", [(4680, 1536, 1536, 256), (1000, 512, 8960, 256), (700, 640, 4480, 192),
+                                      (2500, 1552, 704, 128)])
+def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt):
+    # tiles split over several CTA pairs, several partial tiles added into one
+    # (1000 x 512 x 8960: ~10 pairs per tile), ragged M and N
+    w, q = make_weight(fmt, N, K, seed=101 + K, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    x = oracle.normal(102, M * K)
+    b = oracle.normal(103, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b)
+    outs = {}
+    try:
+        be.set_linear_path(4)
+        be.set_token_tile(bt)
+        for mode in (2, 1):
+            be.set_split_mode(mode)
+            for rep in range(2):  # a second launch reuses the workspace with a new epoch
+                yb = be.alloc(M * N, F32)
+                be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
+                outs[(mode, rep)] = be.download(yb).reshape(M, N)
+    finally:
+        be.set_split_mode(0)
+        be.set_token_tile(0)
+        be.set_linear_path(0)
+    assert np.array_equal(outs[(2, 0)], outs[(2, 1)], equal_nan=True)
+    assert rel_l2(outs[(2, 0)], outs[(1, 0)]) <= 1e-5
+    rows = sampled_rows(M, 64)
+    want = np.stack([oracle.linear(x, 1, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=1,
+                                   x_row=int(r), threads=8)[0] for r in rows])
+    assert rel_l2(outs[(2, 0)][rows], want) <= REL_L2
+
+
+def test_stream_k_gated_residual_with_offsets(be, oracle):
+    M, N, K = 1800, 768, 4096
+    w, q = make_weight("fp8", N, K, seed=111, oracle=oracle)
+    dw = be.weight_fp8(q)
+    x = oracle.normal(112, (M + 40) * K)
+    h0 = oracle.normal(113, (M + 7) * N)
+    mods = oracle.normal(114, 6 * N, 0.5)
+    xb, mb = be.upload(x), be.upload(mods, F32)
+    hb = be.upload(h0, F32)
+    try:
+        be.set_linear_path(4)
+        be.set_split_mode(2)
+        be.linear_gate_residual(xb, 40, M, dw, None, Act.NONE, hb, 7, mb, 5)
+    finally:
+        be.set_split_mode(0)
+        be.set_linear_path(0)
+    got = be.download(hb).reshape(M + 7, N)
+    h0 = h0.reshape(M + 7, N)
+    assert np.array_equal(got[:7], h0[:7])
+    rows = sampled_rows(M, 48)
+    lin = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, x_row=40 + int(r), threads=8)[0] for r in rows])
+    want = oracle.gate_residual(h0[7:][rows].copy(), lin, len(rows), N, mods, 5)
+    assert rel_l2(got[7:][rows] - h0[7:][rows], want - h0[7:][rows]) <= REL_L2
