@@ -162,6 +162,32 @@ LX2V_API lx2v_status lx2v_profile_json(lx2v_ctx *ctx, char *buf, size_t cap, siz
 /* Backend::profile_reset. */
 LX2V_API lx2v_status lx2v_profile_reset(lx2v_ctx *ctx);
 
+/* Size of the scratch array behind lx2v_linear_noalloc: 10 MiB, held on
+ * every GPU that loads this library, for the whole life of the process. */
+#define LX2V_NOALLOC_SCRATCH_BYTES (10u * 1024u * 1024u)
+
+/* lx2v_linear without any device allocation. No counterpart in the
+ * reference (lightx2v-rs has no GPU linear; this is an addition for callers
+ * of this library). For callers that cannot let the library call cudaMalloc
+ * while they run: a serving loop whose device memory was planned up front
+ * and must not grow mid-request, or a caller for whom cudaMalloc's implicit
+ * device-wide synchronisation would stall other streams.
+ * Same arguments and result as lx2v_linear (no gated residual); it always
+ * runs the CTA-pair tensor-core kernel with a stream-K split, and keeps the
+ * split's partial tiles in a fixed array of LX2V_NOALLOC_SCRATCH_BYTES inside
+ * the library instead of a context workspace.
+ * - The first call on a device looks up that array's device address
+ *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ * - Every call on a device shares the array: calls whose kernels may overlap
+ *   on the GPU (other streams or contexts on the same device) race and give
+ *   wrong results. Serialise them.
+ * - LX2V_ERR_UNSUPPORTED when the shape cannot use the tensor-core kernel
+ *   (x not bf16, K or N not a multiple of 16, fewer than 16 rows, ...) or the
+ *   GPU has so many SMs that its partial tiles would not fit the array. */
+LX2V_API lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
+                                         const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                                         size_t y_row);
+
 /* ---- knobs for tests and benchmarks -------------------------------------- */
 /* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05, one
  * CTA per tile), 2 = small-M GEMV, 3 = generic CUDA-core kernel, 4 = tensor-

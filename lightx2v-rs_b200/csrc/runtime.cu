@@ -844,3 +844,141 @@ extern "C" lx2v_status lx2v_launch_count(lx2v_ctx *ctx, uint64_t *count) {
     *count = ctx->launches;
     return LX2V_OK;
 }
+
+// ---- linear without device allocation -------------------------------------------------
+// Some callers cannot let the library call cudaMalloc during a linear: a
+// serving loop that planned all of its device memory up front (the
+// reference's VRAM plan) and must not grow it in the middle of a request, or
+// a caller for whom cudaMalloc's implicit device-wide synchronisation would
+// stall work on other streams. lx2v_linear may allocate (the stream-K
+// workspace, grown on first use); lx2v_linear_noalloc runs the same CTA-pair
+// kernel with its stream-K scratch in a fixed array that the library holds
+// on every device it is loaded on, and allocates nothing.
+//
+// The scratch: [flags: LX2V_NOALLOC_FLAG_BYTES][partial tiles ...]. The
+// flags hold launch epochs (a per-device counter below), so they start at
+// zero (static initialisation) and never need clearing while epochs grow.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LX2V_NOALLOC_SCRATCH_BYTES];
+static constexpr size_t LX2V_NOALLOC_FLAG_BYTES = 4096;
+static constexpr int LX2V_NOALLOC_MAX_DEVICES = 64;
+static constexpr int LX2V_NOALLOC_TOKENS = 128;  // token tile: smallest partial tiles
+
+struct NoallocDevice {
+    void *scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int epoch = 0;
+};
+static NoallocDevice g_noalloc[LX2V_NOALLOC_MAX_DEVICES];
+static std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on ctx->dev (current device), looked up
+// once per device. In host code g_noalloc_scratch names a host-side shadow,
+// not device memory, so the kernel must get this address instead.
+static lx2v_status noalloc_scratch(lx2v_ctx *ctx, void **ptr, int *epoch) {
+    if (ctx->dev < 0 || ctx->dev >= LX2V_NOALLOC_MAX_DEVICES)
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "device %d is beyond the %d devices the static scratch tracks",
+                    ctx->dev, LX2V_NOALLOC_MAX_DEVICES);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoallocDevice &d = g_noalloc[ctx->dev];
+    if (!d.scratch) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(ctx, LX2V_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s", ctx->dev,
+                        cudaGetErrorString(e));
+        d.scratch = p;
+    }
+    if (++d.epoch <= 0) {
+        // epoch counter wrapped: old flags could match again, so clear them
+        CUDA_TRY(ctx, cudaMemsetAsync(d.scratch, 0, LX2V_NOALLOC_FLAG_BYTES, ctx->stream));
+        d.epoch = 1;
+    }
+    *ptr = d.scratch;
+    *epoch = d.epoch;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
+                                           const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                                           size_t y_row) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!x || !w || !y) return fail(ctx, LX2V_ERR_INVALID, "null x, weight or output");
+    if (act != LX2V_ACT_NONE && act != LX2V_ACT_GELU_TANH) return fail(ctx, LX2V_ERR_INVALID, "bad act %d", act);
+    if (x == y || (x->ptr && x->ptr == y->ptr)) return fail(ctx, LX2V_ERR_INVALID, "output aliases input");
+    const size_t N = w->rows, K = w->cols;
+    if ((x_row + rows) * K > x->len)
+        return fail(ctx, LX2V_ERR_INVALID, "x has %zu elements, rows [%zu, %zu) x %zu need more", x->len, x_row,
+                    x_row + rows, K);
+    if ((y_row + rows) * N > y->len)
+        return fail(ctx, LX2V_ERR_INVALID, "output has %zu elements, rows [%zu, %zu) x %zu need more", y->len,
+                    y_row, y_row + rows, N);
+    if (bias && bias->len < N) return fail(ctx, LX2V_ERR_INVALID, "bias has %zu elements, need %zu", bias->len, N);
+    if (rows == 0) return LX2V_OK;
+    if (rows > (1u << 30)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "too many rows");
+    const size_t grp = w->group;
+    const bool groups_ok = w->fmt == LX2V_W_BF16 || grp % 64 == 0 ||
+                           (w->fmt == LX2V_W_Q4 && (grp == 16 || grp == 32));
+    if (!(x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 && groups_ok &&
+          unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16))
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "the tensor-core kernel does not take this shape/dtype");
+    // Scratch this launch may touch: every pair of the grid holds two
+    // 128 x 128 f32 partial tiles, plus the flags.
+    const int bt = LX2V_NOALLOC_TOKENS;
+    const int pairs = ctx->num_sms / 2;
+    const size_t need = LX2V_NOALLOC_FLAG_BYTES + (size_t)pairs * 2 * 128 * bt * sizeof(float);
+    if (pairs * 2 * (int)sizeof(int) > (int)LX2V_NOALLOC_FLAG_BYTES || need > LX2V_NOALLOC_SCRATCH_BYTES)
+        return fail(ctx, LX2V_ERR_UNSUPPORTED,
+                    "this GPU (%d SMs) needs %zu bytes of scratch, beyond the %zu-byte static maximum",
+                    ctx->num_sms, need, (size_t)LX2V_NOALLOC_SCRATCH_BYTES);
+    GemmParams p;
+    memset(&p, 0, sizeof p);
+    s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
+                 (uint32_t)(bt / 2), CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s) return s;
+    if (w->fmt == LX2V_W_Q4)
+        s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 32, 128,
+                     CU_TENSOR_MAP_SWIZZLE_32B);
+    else if (w->fmt == LX2V_W_BF16)
+        s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+        s = make_map(ctx, &p.tmap_w, w->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+    if (s) return s;
+    if (w->fmt != LX2V_W_BF16) {
+        const int sgrp = grp % 64 == 0 ? 1 : (int)(64 / grp);
+        p.sgrp = sgrp;
+        p.gshift = grp % 64 == 0 ? 6 : (grp == 16 ? 4 : 5);
+        s = make_map(ctx, &p.tmap_s, w->fmt == LX2V_W_Q4 ? (void *)w->sz_t : (void *)w->scales_t,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, N, K / grp, 128, (uint32_t)sgrp, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s) return s;
+    }
+    if (w->fmt == LX2V_W_FP8) {
+        s = make_map(ctx, &p.tmap_f, w->flags, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, (size_t)fp8_flag_cols((int)K),
+                     128, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s) return s;
+    }
+    void *scratch = nullptr;
+    int epoch = 0;
+    s = noalloc_scratch(ctx, &scratch, &epoch);
+    if (s) return s;
+    p.y = y->ptr;
+    p.codes = (const uint8_t *)w->codes;
+    p.scales_t = w->scales_t;
+    p.sz_t = w->sz_t;
+    p.bias = bias ? bias->ptr : nullptr;
+    p.bias_f32 = bias && bias->dtype == LX2V_F32;
+    p.err = ctx->err_dev;
+    p.wait_limit_ns = ctx->wait_limit_ns;
+    p.M = (int)rows; p.N = (int)N; p.K = (int)K; p.group = (int)w->group;
+    p.x_row = (int)x_row; p.y_row = (int)y_row;
+    p.act = act;
+    p.out_f32 = y->dtype == LX2V_F32;
+    p.streamk = 1;
+    p.epoch = epoch;
+    p.flags = (int *)scratch;
+    p.partials = (float *)((char *)scratch + LX2V_NOALLOC_FLAG_BYTES);
+    CUDA_TRY(ctx, gemm_pair_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}

@@ -59,6 +59,7 @@ SIGNATURES = {
                                ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "lx2v_weight_dequant_f32": (_st, [_vp, _vp, _vp]),
     "lx2v_linear": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz]),
+    "lx2v_linear_noalloc": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz]),
     "lx2v_linear_gate_residual": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz,
                                         _vp, _sz]),
     "lx2v_gate_residual": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _sz]),

@@ -238,6 +238,18 @@ class CudaBackend:
                                           bias.handle if bias is not None else None, act,
                                           y.handle, y_row))
 
+    def linear_noalloc(self, x: Buf, x_row: int, rows: int, w: Weight, bias: Buf | None, act: int,
+                       y: Buf, y_row: int):
+        """linear() for callers that cannot have the library allocate device
+        memory mid-run (a pre-planned VRAM budget, or no tolerance for
+        cudaMalloc's device-wide synchronisation): the stream-K scratch lives
+        in a fixed LX2V_NOALLOC_SCRATCH_BYTES array inside the library. Calls
+        that may overlap on one GPU share that array and race; the first call
+        on a device looks the array up, so make it before any stream capture."""
+        self._check(self._lib.lx2v_linear_noalloc(self._ctx, x.handle, x_row, rows, w.handle,
+                                                  bias.handle if bias is not None else None, act,
+                                                  y.handle, y_row))
+
     def linear_gate_residual(self, x: Buf, x_row: int, rows: int, w: Weight, bias: Buf | None,
                              act: int, h: Buf, h_row: int, mods: Buf, gate: int):
         """h[h_row + i, j] += act(x[x_row + i, :] . W^T + b)[j] * mods[gate * N + j]."""
