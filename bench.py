@@ -78,58 +78,109 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML polled every ~2 ms from a thread (the region is tens of
+    milliseconds, shorter than nvidia-smi's sampling period); nvidia-smi is
+    the fallback when NVML is unavailable."""
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
-        self.proc = None
-        self.out = []
+    # NVML clocks-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []          # (time, sm_mhz, reasons_mask)
+        self.max_mhz = None
+        self.region = (None, None)
+        self._stop = threading.Event()
+        self._nvml = None
+        self._smi = None
+
+    def _handle(self, nv):
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._nvml = (nv, h)
+            self._t = threading.Thread(target=self._poll_nvml, daemon=True)
+            self._t.start()
         except Exception:
-            self.proc = None
+            self._nvml = None
+            q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            try:
+                self._smi = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._t = threading.Thread(target=self._read_smi, daemon=True)
+                self._t.start()
+            except Exception:
+                self._smi = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.out.append(line.strip())
-
-    def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
+    def _poll_nvml(self):
+        nv, h = self._nvml
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                try:
+                    mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except AttributeError:
+                    mask = int(nv.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+                self.samples.append((time.perf_counter(), mhz, mask))
             except Exception:
-                self.proc.kill()
+                return
+            time.sleep(0.002)
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.out:
+    def _read_smi(self):
+        bits = [0x8, 0x40, 0x20, 0x4]
+        for line in self._smi.stdout:
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 7:
+            if len(f) < 6:
                 continue
             try:
-                sm.append(float(f[0]))
-                mx = float(f[1])
+                mhz, self.max_mhz = float(f[0]), float(f[1])
             except ValueError:
                 continue
-            for name, v in zip(names, f[3:7]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            mask = sum(b for b, v in zip(bits, f[2:6]) if v.lower().startswith("active"))
+            self.samples.append((time.perf_counter(), mhz, mask))
+
+    def start_region(self):
+        self.region = (time.perf_counter(), None)
+
+    def end_region(self):
+        self.region = (self.region[0], time.perf_counter())
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._smi:
+            self._smi.terminate()
+            try:
+                self._smi.wait(timeout=5)
+            except Exception:
+                self._smi.kill()
+        if self._nvml:
+            self._t.join(timeout=1)
+
+    def summary(self):
+        t0, t1 = self.region
+        inside = [s for s in self.samples if t0 is not None and t1 is not None and t0 <= s[0] <= t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": "nvml" if self._nvml else "nvidia-smi"}
+        reasons = sorted({name for _, _, m in inside for bit, name in self.REASONS.items() if m & bit})
+        return {"sm_mhz": float(np.median([s[1] for s in inside])), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(inside), "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
 def make_inputs(m: int, seed_offset: int = 0):
@@ -259,6 +310,8 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     launches0 = be.launch_count()
     pairs = []
     with ClockSampler(local_rank) as clk:
+        time.sleep(0.01)  # first NVML samples before the region
+        clk.start_region()
         for _ in range(args.steps):
             flush_l2()
             a, b = ev(), ev()
@@ -267,6 +320,7 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
             b.record(ext)
             pairs.append((a, b))
         be.sync()
+        clk.end_region()
     barrier()
     launches = be.launch_count() - launches0
     step_ms = [a.elapsed_time(b) for a, b in pairs]

@@ -195,9 +195,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA) ----------------
-        // The readiness of stage i + 1 is tested (without blocking) before the
-        // MMAs of stage i are issued, so the barrier round trip overlaps the
-        // tensor pipe's work instead of idling it between k-blocks.
+        // One wait per barrier per k-block, right before its MMAs: the MMAs
+        // already issued keep the tensor pipe busy meanwhile. (Non-blocking
+        // look-ahead tests of the next stage measured slower on B200: each
+        // barrier access is a ~150-cycle round trip on this thread's path.)
         if (lane == 0 && lead) {
             const uint32_t idesc = idesc_bf16_f32(256, BT);
             bool ok = true;
@@ -213,13 +214,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
                 for (int kb = kb0; kb < kb1; ++kb, ++i) {
-                    // stage i is ready; look ahead at stage i + 1
-                    Ring xn = xs, an = as;
-                    xn.next<SS>();
-                    an.next<AS>();
-                    const bool more = i + 1 < total_kb;
-                    bool xr = more ? mbar_test_wait(&xb_full[xn.s], xn.ph) : true;
-                    bool ar = more ? mbar_test_wait(&a_full[an.s], an.ph) : true;
+                    if (i > 0 && (!mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim) ||
+                                  !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim))) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
@@ -229,12 +225,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                                         (kb != kb0 || kk != 0) ? 1u : 0u);
                     mma_commit_pair(&x_empty[xs.s], 0x3);
                     if (kb == kb1 - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
-                    xs = xn;
-                    as = an;
-                    if (!xr) xr = mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim);
-                    if (xr && !ar) ar = mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim);
-                    if (!xr || !ar) { ok = false; break; }
+                    xs.next<SS>();
+                    as.next<AS>();
                 }
+                if (!ok) break;
                 ab.next<ACC>();
             }
             mma_commit_pair(drain, 0x1);
