@@ -23,7 +23,10 @@
 //               stage for the producer and, AS k-blocks later, the TMEM A
 //               stage for the dequant warps (one commit per k-block).
 //   a_full[a]   leader; 8 arrivals (the 4 warps of the dequant warpgroup that
-//               owns the k-block, in both CTAs; remote for the peer)
+//               owns the k-block, in both CTAs; remote for the peer). When the
+//               two rings have the same depth (SS == AS) a_full is xb_full
+//               itself (9 arrivals + the x bytes) and the MMA thread waits on
+//               one barrier per k-block.
 //   acc_full[b] each CTA; multicast commit
 //   acc_empty[b] leader; 8 arrivals (4 epilogue warps x 2 CTAs)
 #include <cuda.h>
@@ -100,8 +103,12 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     uint64_t *xb_full = bars;               // [SS]  leader: both x halves
     uint64_t *w_full = xb_full + SS;        // [SS]  own codes + side data
     uint64_t *x_empty = w_full + SS;        // [SS]  multicast commit: MMA of the stage done
-    uint64_t *a_full = x_empty + SS;        // [AS]  leader: dequant warps of both CTAs
-    uint64_t *acc_full = a_full + AS;       // [ACC] multicast commit
+    // With equal ring depths one barrier per stage carries both the x bytes
+    // and the dequant arrivals, so the MMA thread waits once per k-block.
+    constexpr bool MERGED = SS == AS;
+    uint64_t *a_full_sep = x_empty + SS;     // [AS]  leader: dequant warps of both CTAs (unmerged rings)
+    uint64_t *a_full = MERGED ? xb_full : a_full_sep;
+    uint64_t *acc_full = a_full_sep + AS;   // [ACC] multicast commit
     uint64_t *acc_empty = acc_full + ACC;   // [ACC] leader: 8 epilogue warps
     uint64_t *drain = acc_empty + ACC;      // [1]   leader: final MMA drain
     PairCtl *ctl = reinterpret_cast<PairCtl *>(drain + 1);
@@ -131,11 +138,12 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SS; ++s) {
-            mbar_init(&xb_full[s], 1);
+            mbar_init(&xb_full[s], MERGED ? 9 : 1);
             mbar_init(&w_full[s], 1);
             mbar_init(&x_empty[s], 1);
         }
-        for (int s = 0; s < AS; ++s) mbar_init(&a_full[s], 8);
+        if (!MERGED)
+            for (int s = 0; s < AS; ++s) mbar_init(&a_full[s], 8);
         for (int b = 0; b < ACC; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 8);
@@ -204,7 +212,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             bool ok = true;
             Ring xs, as, ab;
             bool x_ready = total_kb > 0 && mbar_wait_cluster_bounded(&xb_full[0], 0, err, lim);
-            bool a_ready = x_ready && mbar_wait_cluster_bounded(&a_full[0], 0, err, lim);
+            bool a_ready = x_ready && (MERGED || mbar_wait_cluster_bounded(&a_full[0], 0, err, lim));
             ok = total_kb == 0 || (x_ready && a_ready);
             int i = 0;
             for (int j = 0; j < n_seg && ok; ++j) {
@@ -215,7 +223,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
                 for (int kb = kb0; kb < kb1; ++kb, ++i) {
                     if (i > 0 && (!mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim) ||
-                                  !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim))) { ok = false; break; }
+                                  (!MERGED && !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim)))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
