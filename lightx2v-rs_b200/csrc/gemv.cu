@@ -1,0 +1,262 @@
+// gemv.cu — the quantized linear for a few tokens (M <= 16): bandwidth-bound.
+//
+// Same computation as Backend::linear (crates/lightx2v-core/src/backend.rs:
+// 199-212; CPU reference crates/lightx2v-cpu/src/lib.rs:296-326) with the same
+// operand rounding as the tensor-core kernels (exact dequantisation rounded to
+// bf16, activations bf16, f32 accumulation), for the regime where the weight
+// stream dominates: every weight byte is read once, 16 bytes per thread per
+// load, and decoded in registers straight into mma.sync B fragments.
+//
+// Work split: a CTA of 8 warps owns 64 weight rows (8 per warp, the MMA's N)
+// and one k-range (split-K when there are too few row tiles to fill the GPU).
+// The MMA's M = 16 token rows (x rows beyond M are zero); x's k-range is
+// staged in shared memory once per CTA.
+//
+// k permutation: in mma.m16n8k16 the thread with c = lane % 4 holds the B
+// values at k positions {2c, 2c+1, 2c+8, 2c+9} of a 16-wide step. Thread c
+// loads 16 (Q4: 32) contiguous codes of its row, k = kc + c*VT + j, and step
+// s uses its values j = 4s..4s+3 at those positions; the A fragment (x) of
+// the threads with the same c reads x at the same four k, so every k of the
+// chunk meets its own x exactly once and the dot products are unchanged.
+//
+// Split-K partials go to a workspace; the last CTA of a row tile (atomic
+// arrival count, reset by that CTA) adds them in split order, so results do
+// not depend on CTA timing.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "gemm_common.cuh"  // decoders, GELU
+
+namespace lx2v {
+
+namespace {
+
+constexpr int GV_WARPS = 8;
+constexpr int GV_ROWS = 8 * GV_WARPS;  // weight rows per CTA
+constexpr int GV_THREADS = 32 * GV_WARPS;
+
+template <int FMT>
+struct GvFmt {
+    static constexpr int UNITS = FMT == FMT_Q4 ? 2 : 1;  // 16-value units per thread per chunk
+    static constexpr int VT = 16 * UNITS;                // values per thread per chunk
+    static constexpr int KC = 4 * VT;                    // k per warp chunk
+    static constexpr int STEPS = VT / 4;                 // mma k-steps per chunk
+};
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float ld_elem(const void *p, int f32, int64_t i) {
+    return f32 ? reinterpret_cast<const float *>(p)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+}
+
+// Raw codes of one thread for one chunk (16 bytes; 32 for bf16 weights).
+template <int FMT>
+struct GvRaw {
+    uint4 a, b;
+};
+
+template <int FMT>
+__device__ __forceinline__ GvRaw<FMT> gv_load(const LinearArgs &a, int n, int k) {
+    GvRaw<FMT> r;
+    r.a = make_uint4(0, 0, 0, 0);
+    r.b = make_uint4(0, 0, 0, 0);
+    if (n >= a.N) return r;
+    if (FMT == FMT_Q4) {
+        r.a = __ldg(reinterpret_cast<const uint4 *>(a.codes + ((int64_t)n * a.K + k) / 2));
+    } else if (FMT == FMT_BF16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(a.codes + ((int64_t)n * a.K + k) * 2);
+        r.a = __ldg(p);
+        r.b = __ldg(p + 1);
+    } else {
+        r.a = __ldg(reinterpret_cast<const uint4 *>(a.codes + (int64_t)n * a.K + k));
+    }
+    return r;
+}
+
+// Decode one thread's chunk (values k .. k + VT of row n) to bf16 pairs:
+// out[8u + i] = values (16u + 2i, 16u + 2i + 1).
+template <int FMT>
+__device__ __forceinline__ void gv_decode(const LinearArgs &a, int n, int k, const GvRaw<FMT> &raw,
+                                          uint32_t (&out)[8 * GvFmt<FMT>::UNITS]) {
+    const int nn = n < a.N ? n : a.N - 1;  // rows past N decode zeros from zero codes
+#pragma unroll
+    for (int u = 0; u < GvFmt<FMT>::UNITS; ++u) {
+        const int ku = k + 16 * u;
+        uint32_t o[8];
+        if (FMT == FMT_BF16) {
+            unit_to_bf16<FMT_BF16>(raw.a, raw.b, 0.0f, 0.0f, 0, o);
+        } else if (FMT == FMT_Q4) {
+            float s, z;
+            q4_scale_zero(__ldg(a.sz_t + (int64_t)(ku / a.group) * a.N + nn), s, z);
+            const uint4 r4 = u == 0 ? make_uint4(raw.a.x, raw.a.y, 0, 0) : make_uint4(raw.a.z, raw.a.w, 0, 0);
+            unit_to_bf16<FMT_Q4>(r4, r4, s, z, 0, o);
+        } else {
+            const float s = __ldg(a.scales_t + (int64_t)(ku / a.group) * a.N + nn);
+            const int mode = FMT == FMT_FP8 ? (int)__ldg(a.flags + (int64_t)(ku / 32) * a.N + nn) : 0;
+            unit_to_bf16<FMT>(raw.a, raw.a, s, 0.0f, mode, o);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[8 * u + i] = o[i];
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int splits, int kchunks_per_split,
+                                                         float *partials, int *arrivals) {
+    using F = GvFmt<FMT>;
+    extern __shared__ __align__(16) uint8_t gv_smem[];
+    const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
+    const int n_chunks = a.K / F::KC;
+    const int c_begin = split * kchunks_per_split;
+    const int c_end = min(n_chunks, c_begin + kchunks_per_split);
+    const int k_begin = c_begin * F::KC;
+    const int kext = max(0, (c_end - c_begin) * F::KC);
+    // x rows (16, zero beyond M) of this k-range, bf16, row stride kext + 8
+    const int xs_stride = kext + 8;
+    __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(gv_smem);
+    for (int e = threadIdx.x; e < 16 * (kext / 2); e += GV_THREADS) {
+        const int r = e / (kext / 2), kk = 2 * (e % (kext / 2));
+        float v0 = 0.0f, v1 = 0.0f;
+        if (r < a.M) {
+            const int64_t base = ((int64_t)a.x_row + r) * a.K + k_begin + kk;
+            v0 = ld_elem(a.x, a.x_f32, base);
+            v1 = ld_elem(a.x, a.x_f32, base + 1);
+        }
+        *reinterpret_cast<__nv_bfloat162 *>(xs + r * xs_stride + kk) = __floats2bfloat162_rn(v0, v1);
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int n_warp = tile * GV_ROWS + warp * 8;  // first of this warp's 8 rows
+    const int n = n_warp + g;                      // this thread's B row
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const uint32_t xrow0 = (uint32_t)__cvta_generic_to_shared(xs + g * xs_stride);
+    const uint32_t xrow1 = (uint32_t)__cvta_generic_to_shared(xs + (g + 8) * xs_stride);
+
+    // two chunks of codes in flight per thread
+    GvRaw<FMT> cur = gv_load<FMT>(a, n, k_begin + c * F::VT);
+    for (int ch = c_begin; ch < c_end; ++ch) {
+        const int kc = ch * F::KC;
+        GvRaw<FMT> nxt = cur;
+        if (ch + 1 < c_end) nxt = gv_load<FMT>(a, n, kc + F::KC + c * F::VT);
+        uint32_t w[8 * F::UNITS];
+        gv_decode<FMT>(a, n, kc + c * F::VT, cur, w);
+        const uint32_t xoff = (uint32_t)((kc - k_begin + c * F::VT) * 2);
+#pragma unroll
+        for (int s = 0; s < F::STEPS; ++s) {
+            uint32_t x00, x01, x10, x11;
+            asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(x00), "=r"(x01) : "r"(xrow0 + xoff + 8 * s));
+            asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(x10), "=r"(x11) : "r"(xrow1 + xoff + 8 * s));
+            mma_bf16_16816(d, x00, x10, x01, x11, w[2 * s], w[2 * s + 1]);
+        }
+        cur = nxt;
+    }
+
+    // C fragment: d0, d1 = token g, rows n_warp + 2c, +1; d2, d3 = token g + 8.
+    const int nc = n_warp + 2 * c;
+    if (splits > 1) {
+        float *mine = partials + (int64_t)blockIdx.x * (16 * GV_ROWS);
+        const int col = warp * 8 + 2 * c;
+        __stcg(reinterpret_cast<float2 *>(mine + g * GV_ROWS + col), make_float2(d[0], d[1]));
+        __stcg(reinterpret_cast<float2 *>(mine + (g + 8) * GV_ROWS + col), make_float2(d[2], d[3]));
+        __threadfence();
+        __syncthreads();
+        __shared__ int last;
+        if (threadIdx.x == 0) last = atomicAdd(arrivals + tile, 1) == splits - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int sp = 0; sp < splits; ++sp) {
+            const float *p = partials + (int64_t)(tile * splits + sp) * (16 * GV_ROWS);
+            const float2 u0 = __ldcg(reinterpret_cast<const float2 *>(p + g * GV_ROWS + col));
+            const float2 u1 = __ldcg(reinterpret_cast<const float2 *>(p + (g + 8) * GV_ROWS + col));
+            t[0] += u0.x; t[1] += u0.y; t[2] += u1.x; t[3] += u1.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] = t[i];
+        if (threadIdx.x == 0) arrivals[tile] = 0;  // ready for the next launch
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int tok = g + 8 * h;
+        if (tok >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int nn = nc + j;
+            if (nn >= a.N) continue;
+            float v = d[2 * h + j];
+            if (a.bias) v += ld_elem(a.bias, a.bias_f32, nn);
+            if (a.act == 1) v = gelu2(make_float2(v, v)).x;
+            const int64_t yi = ((int64_t)a.y_row + tok) * a.N + nn;
+            if (a.gate) v = ld_elem(a.y, a.y_f32, yi) + v * ld_elem(a.gate, a.gate_f32, nn);
+            if (a.y_f32) reinterpret_cast<float *>(a.y)[yi] = v;
+            else reinterpret_cast<__nv_bfloat16 *>(a.y)[yi] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+template <int FMT>
+cudaError_t gemv_launch_t(const LinearArgs &a, int num_sms, float *partials, int *arrivals, size_t ws_floats,
+                          cudaStream_t st) {
+    using F = GvFmt<FMT>;
+    const int tiles = (a.N + GV_ROWS - 1) / GV_ROWS;
+    const int n_chunks = a.K / F::KC;
+    // aim for two CTAs per SM, each split at least 4 chunks long
+    int splits = (2 * num_sms + tiles - 1) / tiles;
+    splits = splits < 1 ? 1 : splits;
+    splits = splits > n_chunks / 4 ? (n_chunks / 4 > 0 ? n_chunks / 4 : 1) : splits;
+    if ((size_t)tiles * splits * 16 * GV_ROWS > ws_floats) splits = 1;
+    const int per = (n_chunks + splits - 1) / splits;
+    splits = (n_chunks + per - 1) / per;
+    const size_t smem = (size_t)16 * (per * F::KC + 8) * 2;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;  // workspace too small to split K
+    auto kern = gemv_kernel<FMT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<tiles * splits, GV_THREADS, smem, st>>>(a, splits, per, partials, arrivals);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemv_supported(const LinearArgs &a) {
+    if (a.M < 1 || a.M > 16 || a.N < 1) return false;
+    switch (a.fmt) {
+        case FMT_Q4: return a.K % GvFmt<FMT_Q4>::KC == 0 && a.group % 32 == 0;
+        case FMT_Q8:
+        case FMT_FP8: return a.K % 64 == 0 && a.group % 16 == 0;
+        default: return a.K % 64 == 0;
+    }
+}
+
+// partials: at least gemv_workspace_floats(N, num_sms) floats; arrivals:
+// ceil(N / 64) ints, zero before the first launch (kernels leave them zero).
+size_t gemv_workspace_floats(int N, int num_sms) {
+    const int tiles = (N + GV_ROWS - 1) / GV_ROWS;
+    const int splits = (2 * num_sms + tiles - 1) / tiles;
+    return (size_t)tiles * (splits < 1 ? 1 : splits) * 16 * GV_ROWS;
+}
+
+cudaError_t linear_gemv_launch(const LinearArgs &a, int num_sms, cudaStream_t st, float *partials, int *arrivals,
+                               size_t ws_floats) {
+    switch (a.fmt) {
+        case FMT_Q8: return gemv_launch_t<FMT_Q8>(a, num_sms, partials, arrivals, ws_floats, st);
+        case FMT_Q4: return gemv_launch_t<FMT_Q4>(a, num_sms, partials, arrivals, ws_floats, st);
+        case FMT_FP8: return gemv_launch_t<FMT_FP8>(a, num_sms, partials, arrivals, ws_floats, st);
+        default: return gemv_launch_t<FMT_BF16>(a, num_sms, partials, arrivals, ws_floats, st);
+    }
+}
+
+}  // namespace lx2v

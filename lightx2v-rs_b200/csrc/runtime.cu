@@ -44,6 +44,10 @@ struct lx2v_ctx {
     void *sk_ws = nullptr;       // stream-K workspace: partial tiles + flags
     size_t sk_ws_bytes = 0;
     int sk_epoch = 0;
+    float *gemv_ws = nullptr;    // few-token kernel: split-K partials + arrival counters
+    size_t gemv_ws_floats = 0;
+    int *gemv_arrivals = nullptr;
+    size_t gemv_tiles = 0;
     uint64_t launches = 0;
     bool profile = false;
     std::map<std::string, ProfEntry> prof;
@@ -168,6 +172,28 @@ static lx2v_status ensure_sk_workspace(lx2v_ctx *ctx, int pairs, int bt, float *
     return LX2V_OK;
 }
 
+// Few-token kernel workspace for an output width N: partial tiles, then one
+// arrival counter per 64-row tile (zeroed here; the kernel leaves them zero).
+static lx2v_status ensure_gemv_workspace(lx2v_ctx *ctx, int N) {
+    const size_t floats = gemv_workspace_floats(N, ctx->num_sms);
+    const size_t tiles = (size_t)(N + 63) / 64;
+    if (ctx->gemv_ws_floats >= floats && ctx->gemv_tiles >= tiles) return LX2V_OK;
+    if (ctx->gemv_ws) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->gemv_ws);
+        ctx->gemv_ws = nullptr;
+    }
+    const size_t f = floats > ctx->gemv_ws_floats ? floats : ctx->gemv_ws_floats;
+    const size_t t = tiles > ctx->gemv_tiles ? tiles : ctx->gemv_tiles;
+    const size_t bytes = f * sizeof(float) + t * sizeof(int);
+    CUDA_TRY(ctx, cudaMalloc(&ctx->gemv_ws, bytes));
+    CUDA_TRY(ctx, cudaMemsetAsync(ctx->gemv_ws, 0, bytes, ctx->stream));
+    ctx->gemv_ws_floats = f;
+    ctx->gemv_tiles = t;
+    ctx->gemv_arrivals = (int *)(ctx->gemv_ws + f);
+    return LX2V_OK;
+}
+
 static lx2v_status ensure_staging(lx2v_ctx *ctx, size_t bytes) {
     if (ctx->staging_bytes >= bytes) return LX2V_OK;
     if (ctx->staging) {
@@ -235,6 +261,7 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     for (auto e : ctx->event_pool) cudaEventDestroy(e);
     if (ctx->staging) cudaFree(ctx->staging);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
+    if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -663,11 +690,32 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
                            (w->fmt == LX2V_W_Q4 && (grp == 16 || grp == 32));
     const bool tc_ok = x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 && groups_ok &&
                        unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16;
+    LinearArgs a;
+    memset(&a, 0, sizeof a);
+    a.fmt = w->fmt; a.codes = (const uint8_t *)w->codes; a.scales_t = w->scales_t; a.sz_t = w->sz_t;
+    a.flags = w->flags;
+    a.M = (int)rows; a.N = (int)N; a.K = (int)K; a.group = (int)w->group;
+    a.x = x->ptr; a.x_f32 = x->dtype == LX2V_F32; a.x_row = (int64_t)x_row;
+    a.y = y->ptr; a.y_f32 = y->dtype == LX2V_F32; a.y_row = (int64_t)y_row;
+    a.bias = bias ? bias->ptr : nullptr; a.bias_f32 = bias && bias->dtype == LX2V_F32;
+    a.gate = gate_ptr; a.gate_f32 = mods && mods->dtype == LX2V_F32;
+    a.act = act;
+    const bool gemv_ok = gemv_supported(a);
     int path = ctx->path;
-    if (path == 0) path = tc_ok ? (rows >= 512 && N >= 256 ? 4 : 1) : 3;
+    if (path == 0) path = rows <= 16 && gemv_ok ? 2 : tc_ok ? (rows >= 512 && N >= 256 ? 4 : 1) : 3;
     if ((path == 1 || path == 4) && !tc_ok)
         return fail(ctx, LX2V_ERR_UNSUPPORTED, "the tensor-core kernel does not take this shape/dtype");
-    if (path == 2) return fail(ctx, LX2V_ERR_UNSUPPORTED, "the small-M kernel is not built in this version");
+    if (path == 2) {
+        if (!gemv_ok)
+            return fail(ctx, LX2V_ERR_UNSUPPORTED,
+                        "the few-token kernel takes 1..16 rows, K a multiple of 64 (Q4: 128) and Q4 groups of 32+");
+        lx2v_status s = ensure_gemv_workspace(ctx, (int)N);
+        if (s) return s;
+        CUDA_TRY(ctx, linear_gemv_launch(a, ctx->num_sms, ctx->stream, ctx->gemv_ws, ctx->gemv_arrivals,
+                                         ctx->gemv_ws_floats));
+        ctx->launches++;
+        return LX2V_OK;
+    }
 
     if (path == 1 || path == 4) {
         const bool pair = path == 4;
@@ -733,16 +781,6 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         ctx->launches++;
         return LX2V_OK;
     }
-    LinearArgs a;
-    memset(&a, 0, sizeof a);
-    a.fmt = w->fmt; a.codes = (const uint8_t *)w->codes; a.scales_t = w->scales_t; a.sz_t = w->sz_t;
-    a.flags = w->flags;
-    a.M = (int)rows; a.N = (int)N; a.K = (int)K; a.group = (int)w->group;
-    a.x = x->ptr; a.x_f32 = x->dtype == LX2V_F32; a.x_row = (int64_t)x_row;
-    a.y = y->ptr; a.y_f32 = y->dtype == LX2V_F32; a.y_row = (int64_t)y_row;
-    a.bias = bias ? bias->ptr : nullptr; a.bias_f32 = bias && bias->dtype == LX2V_F32;
-    a.gate = gate_ptr; a.gate_f32 = mods && mods->dtype == LX2V_F32;
-    a.act = act;
     CUDA_TRY(ctx, linear_simt_launch(a, ctx->stream));
     ctx->launches++;
     return LX2V_OK;

@@ -478,3 +478,47 @@ def test_stream_k_gated_residual_with_offsets(be, oracle):
     lin = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, x_row=40 + int(r), threads=8)[0] for r in rows])
     want = oracle.gate_residual(h0[7:][rows].copy(), lin, len(rows), N, mods, 5)
     assert rel_l2(got[7:][rows] - h0[7:][rows], want - h0[7:][rows]) <= REL_L2
+
+
+# ---- few-token kernel (M <= 16, bandwidth-bound) --------------------------------------------
+@pytest.mark.parametrize("fmt", ["fp8", "q8", "q4", "native"])
+@pytest.mark.parametrize("M,N,K", [(1, 8960, 1536), (16, 1536, 8960), (7, 640, 4096), (3, 200, 256), (16, 4608, 1536)])
+def test_few_token_kernel_matches_generic_and_oracle(be, oracle, fmt, M, N, K):
+    w, q = make_weight(fmt, N, K, seed=121 + N, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    x = oracle.normal(122, (M + 2) * K)
+    b = oracle.normal(123, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b)
+    outs = {}
+    try:
+        for path in (2, 3):
+            be.set_linear_path(path)
+            for rep in range(2):  # split-K arrival counters must be back at zero
+                yb = be.alloc((M + 1) * N, F32)
+                be.linear(xb, 2, M, dw, bb, Act.GELU_TANH, yb, 1)
+                outs[(path, rep)] = be.download(yb).reshape(M + 1, N)
+    finally:
+        be.set_linear_path(0)
+    assert np.all(outs[(2, 0)][0] == 0)
+    assert np.array_equal(outs[(2, 0)], outs[(2, 1)], equal_nan=True)
+    assert rel_l2(outs[(2, 0)][1:], outs[(3, 0)][1:]) <= 1e-5
+    want = oracle.linear(x, M, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=1, x_row=2, threads=8)
+    assert rel_l2(outs[(2, 0)][1:], want) <= REL_L2
+
+
+def test_few_token_kernel_is_the_automatic_choice_and_fuses_the_gate(be, oracle):
+    M, N, K = 4, 1536, 8960
+    w, q = make_weight("q4", N, K, seed=131, oracle=oracle)
+    dw = be.weight_q4(q)
+    x = oracle.normal(132, M * K)
+    h0 = oracle.normal(133, M * N)
+    mods = oracle.normal(134, 6 * N, 0.5)
+    xb, mb = be.upload(x), be.upload(mods, F32)
+    hb = be.upload(h0, F32)
+    n0 = be.launch_count()
+    be.linear_gate_residual(xb, 0, M, dw, None, Act.NONE, hb, 0, mb, 5)
+    assert be.launch_count() == n0 + 1
+    got = be.download(hb).reshape(M, N)
+    lin = oracle.linear(x, M, oracle_dequant(oracle, "q4", q, None), N, K, threads=8)
+    want = oracle.gate_residual(h0.reshape(M, N).copy(), lin, M, N, mods, 5)
+    assert rel_l2(got - h0.reshape(M, N), want - h0.reshape(M, N)) <= REL_L2
