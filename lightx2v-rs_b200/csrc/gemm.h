@@ -64,11 +64,11 @@ struct LinearArgs {
 };
 cudaError_t linear_simt_launch(const LinearArgs &a, cudaStream_t st);
 // Few-token (M <= 16) bandwidth-bound kernel (gemv.cu). Split-K partials go
-// to `partials` (gemv_workspace_floats(N, num_sms) floats) and `arrivals`
+// to `partials` (gemv_workspace_floats(N, K, num_sms) floats) and `arrivals`
 // (ceil(N / 64) ints, zero before the first launch; the kernel leaves them
 // zero).
 bool gemv_supported(const LinearArgs &a);
-size_t gemv_workspace_floats(int N, int num_sms);
+size_t gemv_workspace_floats(int N, int K, int num_sms);
 cudaError_t linear_gemv_launch(const LinearArgs &a, int num_sms, cudaStream_t st, float *partials, int *arrivals,
                                size_t ws_floats);
 

@@ -57,56 +57,62 @@ __device__ __forceinline__ float ld_elem(const void *p, int f32, int64_t i) {
     return f32 ? reinterpret_cast<const float *>(p)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
 }
 
-// Raw codes of one thread for one chunk (16 bytes; 32 for bf16 weights).
+// Everything one thread reads from HBM for one chunk: its codes (16 bytes;
+// 32 for bf16 weights), the scale word of their group and, for FP8, the
+// block flag. All of it is loaded up front so every load of the thread's
+// k-range is in flight at once.
 template <int FMT>
-struct GvRaw {
+struct GvChunk {
     uint4 a, b;
+    uint32_t side;  // f32 scale (Q8/FP8) or half2 (scale, zero) (Q4)
+    uint32_t mode;  // FP8 block flag
 };
 
 template <int FMT>
-__device__ __forceinline__ GvRaw<FMT> gv_load(const LinearArgs &a, int n, int k) {
-    GvRaw<FMT> r;
+__device__ __forceinline__ void gv_load(const LinearArgs &a, int n, int k, GvChunk<FMT> &r) {
     r.a = make_uint4(0, 0, 0, 0);
     r.b = make_uint4(0, 0, 0, 0);
-    if (n >= a.N) return r;
+    r.side = 0;
+    r.mode = 0;
+    if (n >= a.N) return;
     if (FMT == FMT_Q4) {
         r.a = __ldg(reinterpret_cast<const uint4 *>(a.codes + ((int64_t)n * a.K + k) / 2));
+        r.side = __ldg(a.sz_t + (int64_t)(k / a.group) * a.N + n);
     } else if (FMT == FMT_BF16) {
         const uint4 *p = reinterpret_cast<const uint4 *>(a.codes + ((int64_t)n * a.K + k) * 2);
         r.a = __ldg(p);
         r.b = __ldg(p + 1);
     } else {
         r.a = __ldg(reinterpret_cast<const uint4 *>(a.codes + (int64_t)n * a.K + k));
+        r.side = __float_as_uint(__ldg(a.scales_t + (int64_t)(k / a.group) * a.N + n));
+        if (FMT == FMT_FP8) r.mode = __ldg(a.flags + (int64_t)(k / 32) * a.N + n);
     }
-    return r;
 }
 
-// Decode one thread's chunk (values k .. k + VT of row n) to bf16 pairs:
-// out[8u + i] = values (16u + 2i, 16u + 2i + 1).
+// Decode one thread's chunk to bf16 pairs: out[8u + i] = values
+// (16u + 2i, 16u + 2i + 1). A thread's chunk never straddles a scale group
+// or an FP8 flag block (gemv_supported).
 template <int FMT>
-__device__ __forceinline__ void gv_decode(const LinearArgs &a, int n, int k, const GvRaw<FMT> &raw,
-                                          uint32_t (&out)[8 * GvFmt<FMT>::UNITS]) {
-    const int nn = n < a.N ? n : a.N - 1;  // rows past N decode zeros from zero codes
+__device__ __forceinline__ void gv_decode(const GvChunk<FMT> &r, uint32_t (&out)[8 * GvFmt<FMT>::UNITS]) {
 #pragma unroll
     for (int u = 0; u < GvFmt<FMT>::UNITS; ++u) {
-        const int ku = k + 16 * u;
         uint32_t o[8];
         if (FMT == FMT_BF16) {
-            unit_to_bf16<FMT_BF16>(raw.a, raw.b, 0.0f, 0.0f, 0, o);
+            unit_to_bf16<FMT_BF16>(r.a, r.b, 0.0f, 0.0f, 0, o);
         } else if (FMT == FMT_Q4) {
-            float s, z;
-            q4_scale_zero(__ldg(a.sz_t + (int64_t)(ku / a.group) * a.N + nn), s, z);
-            const uint4 r4 = u == 0 ? make_uint4(raw.a.x, raw.a.y, 0, 0) : make_uint4(raw.a.z, raw.a.w, 0, 0);
-            unit_to_bf16<FMT_Q4>(r4, r4, s, z, 0, o);
+            float sc, z;
+            q4_scale_zero(r.side, sc, z);
+            const uint4 r4 = u == 0 ? make_uint4(r.a.x, r.a.y, 0, 0) : make_uint4(r.a.z, r.a.w, 0, 0);
+            unit_to_bf16<FMT_Q4>(r4, r4, sc, z, 0, o);
         } else {
-            const float s = __ldg(a.scales_t + (int64_t)(ku / a.group) * a.N + nn);
-            const int mode = FMT == FMT_FP8 ? (int)__ldg(a.flags + (int64_t)(ku / 32) * a.N + nn) : 0;
-            unit_to_bf16<FMT>(raw.a, raw.a, s, 0.0f, mode, o);
+            unit_to_bf16<FMT>(r.a, r.a, __uint_as_float(r.side), 0.0f, (int)r.mode, o);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) out[8 * u + i] = o[i];
     }
 }
+
+constexpr int GV_MAXCH = 8;  // chunks per thread (its whole k-range, loaded at once)
 
 template <int FMT>
 __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int splits, int kchunks_per_split,
@@ -116,41 +122,54 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int spli
     const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
     const int n_chunks = a.K / F::KC;
     const int c_begin = split * kchunks_per_split;
-    const int c_end = min(n_chunks, c_begin + kchunks_per_split);
+    const int nch = min(n_chunks - c_begin, kchunks_per_split);  // <= GV_MAXCH
     const int k_begin = c_begin * F::KC;
-    const int kext = max(0, (c_end - c_begin) * F::KC);
-    // x rows (16, zero beyond M) of this k-range, bf16, row stride kext + 8
-    const int xs_stride = kext + 8;
-    __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(gv_smem);
-    for (int e = threadIdx.x; e < 16 * (kext / 2); e += GV_THREADS) {
-        const int r = e / (kext / 2), kk = 2 * (e % (kext / 2));
-        float v0 = 0.0f, v1 = 0.0f;
-        if (r < a.M) {
-            const int64_t base = ((int64_t)a.x_row + r) * a.K + k_begin + kk;
-            v0 = ld_elem(a.x, a.x_f32, base);
-            v1 = ld_elem(a.x, a.x_f32, base + 1);
-        }
-        *reinterpret_cast<__nv_bfloat162 *>(xs + r * xs_stride + kk) = __floats2bfloat162_rn(v0, v1);
-    }
-    __syncthreads();
+    const int kext = nch * F::KC;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const int n_warp = tile * GV_ROWS + warp * 8;  // first of this warp's 8 rows
     const int n = n_warp + g;                      // this thread's B row
+
+    // 1. issue every weight load of this thread's k-range
+    GvChunk<FMT> ck[GV_MAXCH];
+#pragma unroll
+    for (int j = 0; j < GV_MAXCH; ++j)
+        if (j < nch) gv_load<FMT>(a, n, k_begin + j * F::KC + c * F::VT, ck[j]);
+
+    // 2. meanwhile stage x rows (16, zero beyond M) of the k-range as bf16,
+    //    row stride kext + 8, 8 values per thread and step
+    const int xs_stride = kext + 8;
+    __nv_bfloat16 *xs = reinterpret_cast<__nv_bfloat16 *>(gv_smem);
+    const int per_row = kext / 8;
+    for (int e = threadIdx.x; e < 16 * per_row; e += GV_THREADS) {
+        const int r = e / per_row, kk = 8 * (e - r * per_row);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < a.M) {
+            const int64_t base = ((int64_t)a.x_row + r) * a.K + k_begin + kk;
+            if (a.x_f32) {
+                const float4 f0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + base);
+                const float4 f1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + base + 4);
+                v.x = pack_bf16x2(f0.x, f0.y); v.y = pack_bf16x2(f0.z, f0.w);
+                v.z = pack_bf16x2(f1.x, f1.y); v.w = pack_bf16x2(f1.z, f1.w);
+            } else {
+                v = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(a.x) + base);
+            }
+        }
+        *reinterpret_cast<uint4 *>(xs + r * xs_stride + kk) = v;
+    }
+    __syncthreads();
+
+    // 3. decode and multiply, chunk by chunk
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const uint32_t xrow0 = (uint32_t)__cvta_generic_to_shared(xs + g * xs_stride);
     const uint32_t xrow1 = (uint32_t)__cvta_generic_to_shared(xs + (g + 8) * xs_stride);
-
-    // two chunks of codes in flight per thread
-    GvRaw<FMT> cur = gv_load<FMT>(a, n, k_begin + c * F::VT);
-    for (int ch = c_begin; ch < c_end; ++ch) {
-        const int kc = ch * F::KC;
-        GvRaw<FMT> nxt = cur;
-        if (ch + 1 < c_end) nxt = gv_load<FMT>(a, n, kc + F::KC + c * F::VT);
+#pragma unroll
+    for (int j = 0; j < GV_MAXCH; ++j) {
+        if (j >= nch) break;
         uint32_t w[8 * F::UNITS];
-        gv_decode<FMT>(a, n, kc + c * F::VT, cur, w);
-        const uint32_t xoff = (uint32_t)((kc - k_begin + c * F::VT) * 2);
+        gv_decode<FMT>(ck[j], w);
+        const uint32_t xoff = (uint32_t)((j * F::KC + c * F::VT) * 2);
 #pragma unroll
         for (int s = 0; s < F::STEPS; ++s) {
             uint32_t x00, x01, x10, x11;
@@ -158,7 +177,6 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int spli
             asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(x10), "=r"(x11) : "r"(xrow1 + xoff + 8 * s));
             mma_bf16_16816(d, x00, x10, x01, x11, w[2 * s], w[2 * s + 1]);
         }
-        cur = nxt;
     }
 
     // C fragment: d0, d1 = token g, rows n_warp + 2c, +1; d2, d3 = token g + 8.
@@ -211,15 +229,14 @@ cudaError_t gemv_launch_t(const LinearArgs &a, int num_sms, float *partials, int
     using F = GvFmt<FMT>;
     const int tiles = (a.N + GV_ROWS - 1) / GV_ROWS;
     const int n_chunks = a.K / F::KC;
-    // aim for two CTAs per SM, each split at least 4 chunks long
-    int splits = (2 * num_sms + tiles - 1) / tiles;
-    splits = splits < 1 ? 1 : splits;
-    splits = splits > n_chunks / 4 ? (n_chunks / 4 > 0 ? n_chunks / 4 : 1) : splits;
-    if ((size_t)tiles * splits * 16 * GV_ROWS > ws_floats) splits = 1;
+    // every split at most GV_MAXCH chunks (a thread loads its whole range at
+    // once); more splits only while the GPU has fewer than two CTAs per SM
+    int splits = (n_chunks + GV_MAXCH - 1) / GV_MAXCH;
+    while (tiles * splits < 2 * num_sms && n_chunks / (splits + 1) >= 2) ++splits;
     const int per = (n_chunks + splits - 1) / splits;
     splits = (n_chunks + per - 1) / per;
+    if (splits > 1 && (size_t)tiles * splits * 16 * GV_ROWS > ws_floats) return cudaErrorInvalidValue;
     const size_t smem = (size_t)16 * (per * F::KC + 8) * 2;
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;  // workspace too small to split K
     auto kern = gemv_kernel<FMT>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -241,11 +258,15 @@ bool gemv_supported(const LinearArgs &a) {
     }
 }
 
-// partials: at least gemv_workspace_floats(N, num_sms) floats; arrivals:
+// partials: at least gemv_workspace_floats(N, K, num_sms) floats; arrivals:
 // ceil(N / 64) ints, zero before the first launch (kernels leave them zero).
-size_t gemv_workspace_floats(int N, int num_sms) {
+size_t gemv_workspace_floats(int N, int K, int num_sms) {
+    // the largest split count gemv_launch_t picks for this shape (Q8/FP8/bf16
+    // chunks are the narrowest, so they need the most splits)
     const int tiles = (N + GV_ROWS - 1) / GV_ROWS;
-    const int splits = (2 * num_sms + tiles - 1) / tiles;
+    const int n_chunks = K / 64;
+    int splits = (n_chunks + GV_MAXCH - 1) / GV_MAXCH;
+    while (tiles * splits < 2 * num_sms && n_chunks / (splits + 1) >= 2) ++splits;
     return (size_t)tiles * (splits < 1 ? 1 : splits) * 16 * GV_ROWS;
 }
 

@@ -174,8 +174,8 @@ static lx2v_status ensure_sk_workspace(lx2v_ctx *ctx, int pairs, int bt, float *
 
 // Few-token kernel workspace for an output width N: partial tiles, then one
 // arrival counter per 64-row tile (zeroed here; the kernel leaves them zero).
-static lx2v_status ensure_gemv_workspace(lx2v_ctx *ctx, int N) {
-    const size_t floats = gemv_workspace_floats(N, ctx->num_sms);
+static lx2v_status ensure_gemv_workspace(lx2v_ctx *ctx, int N, int K) {
+    const size_t floats = gemv_workspace_floats(N, K, ctx->num_sms);
     const size_t tiles = (size_t)(N + 63) / 64;
     if (ctx->gemv_ws_floats >= floats && ctx->gemv_tiles >= tiles) return LX2V_OK;
     if (ctx->gemv_ws) {
@@ -709,7 +709,7 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         if (!gemv_ok)
             return fail(ctx, LX2V_ERR_UNSUPPORTED,
                         "the few-token kernel takes 1..16 rows, K a multiple of 64 (Q4: 128) and Q4 groups of 32+");
-        lx2v_status s = ensure_gemv_workspace(ctx, (int)N);
+        lx2v_status s = ensure_gemv_workspace(ctx, (int)N, (int)K);
         if (s) return s;
         CUDA_TRY(ctx, linear_gemv_launch(a, ctx->num_sms, ctx->stream, ctx->gemv_ws, ctx->gemv_arrivals,
                                          ctx->gemv_ws_floats));
