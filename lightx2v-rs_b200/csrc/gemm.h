@@ -36,6 +36,7 @@ struct alignas(64) GemmParams {
     // those partials in its epilogue.
     int streamk;
     int epoch;
+    int kgroup;               // pair kernel: k-blocks per MMA group (1, or 2 when K % 128 == 0)
     float *partials;
     int *flags;
 };

@@ -92,7 +92,7 @@ struct PairWork {
     }
 };
 
-template <int FMT, int BT, int ACC, int SS, int AS, int DQW, bool SK>
+template <int FMT, int BT, int ACC, int SS, int AS, int DQW, bool SK, int GRP>
 __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
     static_assert(SS >= AS, "an A stage is released through the x ring");
@@ -106,6 +106,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     // With equal ring depths one barrier per stage carries both the x bytes
     // and the dequant arrivals, so the MMA thread waits once per k-block.
     constexpr bool MERGED = SS == AS;
+    // GRP k-blocks form one MMA group: one ready wait and one commit per
+    // group (the MMA thread's barrier round trips are what bounds the k-loop
+    // on B200); data stays in 64-wide k-block stages.
+    static_assert(GRP == 1 || (MERGED && SS % GRP == 0), "k-block groups need merged rings");
+    constexpr int NG = SS / GRP;  // group slots of xb_full / x_empty
     uint64_t *a_full_sep = x_empty + SS;     // [AS]  leader: dequant warps of both CTAs (unmerged rings)
     uint64_t *a_full = MERGED ? xb_full : a_full_sep;
     uint64_t *acc_full = a_full_sep + AS;   // [ACC] multicast commit
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     const int n_mt = (p.M + BT - 1) / BT;
     const int n_ft = (p.N + 255) / 256;
     const int n_tiles = n_mt * n_ft;
-    const int KB = (p.K + BK - 1) / BK;
+    const int KB = ((p.K + BK - 1) / BK) / GRP;  // groups per tile (the host keeps K a multiple of GRP k-blocks)
     PairWork work;
     work.KB = KB;
     work.pair = pair;
@@ -131,14 +136,15 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     work.lo = units * pair / npairs;
     work.hi = units * (pair + 1) / npairs;
     const int n_seg = work.count();
-    const int total_kb = (int)work.total_kb();  // k-blocks this pair runs, over all its segments
+    const int total_gr = (int)work.total_kb();   // groups this pair runs, over all its segments
+    const int total_kb = total_gr * GRP;          // k-blocks
     int *err = p.err;
     const uint64_t lim = p.wait_limit_ns;
     const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SS; ++s) {
-            mbar_init(&xb_full[s], MERGED ? 9 : 1);
+            mbar_init(&xb_full[s], MERGED ? 1 + 8 * GRP : 1);
             mbar_init(&w_full[s], 1);
             mbar_init(&x_empty[s], 1);
         }
@@ -164,11 +170,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
-            int last_phase[SS];
-            for (int s = 0; s < SS; ++s) last_phase[s] = -1;
+            int last_phase[NG];
+            for (int s = 0; s < NG; ++s) last_phase[s] = -1;
             const int wk_div = FMT == FMT_Q4 ? 2 : 1;
             const uint32_t w_tx = C::W_BYTES + (FMT != FMT_BF16 ? 128 * 4 * p.sgrp : 0) + C::F_BYTES;
-            Ring xs;
+            Ring gs;  // group slot
             bool ok = true;
             for (int j = 0; j < n_seg && ok; ++j) {
                 int tile, kb0, kb1;
@@ -176,28 +182,34 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 const int mt = tile % n_mt, ft = tile / n_mt;
                 const int row0 = ft * 256 + (int)rank * 128;
                 const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait_cluster_bounded(&x_empty[xs.s], xs.ph ^ 1, err, lim)) { ok = false; break; }
-                    if (lead) mbar_arrive_expect_tx(&xb_full[xs.s], 2 * C::XH_BYTES);
-                    mbar_arrive_expect_tx(&w_full[xs.s], w_tx);
-                    tma_load_2d_pair(smem + xs.s * C::XH_BYTES, &p.tmap_x, mapa_shared(smem_u32(&xb_full[xs.s]), 0),
-                                     kb * BK, xrow);
-                    tma_load_2d(smem + C::OFF_W + xs.s * C::W_BYTES, &p.tmap_w, &w_full[xs.s], kb * BK / wk_div, row0);
-                    if (FMT != FMT_BF16)
-                        tma_load_2d(smem + C::OFF_S + xs.s * C::S_BYTES, &p.tmap_s, &w_full[xs.s], row0,
-                                    (kb * BK) / p.group);
-                    if (FMT == FMT_FP8)
-                        tma_load_2d(smem + C::OFF_F + xs.s * C::F_BYTES, &p.tmap_f, &w_full[xs.s], row0, kb * 2);
-                    last_phase[xs.s] = xs.ph;
-                    xs.next<SS>();
+                for (int gr = kb0; gr < kb1; ++gr) {
+                    if (!mbar_wait_cluster_bounded(&x_empty[gs.s], gs.ph ^ 1, err, lim)) { ok = false; break; }
+                    if (lead) mbar_arrive_expect_tx(&xb_full[gs.s], GRP * 2 * C::XH_BYTES);
+                    const uint32_t xbar = mapa_shared(smem_u32(&xb_full[gs.s]), 0);
+#pragma unroll
+                    for (int h = 0; h < GRP; ++h) {
+                        const int kb = gr * GRP + h;
+                        const int s = gs.s * GRP + h;  // data stage slot
+                        mbar_arrive_expect_tx(&w_full[s], w_tx);
+                        tma_load_2d_pair(smem + s * C::XH_BYTES, &p.tmap_x, xbar, kb * BK, xrow);
+                        tma_load_2d(smem + C::OFF_W + s * C::W_BYTES, &p.tmap_w, &w_full[s], kb * BK / wk_div, row0);
+                        if (FMT != FMT_BF16)
+                            tma_load_2d(smem + C::OFF_S + s * C::S_BYTES, &p.tmap_s, &w_full[s], row0,
+                                        (kb * BK) / p.group);
+                        if (FMT == FMT_FP8)
+                            tma_load_2d(smem + C::OFF_F + s * C::F_BYTES, &p.tmap_f, &w_full[s], row0, kb * 2);
+                    }
+                    last_phase[gs.s] = gs.ph;
+                    gs.next<NG>();
                 }
             }
-            // Drain: a stage's loads have landed once its own codes arrived and
-            // the leader's MMA released it (x halves are counted on the leader).
-            for (int s = 0; s < SS; ++s)
-                if (last_phase[s] >= 0) {
-                    mbar_wait_bounded(&w_full[s], (uint32_t)last_phase[s], nullptr, drain_lim);
-                    mbar_wait_cluster_bounded(&x_empty[s], (uint32_t)last_phase[s], nullptr, drain_lim);
+            // Drain: a group's loads have landed once its codes arrived and the
+            // leader's MMA released it (x halves are counted on the leader).
+            for (int g2 = 0; g2 < NG; ++g2)
+                if (last_phase[g2] >= 0) {
+                    for (int h = 0; h < GRP; ++h)
+                        mbar_wait_bounded(&w_full[g2 * GRP + h], (uint32_t)last_phase[g2], nullptr, drain_lim);
+                    mbar_wait_cluster_bounded(&x_empty[g2], (uint32_t)last_phase[g2], nullptr, drain_lim);
                 }
         }
         __syncwarp();
@@ -210,10 +222,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         if (lane == 0 && lead) {
             const uint32_t idesc = idesc_bf16_f32(256, BT);
             bool ok = true;
-            Ring xs, as, ab;
+            Ring xs, as, ab;  // xs: group slot (NG), as: A stage (AS, per k-block)
             bool x_ready = total_kb > 0 && mbar_wait_cluster_bounded(&xb_full[0], 0, err, lim);
             bool a_ready = x_ready && (MERGED || mbar_wait_cluster_bounded(&a_full[0], 0, err, lim));
-            ok = total_kb == 0 || (x_ready && a_ready);
+            ok = total_gr == 0 || (x_ready && a_ready);
             int i = 0;
             for (int j = 0; j < n_seg && ok; ++j) {
                 int tile, kb0, kb1;
@@ -228,16 +240,19 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
-                    const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + xs.s * C::XH_BYTES));
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc,
-                                        (kb != kb0 || kk != 0) ? 1u : 0u);
+                    for (int h = 0; h < GRP; ++h) {
+                        const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL0 + as.s * (BK / 2));
+                        const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + (xs.s * GRP + h) * C::XH_BYTES));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            mma_ts_f16_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc,
+                                            (kb != kb0 || h != 0 || kk != 0) ? 1u : 0u);
+                        as.next<AS>();
+                    }
                     mma_commit_pair(&x_empty[xs.s], 0x3);
                     if (kb == kb1 - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
-                    xs.next<SS>();
-                    as.next<AS>();
+                    xs.next<NG>();
                 }
                 if (!ok) break;
                 ab.next<ACC>();
@@ -317,8 +332,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             if (lane == 0) {
                 w = mbar_wait_bounded(&w_full[s], ph, err, lim) ? 1 : 0;
                 if (w && i >= AS) {
-                    const int e = i - AS;
-                    w = mbar_wait_cluster_bounded(&x_empty[e % SS], (uint32_t)(e / SS) & 1u, err, lim) ? 1 : 0;
+                    const int e = (i - AS) / GRP;  // the group whose MMAs free this A stage
+                    w = mbar_wait_cluster_bounded(&x_empty[e % NG], (uint32_t)(e / NG) & 1u, err, lim) ? 1 : 0;
                 }
             }
             w = __shfl_sync(0xFFFFFFFFu, w, 0);
@@ -337,7 +352,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[a]), 0));
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[MERGED ? (i / GRP) % NG : a]), 0));
         }
     }
 
@@ -362,10 +377,10 @@ constexpr int pair_stages(int fmt, int bt) {
     return n - n % 4;
 }
 
-template <int FMT, int BT, int ACC, int SS, int AS, bool SK, int DQW = 4>
+template <int FMT, int BT, int ACC, int SS, int AS, bool SK, int GRP, int DQW = 4>
 static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
-    auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW, SK>;
+    auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW, SK, GRP>;
     constexpr int PAIR_THREADS = 32 * (8 + 4 * DQW);
     static int max_pairs = 0;
     const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
@@ -393,7 +408,7 @@ static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
     // stream-K: every pair gets at least one k-block (the host checked
     // n_tiles * KB >= pairs)
-    const long long work = SK ? (long long)n_tiles * ((p.K + BK - 1) / BK) : n_tiles;
+    const long long work = SK ? (long long)n_tiles * (((p.K + BK - 1) / BK) / GRP) : n_tiles;
     const int pairs = work < max_pairs ? (int)work : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     return cudaLaunchKernelEx(&cfg, kern, p);
@@ -401,8 +416,13 @@ static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t
 
 template <int FMT, int BT, int ACC, int SS, int AS>
 static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
-    return p.streamk ? pair_launch_sk<FMT, BT, ACC, SS, AS, true>(p, num_sms, st)
-                     : pair_launch_sk<FMT, BT, ACC, SS, AS, false>(p, num_sms, st);
+    if constexpr (SS == AS && SS % 2 == 0) {
+        if (p.kgroup == 2)
+            return p.streamk ? pair_launch_sk<FMT, BT, ACC, SS, AS, true, 2>(p, num_sms, st)
+                             : pair_launch_sk<FMT, BT, ACC, SS, AS, false, 2>(p, num_sms, st);
+    }
+    return p.streamk ? pair_launch_sk<FMT, BT, ACC, SS, AS, true, 1>(p, num_sms, st)
+                     : pair_launch_sk<FMT, BT, ACC, SS, AS, false, 1>(p, num_sms, st);
 }
 
 template <int FMT>

@@ -768,6 +768,7 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         p.act = act;
         p.out_f32 = y->dtype == LX2V_F32;
         p.reduce = mods ? 1 : 0;
+        p.kgroup = K % 128 == 0 ? 2 : 1;
         if (pair && use_streamk(ctx, (int)rows, (int)N, (int)K, bt)) {
             const int pairs = ctx->num_sms / 2;
             s = ensure_sk_workspace(ctx, pairs, bt, &p.partials, &p.flags);
