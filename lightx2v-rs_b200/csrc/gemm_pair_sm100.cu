@@ -109,8 +109,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     // GRP k-blocks form one MMA group: one ready wait and one commit per
     // group (the MMA thread's barrier round trips are what bounds the k-loop
     // on B200); data stays in 64-wide k-block stages.
-    static_assert(GRP == 1 || (MERGED && SS % GRP == 0), "k-block groups need merged rings");
-    constexpr int NG = SS / GRP;  // group slots of xb_full / x_empty
+    static_assert(SS % GRP == 0 && AS % GRP == 0, "k-block groups tile both rings");
+    constexpr int NG = SS / GRP;   // group slots of xb_full / x_empty
+    constexpr int NGA = AS / GRP;  // group slots of a_full (unmerged rings)
     uint64_t *a_full_sep = x_empty + SS;     // [AS]  leader: dequant warps of both CTAs (unmerged rings)
     uint64_t *a_full = MERGED ? xb_full : a_full_sep;
     uint64_t *acc_full = a_full_sep + AS;   // [ACC] multicast commit
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             mbar_init(&x_empty[s], 1);
         }
         if (!MERGED)
-            for (int s = 0; s < AS; ++s) mbar_init(&a_full[s], 8);
+            for (int s = 0; s < AS; ++s) mbar_init(&a_full[s], 8 * GRP);
         for (int b = 0; b < ACC; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 8);
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         if (lane == 0 && lead) {
             const uint32_t idesc = idesc_bf16_f32(256, BT);
             bool ok = true;
-            Ring xs, as, ab;  // xs: group slot (NG), as: A stage (AS, per k-block)
+            Ring xs, as, ab, ag;  // xs: group slot (NG), as: A stage (AS, per k-block), ag: A group slot (NGA)
             bool x_ready = total_kb > 0 && mbar_wait_cluster_bounded(&xb_full[0], 0, err, lim);
             bool a_ready = x_ready && (MERGED || mbar_wait_cluster_bounded(&a_full[0], 0, err, lim));
             ok = total_gr == 0 || (x_ready && a_ready);
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
                 for (int kb = kb0; kb < kb1; ++kb, ++i) {
                     if (i > 0 && (!mbar_wait_cluster_bounded(&xb_full[xs.s], xs.ph, err, lim) ||
-                                  (!MERGED && !mbar_wait_cluster_bounded(&a_full[as.s], as.ph, err, lim)))) {
+                                  (!MERGED && !mbar_wait_cluster_bounded(&a_full[ag.s], ag.ph, err, lim)))) {
                         ok = false;
                         break;
                     }
@@ -253,6 +254,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                     mma_commit_pair(&x_empty[xs.s], 0x3);
                     if (kb == kb1 - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
                     xs.next<NG>();
+                    ag.next<NGA>();
                 }
                 if (!ok) break;
                 ab.next<ACC>();
@@ -352,7 +354,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[MERGED ? (i / GRP) % NG : a]), 0));
+            if (lane == 0)
+                mbar_arrive_cluster(mapa_shared(smem_u32(&a_full[MERGED ? (i / GRP) % NG : (i / GRP) % NGA]), 0));
         }
     }
 
@@ -416,7 +419,7 @@ static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t
 
 template <int FMT, int BT, int ACC, int SS, int AS>
 static cudaError_t pair_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
-    if constexpr (SS == AS && SS % 2 == 0) {
+    if constexpr (SS % 2 == 0 && AS % 2 == 0) {
         if (p.kgroup == 2)
             return p.streamk ? pair_launch_sk<FMT, BT, ACC, SS, AS, true, 2>(p, num_sms, st)
                              : pair_launch_sk<FMT, BT, ACC, SS, AS, false, 2>(p, num_sms, st);
