@@ -13,9 +13,12 @@
 namespace lx2v {
 
 constexpr int BK = 64;          // k columns per pipeline stage
-constexpr int STG_ROWS = 16;    // tokens per epilogue staging chunk
-constexpr int STG_COLS = 128;   // features per staging chunk (one CTA's rows)
-constexpr int STG_BYTES = STG_ROWS * STG_COLS * 4;
+// Epilogue staging: one [32 tokens][32 features] f32 tile per epilogue warp,
+// rows padded to 36 floats (column writes and 16-byte row reads both run at
+// the minimum number of shared-memory wavefronts).
+constexpr int STG_PITCH = 36;
+constexpr int STG_WARP_FLOATS = 32 * STG_PITCH;
+constexpr int STG_TOTAL = 4 * STG_WARP_FLOATS * 4;  // bytes, four epilogue warps
 constexpr int EPI_THREADS = 128;
 constexpr int TMEM_COLS = 512;
 
@@ -123,21 +126,19 @@ struct PartialIO {
 // Epilogue of one accumulator tile held in this CTA's TMEM: 128 features
 // (lanes; this thread = feature f_base + 32*q + lane) x `ntok` tokens
 // (columns from `acc_addr`, tokens m0 .. m0 + ntok). Bias, GELU and gate are
-// applied in f32; rows go through a [16 tokens][128 features] smem staging
-// tile to 16-byte coalesced global stores, or to vector reductions into h
-// for the gated residual. `release` runs once the last TMEM load of the tile
-// has completed (the accumulator can be reused from then on). Partial tiles
-// (`io`) are stored token-major, [token][128 features] f32, so a warp's
-// accesses for one token are 128 contiguous bytes.
+// applied in f32. Each warp transposes its 32 features x 32 tokens through
+// its own staging tile and then writes, per thread, one token's 32 features
+// (64 or 128 contiguous bytes of y) with 16-byte stores, or vector reductions
+// into h for the gated residual; warps never wait for each other. `release`
+// runs once the last TMEM load of the tile has completed (the accumulator can
+// be reused from then on). Partial tiles (`io`) are stored token-major,
+// [token][128 features] f32, so a warp's accesses for one token are 128
+// contiguous bytes.
 template <bool PARTIAL = false, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_addr, int ntok, int f_base,
-                                              int m0, int q, int lane, uint8_t *stg_base, int &chunk_ctr,
-                                              Release release, const PartialIO &io = PartialIO()) {
+                                              int m0, int q, int lane, uint8_t *stg_base, Release release,
+                                              const PartialIO &io = PartialIO()) {
     const int et = q * 32 + lane;  // 0..127
-    const bool out_f32 = p.out_f32 != 0;
-    const int esz = out_f32 ? 4 : 2;
-    const int row_bytes = STG_COLS * esz;
-    const int cpr = row_bytes / 16;  // 16-byte chunks per staged row
     const int f = f_base + et;
     float bias_f = 0.0f, gate_f = 1.0f;
     if (f < p.N) {
@@ -147,6 +148,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
                                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.gate)[f]);
     }
     const float2 bias2 = make_float2(bias_f, bias_f), gate2 = make_float2(gate_f, gate_f);
+    float *stg = reinterpret_cast<float *>(stg_base) + q * STG_WARP_FLOATS;
+    const int fw = f_base + 32 * q;  // first feature of this warp
+    const int nvalid = p.N - fw;     // this warp's features inside N (N % 16 == 0)
     const int nld = min(ntok / 32, (p.M - m0 + 31) / 32);
     for (int c = 0; c < nld; ++c) {
         uint32_t acc[32];
@@ -167,53 +171,46 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
                     acc[i] = __float_as_uint(__uint_as_float(acc[i]) + __ldcg(src + i * 128));
             }
         }
-        float2 v[16];
+        __syncwarp();  // the previous chunk's rows have been read
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             float2 t = __fadd2_rn(make_float2(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1])), bias2);
             if (p.act == 1) t = gelu2(t);
-            v[i] = p.gate ? __fmul2_rn(t, gate2) : t;
+            if (p.gate) t = __fmul2_rn(t, gate2);
+            stg[(2 * i) * STG_PITCH + lane] = t.x;       // token 2i, feature lane
+            stg[(2 * i + 1) * STG_PITCH + lane] = t.y;
         }
+        __syncwarp();
+        const int token = m0 + c * 32 + lane;  // this thread now owns one token row
+        if (token >= p.M || nvalid <= 0) continue;
+        const float4 *row = reinterpret_cast<const float4 *>(stg + lane * STG_PITCH);
+        const int64_t yoff = ((int64_t)p.y_row + token) * p.N + fw;
+        if (p.out_f32) {
+            float *dst = reinterpret_cast<float *>(p.y) + yoff;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int row0 = m0 + c * 32 + h * STG_ROWS;
-            if (row0 >= p.M) break;
-            uint8_t *stg = stg_base + (chunk_ctr & 1) * STG_BYTES;
-            ++chunk_ctr;
-            if (out_f32) {
-                float *s32 = reinterpret_cast<float *>(stg) + et;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    s32[(2 * i) * STG_COLS] = v[h * 8 + i].x;
-                    s32[(2 * i + 1) * STG_COLS] = v[h * 8 + i].y;
-                }
-            } else {
-                unsigned short *s16 = reinterpret_cast<unsigned short *>(stg) + et;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t pk = pack_bf16x2(v[h * 8 + i]);
-                    s16[(2 * i) * STG_COLS] = (unsigned short)(pk & 0xFFFFu);
-                    s16[(2 * i + 1) * STG_COLS] = (unsigned short)(pk >> 16);
+            for (int j = 0; j < 8; ++j) {
+                if (4 * j >= nvalid) break;
+                const float4 v = row[j];
+                if (!p.reduce) {
+                    *reinterpret_cast<float4 *>(dst + 4 * j) = v;
+                } else {
+                    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j), "f"(v.x),
+                                 "f"(v.y), "f"(v.z), "f"(v.w)
+                                 : "memory");
                 }
             }
-            named_bar_sync(1, EPI_THREADS);
-            const int vals = 16 / esz;  // elements per 16-byte chunk
-            for (int id = et; id < STG_ROWS * cpr; id += EPI_THREADS) {
-                const int row = id / cpr, cc = id - row * cpr;
-                const int token = row0 + row;
-                const int f0 = f_base + cc * vals;
-                if (token >= p.M || f0 >= p.N) continue;
-                const uint4 u = *reinterpret_cast<const uint4 *>(stg + row * row_bytes + cc * 16);
-                char *dst = reinterpret_cast<char *>(p.y) + (((int64_t)p.y_row + token) * p.N + f0) * esz;
+        } else {
+            __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.y) + yoff;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (8 * j >= nvalid) break;
+                const float4 a = row[2 * j], b = row[2 * j + 1];
+                const uint4 u = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                                           pack_bf16x2(b.z, b.w));
                 if (!p.reduce) {
-                    *reinterpret_cast<uint4 *>(dst) = u;
-                } else if (out_f32) {
-                    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-                                 "f"(__uint_as_float(u.x)), "f"(__uint_as_float(u.y)),
-                                 "f"(__uint_as_float(u.z)), "f"(__uint_as_float(u.w))
-                                 : "memory");
+                    *reinterpret_cast<uint4 *>(dst + 8 * j) = u;
                 } else {
-                    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst + 8 * j),
                                  "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
                                  : "memory");
                 }

@@ -51,7 +51,7 @@ struct PairCfg {
     static constexpr int OFF_S = OFF_W + SS * W_BYTES;
     static constexpr int OFF_F = OFF_S + SS * S_BYTES;
     static constexpr int OFF_STG = (OFF_F + SS * F_BYTES + 127) & ~127;
-    static constexpr int OFF_BAR = OFF_STG + 2 * STG_BYTES;
+    static constexpr int OFF_BAR = OFF_STG + STG_TOTAL;
     static constexpr int NUM_BARS = 3 * SS + AS + 2 * ACC + 1;
     static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
     static_assert(XH_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "swizzle atoms");
@@ -267,7 +267,6 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
         // ---------------- epilogue (both CTAs) ----------------
         const int q = warp - 4;
         const bool leader_thread = threadIdx.x == 128;
-        int chunk_ctr = 0;
         Ring ab;
         const int64_t part_floats = (int64_t)128 * BT;  // one CTA's partial tile
         for (int j = 0; j < n_seg; ++j) {
@@ -303,7 +302,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
             const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
             epilogue_tile<SK>(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
-                          chunk_ctr, [&] {
+                          [&] {
                               tc_fence_before();
                               __syncwarp();
                               if (lane == 0) mbar_arrive_cluster(rel);
@@ -369,7 +368,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 
 constexpr int pair_stages(int fmt, int bt) {
-    const int budget = 227 * 1024 - 1024 - 2 * STG_BYTES - 512;
+    const int budget = 227 * 1024 - 1024 - STG_TOTAL - 512;
     const int w = 128 * (fmt == FMT_Q4 ? 32 : fmt == FMT_BF16 ? 128 : 64);
     const int side = fmt == FMT_Q4 ? 128 * 16 : fmt == FMT_BF16 ? 0 : 512 + (fmt == FMT_FP8 ? 256 : 0);
     const int stage = (bt / 2) * BK * 2 + w + side;

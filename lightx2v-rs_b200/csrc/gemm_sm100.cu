@@ -54,7 +54,7 @@ struct Cfg {
     static constexpr int OFF_S = OFF_W + SS * W_STAGE_BYTES;
     static constexpr int OFF_F = OFF_S + SS * S_STAGE_BYTES;
     static constexpr int OFF_STG = (OFF_F + SS * F_STAGE_BYTES + 127) & ~127;
-    static constexpr int OFF_BAR = OFF_STG + 2 * STG_BYTES;
+    static constexpr int OFF_BAR = OFF_STG + STG_TOTAL;
     static constexpr int NUM_BARS = 2 * SS + 2 * AS + 2 * ACC + 1;
     static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
     static_assert(X_STAGE_BYTES % 1024 == 0 && W_STAGE_BYTES % 1024 == 0, "swizzle atoms");
@@ -234,7 +234,6 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_dq_kernel(const __
         // ---------------- epilogue ----------------
         const int q = warp - 4;
         const bool leader = threadIdx.x == 128;
-        int chunk_ctr = 0;
         Ring ab;
         for (int j = 0; j < my_tiles; ++j) {
             const int tile = (int)blockIdx.x + j * (int)gridDim.x;
@@ -245,7 +244,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_dq_kernel(const __
             tc_fence_after();
             const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
             uint64_t *rel_bar = &acc_empty[ab.s];
-            epilogue_tile(p, acc_addr, BT, ft * 128, mt * BT, q, lane, smem + C::OFF_STG, chunk_ctr, [&] {
+            epilogue_tile(p, acc_addr, BT, ft * 128, mt * BT, q, lane, smem + C::OFF_STG, [&] {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(rel_bar);
@@ -286,7 +285,7 @@ static cudaError_t launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
 // Shared stages that fit next to the epilogue staging: each stage holds the
 // x tile (BT*128 B) and the code tile (4, 8 or 16 KB), at most 8 stages.
 constexpr int smem_stages(int fmt, int bt) {
-    const int budget = 227 * 1024 - 1024 - 2 * STG_ROWS * STG_COLS * 4 - 512;
+    const int budget = 227 * 1024 - 1024 - STG_TOTAL - 512;
     const int w = 128 * (fmt == FMT_Q4 ? 32 : fmt == FMT_BF16 ? 128 : 64);
     const int side = fmt == FMT_Q4 ? 128 * 16 : fmt == FMT_BF16 ? 0 : 512 + (fmt == FMT_FP8 ? 256 : 0);
     const int stage = bt * BK * 2 + w + side;
@@ -316,15 +315,15 @@ cudaError_t gemm_dq_launch(int fmt, int bt, const GemmParams &p, int num_sms, cu
 int gemm_dq_token_tile(int M, int N, int K, int units, int feat_tile) {
     // Wave model of the persistent grid: `units` CTAs (or CTA pairs) each run
     // whole tiles of feat_tile features x bt tokens, so a launch takes
-    // ceil(tiles / units) rounds of bt * K MMA columns. The 256-token tile
-    // has a single TMEM accumulator, so its epilogue is not hidden behind the
-    // next tile's k-loop; measured on B200 that costs about as much as 192
-    // more k-columns per tile. A 128-token tile moves more bytes per FLOP and
-    // pays the per-k-block handoffs on fewer columns: measured ~1.65x the
-    // time per column of the wider tiles. The cheapest tile wins; ties go to
-    // the wider tile. (FP8 set of the Wan2.1-1.3B chunk, M = 4680: QKV,
-    // FFN1 -> 192; out -> 256 (tie); FFN2 -> 256.)
+    // ceil(tiles / units) rounds of bt * (e * K + E) MMA-column time. Fitted on
+    // B200 (FP8 linears of the Wan2.1-1.3B chunk at K = 1536 and 8960): the
+    // 256-token tile has the cheapest k-loop (e = 1) but a single TMEM
+    // accumulator, so its epilogue is exposed (E = 1190 k-columns); 192 tokens
+    // keep two accumulators (E = 700) but pay the MMA thread's per-k-block
+    // round trips on fewer columns (e = 1.42); 128 tokens: e = 1.9, E = 800.
+    // Ties go to the wider tile. (M = 4680: QKV, out, FFN1, FFN2 -> 256.)
     const int cand[3] = {256, 192, 128};
+    const double e[3] = {1.0, 1.42, 1.9}, E[3] = {1190.0, 700.0, 800.0};
     int best = 128;
     double best_cost = 0.0;
     for (int c = 0; c < 3; ++c) {
@@ -332,7 +331,7 @@ int gemm_dq_token_tile(int M, int N, int K, int units, int feat_tile) {
         if (c > 0 && M < bt / 2) continue;
         const long long tiles = (long long)((M + bt - 1) / bt) * ((N + feat_tile - 1) / feat_tile);
         const long long waves = (tiles + units - 1) / units;
-        const double cost = (double)waves * bt * (K + (bt == 256 ? 192 : 0)) * (bt == 128 ? 1.65 : 1.0);
+        const double cost = (double)waves * bt * (e[c] * K + E[c]);
         if (c == 0 || cost < best_cost) {
             best = bt;
             best_cost = cost;
