@@ -210,6 +210,27 @@ __device__ __forceinline__ void q4_scale_zero(uint32_t sz, float &s, float &z) {
 // `raw` holds the unit's codes: 16 bytes (Q8/FP8), 8 bytes in .x/.y (Q4),
 // or 32 bytes of bf16 split over raw/raw2 (native).
 // fp8_mode: 0 fast, 1 fast + special-code fix-up, 2 reference formula.
+// The FP8 units of blocks that hold special codes or extreme scales (modes 1
+// and 2), out of line: they are rare, and keeping their code out of the
+// decode loop keeps that loop small for the instruction cache that the
+// kernel's other warps share.
+struct PackedUnit {
+    uint32_t w[8];
+};
+static __device__ __noinline__ PackedUnit fp8_unit_special(const uint4 raw, float s, int fp8_mode) {
+    float2 p[8];
+    if (fp8_mode == 1) {
+        fp8_products_hw(raw, s, p);
+        fp8_fixup(raw, p);
+    } else {
+        fp8_products_slow(raw, s, p);
+    }
+    PackedUnit u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u.w[i] = pack_bf16x2(p[i]);
+    return u;
+}
+
 template <int FMT>
 __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, float s, float z,
                                              int fp8_mode, uint32_t (&out)[8]) {
@@ -224,12 +245,13 @@ __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, 
     } else if (FMT == FMT_Q4) {
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
     } else {
-        if (fp8_mode != 2) {
-            fp8_products_hw(raw, s, p);
-            if (fp8_mode == 1) fp8_fixup(raw, p);
-        } else {
-            fp8_products_slow(raw, s, p);
+        if (fp8_mode != 0) {
+            const PackedUnit u = fp8_unit_special(raw, s, fp8_mode);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[i] = u.w[i];
+            return;
         }
+        fp8_products_hw(raw, s, p);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] = pack_bf16x2(p[i]);

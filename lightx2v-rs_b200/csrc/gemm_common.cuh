@@ -78,6 +78,11 @@ __device__ __forceinline__ uint2 lds64(const uint8_t *p) {
 // Scale-group index of a unit inside the stage's scale box: the box starts
 // at the k-block's first group; groups are >= 16 columns and either divide
 // 64 (p.gshift = log2(group)) or are multiples of 64 (p.gshift = 6).
+// FP8: every unit first takes the branch-free hardware-converter path; only
+// when some row of the warp has a flagged block (special codes or an extreme
+// scale, rare) are those rows' units decoded again on the exact slow path.
+// Keeping the common path free of per-unit branches lets the compiler overlap
+// the units' shared-memory loads.
 template <int FMT, int UNITS>
 __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t *wstage, const uint8_t *sstage,
                                              const uint8_t *fstage, int r, int u0, uint32_t (&packed)[8 * UNITS]) {
@@ -106,12 +111,30 @@ __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t 
                 // 64-byte rows, 64B swizzle: chunk ^= (row >> 1) & 3; a unit is one chunk
                 const uint4 raw = lds128(wt + ((ui ^ ((r >> 1) & 3)) << 4));
                 const float s = __uint_as_float(sw[r]);
-                const int mode = FMT == FMT_FP8 ? fstage[(ui >> 1) * 128 + r] : 0;
-                unit_to_bf16<FMT>(raw, raw, s, 0.0f, mode, o);
+                unit_to_bf16<FMT>(raw, raw, s, 0.0f, 0, o);
             }
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) out[i] = o[i];
+    }
+    if (FMT == FMT_FP8) {
+        int flagged = 0;
+#pragma unroll
+        for (int u = 0; u < UNITS; u += 2) flagged |= fstage[((u0 + u) >> 1) * 128 + r];
+        if (__any_sync(0xFFFFFFFFu, flagged != 0) && flagged != 0) {
+            const uint32_t *sw = reinterpret_cast<const uint32_t *>(sstage);
+#pragma unroll
+            for (int u = 0; u < UNITS; ++u) {
+                const int ui = u0 + u;
+                const int mode = fstage[(ui >> 1) * 128 + r];
+                if (mode != 0) {
+                    const uint4 raw = lds128(wt + ((ui ^ ((r >> 1) & 3)) << 4));
+                    const PackedUnit pu = fp8_unit_special(raw, __uint_as_float(sw[r]), mode);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) packed[8 * u + i] = pu.w[i];
+                }
+            }
+        }
     }
 }
 
@@ -182,7 +205,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
         }
         __syncwarp();
         const int token = m0 + c * 32 + lane;  // this thread now owns one token row
-        if (token >= p.M || nvalid <= 0) continue;
+        // (no early exit here: the next chunk's tcgen05.ld is warp-collective)
+        if (token < p.M && nvalid > 0) {
         const float4 *row = reinterpret_cast<const float4 *>(stg + lane * STG_PITCH);
         const int64_t yoff = ((int64_t)p.y_row + token) * p.N + fw;
         if (p.out_f32) {
@@ -216,6 +240,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
                 }
             }
         }
+        }
+        __syncwarp();
     }
 }
 

@@ -344,11 +344,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
             const uint8_t *wst = smem + C::OFF_W + s * C::W_BYTES;
             const uint8_t *sst = smem + C::OFF_S + s * C::S_BYTES;
             const uint8_t *fst = smem + C::OFF_F + s * C::F_BYTES;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t packed[16];
-                decode_units<FMT, 2>(p, wst, sst, fst, r, 2 * h, packed);
-                tmem_st_32x32b_x16(ta + (uint32_t)(h * 16), packed);
+            {
+                uint32_t packed[32];
+                decode_units<FMT, 4>(p, wst, sst, fst, r, 0, packed);
+                tmem_st_32x32b_x16(ta, *reinterpret_cast<uint32_t(*)[16]>(packed));
+                tmem_st_32x32b_x16(ta + 16u, *reinterpret_cast<uint32_t(*)[16]>(packed + 16));
             }
             tmem_wait_st();
             tc_fence_before();
