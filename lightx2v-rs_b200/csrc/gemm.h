@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <cstdint>
 
 namespace lx2v {
@@ -47,6 +48,10 @@ int gemm_dq_token_tile(int M, int N, int K, int units, int feat_tile);
 // The same GEMM on CTA pairs (cta_group::2): pair tile = 256 features x bt
 // tokens; tmap_x's box must be {64, bt/2}.
 cudaError_t gemm_pair_launch(int fmt, int bt, const GemmParams &p, int num_sms, cudaStream_t st);
+// Second pass of the two-pass linear (gemm_ss_sm100.cu): tmap_w maps a bf16
+// [N][K] weight (box {64, 128}, 128-byte swizzle), tmap_x has box {64, bt/2}.
+cudaError_t gemm_ss_pair_launch(int bt, const GemmParams &p, int num_sms, cudaStream_t st);
+int gemm_ss_token_tile(int M, int N, int K, int pairs);
 
 // Small-M path and the generic CUDA-core path (kernels.cu); they take plain
 // pointers instead of tensor maps.
@@ -78,6 +83,10 @@ cudaError_t convert_launch(const void *src, int src_f32, void *dst, int dst_f32,
                            cudaStream_t st);
 cudaError_t gate_residual_launch(void *h, int h_f32, const void *a, int a_f32, const void *gate,
                                  int gate_f32, size_t rows, size_t dim, cudaStream_t st);
+// First pass of the two-pass linear: the weight decoded to bf16, [N][K].
+cudaError_t dequant_bf16_launch(int fmt, const uint8_t *codes, const float *scales_t, const uint32_t *sz_t,
+                                const uint8_t *flags, int N, int K, int group, __nv_bfloat16 *out,
+                                cudaStream_t st);
 cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,
                                const uint32_t *sz_t, const uint8_t *flags, int N, int K, int group,
                                float *out, cudaStream_t st);

@@ -1,0 +1,288 @@
+// gemm_ss_sm100.cu — second pass of the two-pass linear: y = act(x W^T + b)
+// (or h += gate * act(x W^T + b)) with W already decoded to a bf16 [N][K]
+// array (dequant_bf16_kernel, or a bf16 weight as uploaded). Same result as
+// the one-pass kernels (Backend::linear and the fused gated residual,
+// crates/lightx2v-core/src/backend.rs:199-212, 244-253): both multiply the
+// same bf16 operands with f32 accumulation.
+//
+// Why two passes: at thousands of tokens each weight element is used by
+// every token tile, so decoding it once per call (an HBM-bound pass over
+// N x K) and then running a GEMM whose operands both come from shared memory
+// costs less than decoding it again for every token tile inside the GEMM,
+// where the decode warps share the SM with the MMA-issuing thread.
+//
+// Tile: a cluster of two CTAs on two SMs computes 256 output features x BT
+// tokens with tcgen05.mma.cta_group::2.kind::f16 (M = 256, N = BT, K = 16):
+// CTA r TMA-loads weight rows [128 r, 128 r + 128) of the tile (A) and tokens
+// [BT/2 r, BT/2 r + BT/2) of x (B) into its own shared memory, both 128-byte
+// swizzled K-major; the leader issues the MMAs. Accumulators: ACC buffers of
+// BT TMEM columns, so the epilogue of one tile overlaps the k-loop of the
+// next. Persistent grid of CTA pairs, tiles strided over pairs, token tile
+// fastest (neighbouring pairs share the weight tile in L2).
+//
+// Warp roles (256 threads per CTA): warp 0 TMA producer (both CTAs), warp 1
+// MMA issuer (leader CTA) and TMEM allocation, warps 4-7 epilogue (both
+// CTAs; gemm_common.cuh epilogue_tile).
+//
+// Synchronisation (all waits bounded, ptx.cuh), per group of GRP k-blocks:
+//   full[g]      leader; 1 arrival (the leader producer's expect_tx) plus the
+//                A and x bytes of both CTAs (TMA .cta_group::2, no multicast)
+//   empty[g]     each CTA; multicast tcgen05.commit once the group's MMAs
+//                completed: frees both CTAs' stages of the group
+//   acc_full[b]  each CTA; multicast commit after a tile's last group
+//   acc_empty[b] leader; 8 arrivals (4 epilogue warps x 2 CTAs)
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include "gemm_common.cuh"
+
+namespace lx2v {
+
+template <int BT, int ACC, int SS>
+struct SsCfg {
+    static constexpr int XH_BYTES = (BT / 2) * BK * 2;  // this CTA's half of the x tile
+    static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's 128 weight rows
+    static constexpr int OFF_A = SS * XH_BYTES;
+    static constexpr int OFF_STG = OFF_A + SS * A_BYTES;
+    static constexpr int OFF_BAR = OFF_STG + STG_TOTAL;
+    static constexpr int NUM_BARS = 2 * SS + 2 * ACC + 1;
+    static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
+    static_assert(ACC * BT <= TMEM_COLS, "TMEM budget");
+    static_assert(BT % 64 == 0 && BT <= 256, "pair token tile");
+    static_assert(XH_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+constexpr int SS_THREADS = 256;
+
+struct SsCtl {
+    uint32_t tmem_base;
+    int epi_ok;
+};
+
+template <int BT, int ACC, int SS, int GRP>
+__global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __grid_constant__ GemmParams p) {
+    using C = SsCfg<BT, ACC, SS>;
+    static_assert(SS % GRP == 0, "k-block groups tile the ring");
+    constexpr int NG = SS / GRP;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
+    uint64_t *full = bars;                  // [NG]
+    uint64_t *empty = full + NG;            // [NG]
+    uint64_t *acc_full = empty + NG;        // [ACC]
+    uint64_t *acc_empty = acc_full + ACC;   // [ACC]
+    uint64_t *drain = acc_empty + ACC;      // [1]
+    SsCtl *ctl = reinterpret_cast<SsCtl *>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool lead = rank == 0;
+    const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+    const int n_mt = (p.M + BT - 1) / BT;
+    const int n_ft = (p.N + 255) / 256;
+    const int n_tiles = n_mt * n_ft;
+    const int KG = ((p.K + BK - 1) / BK) / GRP;  // groups per tile (the host keeps K a multiple of GRP k-blocks)
+    int *err = p.err;
+    const uint64_t lim = p.wait_limit_ns;
+    const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
+
+    if (threadIdx.x == 0) {
+        for (int g = 0; g < NG; ++g) {
+            mbar_init(&full[g], 1);
+            mbar_init(&empty[g], 1);
+        }
+        for (int b = 0; b < ACC; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&p.tmap_x);
+        tma_prefetch_desc(&p.tmap_w);
+    }
+    if (warp == 1) tmem_alloc_pair(&ctl->tmem_base, TMEM_COLS);
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            int last_phase[NG];
+            for (int g = 0; g < NG; ++g) last_phase[g] = -1;
+            constexpr uint32_t tx = GRP * 2 * (C::XH_BYTES + C::A_BYTES);
+            Ring gs;
+            bool ok = true;
+            for (int t = pair; t < n_tiles && ok; t += npairs) {
+                const int mt = t % n_mt, ft = t / n_mt;
+                const int row0 = ft * 256 + (int)rank * 128;
+                const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
+                for (int gr = 0; gr < KG; ++gr) {
+                    if (!mbar_wait_cluster_bounded(&empty[gs.s], gs.ph ^ 1, err, lim)) { ok = false; break; }
+                    if (lead) mbar_arrive_expect_tx(&full[gs.s], tx);
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[gs.s]), 0);
+#pragma unroll
+                    for (int h = 0; h < GRP; ++h) {
+                        const int kb = gr * GRP + h;
+                        const int s = gs.s * GRP + h;
+                        tma_load_2d_pair(smem + s * C::XH_BYTES, &p.tmap_x, fbar, kb * BK, xrow);
+                        tma_load_2d_pair(smem + C::OFF_A + s * C::A_BYTES, &p.tmap_w, fbar, kb * BK, row0);
+                    }
+                    last_phase[gs.s] = gs.ph;
+                    gs.next<NG>();
+                }
+            }
+            // Drain: a group's loads have landed once the leader's MMAs
+            // released it.
+            for (int g = 0; g < NG; ++g)
+                if (last_phase[g] >= 0) mbar_wait_cluster_bounded(&empty[g], (uint32_t)last_phase[g], nullptr, drain_lim);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader CTA) ----------------
+        if (lane == 0 && lead) {
+            const uint32_t idesc = idesc_bf16_f32(256, BT);
+            Ring gs, ab;
+            bool ok = true;
+            for (int t = pair; t < n_tiles && ok; t += npairs) {
+                if (!mbar_wait_cluster_bounded(&acc_empty[ab.s], ab.ph ^ 1, err, lim)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
+                for (int gr = 0; gr < KG; ++gr) {
+                    if (!mbar_wait_cluster_bounded(&full[gs.s], gs.ph, err, lim)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int h = 0; h < GRP; ++h) {
+                        const int s = gs.s * GRP + h;
+                        const uint64_t a_desc = smem_desc_sw128(smem_u32(smem + C::OFF_A + s * C::A_BYTES));
+                        const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + s * C::XH_BYTES));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            mma_ss_f16_pair(d_tmem, a_desc + (uint64_t)(kk * 2), b_desc + (uint64_t)(kk * 2), idesc,
+                                            (gr != 0 || h != 0 || kk != 0) ? 1u : 0u);
+                    }
+                    mma_commit_pair(&empty[gs.s], 0x3);
+                    if (gr == KG - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
+                    gs.next<NG>();
+                }
+                ab.next<ACC>();
+            }
+            mma_commit_pair(drain, 0x1);
+            mbar_wait_bounded(drain, 0, nullptr, drain_lim);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ---------------- epilogue (both CTAs) ----------------
+        const int q = warp - 4;
+        const bool leader_thread = threadIdx.x == 128;
+        Ring ab;
+        for (int t = pair; t < n_tiles; t += npairs) {
+            const int mt = t % n_mt, ft = t / n_mt;
+            if (leader_thread) ctl->epi_ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+            named_bar_sync(1, EPI_THREADS);
+            if (!ctl->epi_ok) break;
+            tc_fence_after();
+            const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
+            const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
+            epilogue_tile<false>(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
+                                 [&] {
+                                     tc_fence_before();
+                                     __syncwarp();
+                                     if (lane == 0) mbar_arrive_cluster(rel);
+                                 });
+            ab.next<ACC>();
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // the leader's MMAs and both epilogues are done with both TMEMs
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
+}
+
+// ---- host launcher --------------------------------------------------------
+// Ring depth: as many 64-wide k-block stages as shared memory holds (at most
+// 8), even so that groups of two k-blocks tile it.
+constexpr int ss_stages(int bt) {
+    const int budget = 227 * 1024 - 1024 - STG_TOTAL - 512;
+    const int stage = (bt / 2) * BK * 2 + 128 * BK * 2;
+    const int n = budget / stage > 8 ? 8 : budget / stage;
+    return n - n % 2;
+}
+
+template <int BT, int ACC, int SS, int GRP>
+static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
+    using C = SsCfg<BT, ACC, SS>;
+    auto kern = gemm_ss_pair_kernel<BT, ACC, SS, GRP>;
+    static int max_pairs = 0;
+    const int smem = C::SMEM_BYTES;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(SS_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_pairs == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3(2 * (num_sms / 2));
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        max_pairs = clusters > 0 ? clusters : 1;
+    }
+    const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
+    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    cfg.gridDim = dim3(2 * pairs);
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int BT, int ACC>
+static cudaError_t ss_launch_bt(const GemmParams &p, int num_sms, cudaStream_t st) {
+    constexpr int SS = ss_stages(BT);
+    if (p.kgroup == 2) return ss_launch_t<BT, ACC, SS, 2>(p, num_sms, st);
+    return ss_launch_t<BT, ACC, SS, 1>(p, num_sms, st);
+}
+
+cudaError_t gemm_ss_pair_launch(int bt, const GemmParams &p, int num_sms, cudaStream_t st) {
+    switch (bt) {
+        case 128: return ss_launch_bt<128, 4>(p, num_sms, st);
+        case 192: return ss_launch_bt<192, 2>(p, num_sms, st);
+        case 256: return ss_launch_bt<256, 2>(p, num_sms, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// Token tile for an M x N output on `pairs` CTA pairs. A wave of tiles takes
+// time proportional to K * (BT + 150) on B200: a 128-token tile runs its
+// k-loop at well under half the time of a 256-token one per wave, since the
+// weight tile it streams per k-block is as large (fitted on the 1.3B chunk's
+// four linears, M = 4680: it ranks the three tiles as measured for each).
+int gemm_ss_token_tile(int M, int N, int K, int pairs) {
+    (void)K;
+    const int cand[3] = {256, 192, 128};
+    int best = 256;
+    double best_cost = 0.0;
+    for (int i = 0; i < 3; ++i) {
+        const int bt = cand[i];
+        const long long tiles = (long long)((M + bt - 1) / bt) * ((N + 255) / 256);
+        const long long waves = (tiles + pairs - 1) / pairs;
+        const double cost = (double)waves * (bt + 150.0);
+        if (i == 0 || cost < best_cost) {
+            best = bt;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+}  // namespace lx2v

@@ -2,6 +2,7 @@
 //   convert          f32 <-> bf16 element conversion (upload / download / copy)
 //   gate_residual    Backend::gate_residual, crates/lightx2v-cpu/src/lib.rs:394-404
 //   dequant_f32      bit-exact weight decode (test hook for quant.rs dequantize)
+//   dequant_bf16     first pass of the two-pass linear: the bf16 weight operand
 //   linear_simt      Backend::linear for shapes the tensor-core kernel does not
 //                    take (K not a multiple of 16, odd groups, tiny M, f32 x).
 #include <cuda_bf16.h>
@@ -98,6 +99,53 @@ __global__ void dequant_elems_kernel(WeightView w, float *out) {
     const int64_t total = (int64_t)w.n * w.k;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = dq_elem(w, i / w.k, i % w.k);
+}
+
+// ---- dequant to bf16 (first pass of the two-pass linear) --------------------------
+// Row-major bf16 copy of the weight, [N][K], each value the decoded weight
+// rounded to nearest-even: the same bf16 operand that the dequant warps of the
+// one-pass kernels write into TMEM (unit_to_bf16, with the FP8 blocks' flag
+// choosing the hardware, fixed-up or reference decode), so both kinds of
+// kernel multiply identical operands. Thread = one 16-value unit; consecutive
+// threads take consecutive units of a row (16-byte code loads, 32-byte stores).
+template <int FMT>
+__global__ void __launch_bounds__(256) dequant_bf16_kernel(WeightView w, __nv_bfloat16 *out) {
+    const int units_per_row = w.k / 16;
+    const int64_t total = (int64_t)w.n * units_per_row;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        const int n = (int)(u / units_per_row), k0 = (int)(u % units_per_row) * 16;
+        const int64_t base = (int64_t)n * w.k + k0;
+        const int64_t g = k0 / w.group;
+        uint32_t o[8];
+        if (FMT == FMT_Q4) {
+            const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(w.codes + base / 2));
+            float s, z;
+            q4_scale_zero(__ldg(w.sz_t + g * w.n + n), s, z);
+            unit_to_bf16<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), make_uint4(0, 0, 0, 0), s, z, 0, o);
+        } else {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(w.codes + base));
+            const int mode = FMT == FMT_FP8 ? __ldg(w.flags + (int64_t)(k0 / 32) * w.n + n) : 0;
+            unit_to_bf16<FMT>(raw, raw, __ldg(w.scales_t + g * w.n + n), 0.0f, mode, o);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(out + base);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+cudaError_t dequant_bf16_launch(int fmt, const uint8_t *codes, const float *scales_t, const uint32_t *sz_t,
+                                const uint8_t *flags, int N, int K, int group, __nv_bfloat16 *out,
+                                cudaStream_t st) {
+    WeightView w{fmt, N, K, group, codes, scales_t, sz_t, flags};
+    if ((size_t)N * K == 0) return cudaSuccess;
+    if (fmt == FMT_BF16 || !unit_path_ok(fmt, K, group)) return cudaErrorInvalidValue;
+    const int g = grid_for((size_t)N * K / 16, 256);
+    switch (fmt) {
+        case FMT_Q8: dequant_bf16_kernel<FMT_Q8><<<g, 256, 0, st>>>(w, out); break;
+        case FMT_Q4: dequant_bf16_kernel<FMT_Q4><<<g, 256, 0, st>>>(w, out); break;
+        default: dequant_bf16_kernel<FMT_FP8><<<g, 256, 0, st>>>(w, out); break;
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,

@@ -225,6 +225,18 @@ __device__ __forceinline__ void mma_ts_f16_pair(uint32_t d_tmem, uint32_t a_tmem
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Pair MMA with both operands in shared memory: D[tmem, both CTAs] (+)=
+// A[smem desc, both CTAs: 128 rows each] * B[smem desc, both CTAs: N/2 rows
+// each]^T (the descriptors name the same offset in both CTAs).
+__device__ __forceinline__ void mma_ss_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // Arrive once on `bar` in each CTA of `cta_mask` when all prior tcgen05 ops of
 // this thread finish (commit of the pair's MMAs).
 __device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {

@@ -45,6 +45,8 @@ struct lx2v_ctx {
     size_t sk_ws_bytes = 0;
     int sk_epoch = 0;
     float *gemv_ws = nullptr;    // few-token kernel: split-K partials + arrival counters
+    void *dq_ws = nullptr;       // two-pass linear: the weight decoded to bf16
+    size_t dq_ws_bytes = 0;
     size_t gemv_ws_floats = 0;
     int *gemv_arrivals = nullptr;
     size_t gemv_tiles = 0;
@@ -194,6 +196,21 @@ static lx2v_status ensure_gemv_workspace(lx2v_ctx *ctx, int N, int K) {
     return LX2V_OK;
 }
 
+// Two-pass linear workspace: one bf16 [N][K] weight (grow-only; a call
+// reuses it once the previous call's GEMM has read it, by stream order).
+static lx2v_status ensure_dq_workspace(lx2v_ctx *ctx, size_t bytes) {
+    if (ctx->dq_ws_bytes >= bytes) return LX2V_OK;
+    if (ctx->dq_ws) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->dq_ws);
+        ctx->dq_ws = nullptr;
+        ctx->dq_ws_bytes = 0;
+    }
+    CUDA_TRY(ctx, cudaMalloc(&ctx->dq_ws, bytes));
+    ctx->dq_ws_bytes = bytes;
+    return LX2V_OK;
+}
+
 static lx2v_status ensure_staging(lx2v_ctx *ctx, size_t bytes) {
     if (ctx->staging_bytes >= bytes) return LX2V_OK;
     if (ctx->staging) {
@@ -262,6 +279,7 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     if (ctx->staging) cudaFree(ctx->staging);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
+    if (ctx->dq_ws) cudaFree(ctx->dq_ws);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -649,6 +667,12 @@ static lx2v_status make_map(lx2v_ctx *ctx, CUtensorMap *map, const void *base, C
 // read per pair. With several waves of tiles it measured slower than whole
 // tiles on B200 (FFN2 of the 1.3B chunk: 762 vs 804 TFLOP/s), so it is only
 // taken when it at least shortens the critical path by 40%.
+// Rows from which the two-pass linear (decode the weight once to bf16, then a
+// GEMM with both operands in shared memory) is the automatic choice for
+// quantized weights: below it the one-pass kernel's per-tile decode is
+// cheaper than the extra pass over N x K.
+static constexpr int TWO_PASS_MIN_ROWS = 1024;
+
 static bool use_streamk(const lx2v_ctx *ctx, int M, int N, int K, int bt) {
     if (ctx->split_mode == 1) return false;
     const int pairs = ctx->num_sms / 2;
@@ -701,10 +725,21 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     a.gate = gate_ptr; a.gate_f32 = mods && mods->dtype == LX2V_F32;
     a.act = act;
     const bool gemv_ok = gemv_supported(a);
+    // Two-pass linear (decode once, then both GEMM operands from shared
+    // memory): any group size the unit decode takes.
+    const bool ss_ok = x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 &&
+                       unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16;
     int path = ctx->path;
-    if (path == 0) path = rows <= 16 && gemv_ok ? 2 : tc_ok ? (rows >= 512 && N >= 256 ? 4 : 1) : 3;
+    if (path == 0) {
+        if (rows <= 16 && gemv_ok) path = 2;
+        else if (ss_ok && N >= 256 && rows >= (w->fmt == LX2V_W_BF16 ? 512u : (size_t)TWO_PASS_MIN_ROWS)) path = 5;
+        else if (tc_ok) path = rows >= 512 && N >= 256 ? 4 : 1;
+        else path = 3;
+    }
     if ((path == 1 || path == 4) && !tc_ok)
         return fail(ctx, LX2V_ERR_UNSUPPORTED, "the tensor-core kernel does not take this shape/dtype");
+    if (path == 5 && !ss_ok)
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "the two-pass kernel does not take this shape/dtype");
     if (path == 2) {
         if (!gemv_ok)
             return fail(ctx, LX2V_ERR_UNSUPPORTED,
@@ -713,6 +748,45 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         if (s) return s;
         CUDA_TRY(ctx, linear_gemv_launch(a, ctx->num_sms, ctx->stream, ctx->gemv_ws, ctx->gemv_arrivals,
                                          ctx->gemv_ws_floats));
+        ctx->launches++;
+        return LX2V_OK;
+    }
+
+    if (path == 5) {
+        const void *wa = w->codes;
+        if (w->fmt != LX2V_W_BF16) {
+            lx2v_status s = ensure_dq_workspace(ctx, N * K * 2);
+            if (s) return s;
+            CUDA_TRY(ctx, dequant_bf16_launch(w->fmt, (const uint8_t *)w->codes, w->scales_t, w->sz_t, w->flags,
+                                              (int)N, (int)K, (int)w->group, (__nv_bfloat16 *)ctx->dq_ws,
+                                              ctx->stream));
+            ctx->launches++;
+            wa = ctx->dq_ws;
+        }
+        GemmParams p;
+        memset(&p, 0, sizeof p);
+        const int bt = ctx->token_tile ? ctx->token_tile
+                                       : gemm_ss_token_tile((int)rows, (int)N, (int)K, ctx->num_sms / 2);
+        lx2v_status s = make_map(ctx, &p.tmap_x, x->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, x_row + rows, 64,
+                                 (uint32_t)(bt / 2), CU_TENSOR_MAP_SWIZZLE_128B);
+        if (s) return s;
+        s = make_map(ctx, &p.tmap_w, wa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+        if (s) return s;
+        p.y = y->ptr;
+        p.bias = bias ? bias->ptr : nullptr;
+        p.bias_f32 = bias && bias->dtype == LX2V_F32;
+        p.gate = gate_ptr;
+        p.gate_f32 = mods && mods->dtype == LX2V_F32;
+        p.err = ctx->err_dev;
+        p.wait_limit_ns = ctx->wait_limit_ns;
+        p.M = (int)rows; p.N = (int)N; p.K = (int)K; p.group = (int)w->group;
+        p.x_row = (int)x_row; p.y_row = (int)y_row;
+        p.act = act;
+        p.out_f32 = y->dtype == LX2V_F32;
+        p.reduce = mods ? 1 : 0;
+        p.kgroup = K % 128 == 0 ? 2 : 1;
+        CUDA_TRY(ctx, gemm_ss_pair_launch(bt, p, ctx->num_sms, ctx->stream));
         ctx->launches++;
         return LX2V_OK;
     }
@@ -850,7 +924,7 @@ extern "C" lx2v_status lx2v_profile_reset(lx2v_ctx *ctx) {
 
 extern "C" lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path) {
     if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
-    if (path < 0 || path > 4) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
+    if (path < 0 || path > 5) return fail(ctx, LX2V_ERR_INVALID, "bad path %d", path);
     ctx->path = path;
     return LX2V_OK;
 }

@@ -325,7 +325,7 @@ def test_pair_kernel_matches_oracle_and_single_cta(be, oracle, fmt, M, N, K, bt)
     outs = {}
     try:
         be.set_token_tile(bt)
-        for path in (4, 1):
+        for path in (4, 5, 1):
             be.set_linear_path(path)
             yb = be.alloc(M * N, F32)
             be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
@@ -334,12 +334,14 @@ def test_pair_kernel_matches_oracle_and_single_cta(be, oracle, fmt, M, N, K, bt)
         be.set_linear_path(0)
         be.set_token_tile(0)
     want = oracle.linear(x, M, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=1, threads=8)
-    assert rel_l2(outs[4], want) <= REL_L2
-    # same bf16 operands, different summation order
-    assert rel_l2(outs[4], outs[1]) <= 1e-5
+    for path in (4, 5):
+        assert rel_l2(outs[path], want) <= REL_L2, path
+        # same bf16 operands, different summation order
+        assert rel_l2(outs[path], outs[1]) <= 1e-5, path
 
 
-def test_pair_kernel_gated_residual_and_offsets(be, oracle):
+@pytest.mark.parametrize("path", [4, 5])
+def test_pair_kernel_gated_residual_and_offsets(be, oracle, path):
     M, N, K = 900, 768, 512
     w, q = make_weight("fp8", N, K, seed=61, oracle=oracle)
     dw = be.weight_fp8(q)
@@ -349,7 +351,7 @@ def test_pair_kernel_gated_residual_and_offsets(be, oracle):
     xb, mb = be.upload(x), be.upload(mods, F32)
     hb = be.upload(h0, F32)
     try:
-        be.set_linear_path(4)
+        be.set_linear_path(path)
         be.linear_gate_residual(xb, 40, M, dw, None, Act.NONE, hb, 7, mb, 5)
     finally:
         be.set_linear_path(0)
@@ -359,6 +361,39 @@ def test_pair_kernel_gated_residual_and_offsets(be, oracle):
     want[7:] = oracle.gate_residual(h0.reshape(M + 7, N)[7:], lin, M, N, mods, 5)
     assert np.array_equal(got[:7], h0.reshape(M + 7, N)[:7])
     assert rel_l2(got[7:] - h0.reshape(M + 7, N)[7:], want[7:] - h0.reshape(M + 7, N)[7:]) <= REL_L2
+
+
+# ---- two-pass linear (weight decoded once to bf16, then both operands from smem) ----------
+@pytest.mark.parametrize("fmt", ["fp8", "q4"])
+@pytest.mark.parametrize("M,N,K,bt", [(4680, 1536, 1536, 128), (4680, 4608, 1536, 256), (2100, 1552, 8960, 192),
+                                      (1030, 8960, 704, 256)])
+def test_two_pass_matches_one_pass_at_chunk_shapes(be, oracle, fmt, M, N, K, bt):
+    # the token tiles and k-block groupings of the 1.3B chunk's linears, plus
+    # ragged N / M and K without 128-column groups (704 = 11 k-blocks)
+    w, q = make_weight(fmt, N, K, seed=131 + N, oracle=oracle)
+    dw = upload_weight(be, fmt, q, w, N, K)
+    x = oracle.normal(132, M * K)
+    b = oracle.normal(133, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b)
+    outs = {}
+    try:
+        be.set_token_tile(bt)
+        for path in (5, 4):
+            be.set_linear_path(path)
+            for rep in range(2 if path == 5 else 1):  # the second call reuses the decoded-weight workspace
+                yb = be.alloc(M * N, F32)
+                be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
+                outs[(path, rep)] = be.download(yb).reshape(M, N)
+    finally:
+        be.set_linear_path(0)
+        be.set_token_tile(0)
+    assert np.array_equal(outs[(5, 0)], outs[(5, 1)], equal_nan=True)
+    # same bf16 operands, f32 sums possibly in another order
+    assert rel_l2(outs[(5, 0)], outs[(4, 0)]) <= 1e-5
+    rows = sampled_rows(M, 32)
+    want = np.stack([oracle.linear(x, 1, oracle_dequant(oracle, fmt, q, w), N, K, bias=b, act=1,
+                                   x_row=int(r), threads=8)[0] for r in rows])
+    assert rel_l2(outs[(5, 0)][rows], want) <= REL_L2
 
 
 # ---- GEMM operand decode: bit-exact through a one-hot activation --------------------------
@@ -385,7 +420,7 @@ def fp8_all_codes_weight(N, K, seed):
 
 
 @pytest.mark.parametrize("fmt", ["fp8_all", "fp8", "q8", "q4", "native"])
-@pytest.mark.parametrize("path", [1, 4, 3])
+@pytest.mark.parametrize("path", [1, 4, 5, 3])
 def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
     # x = identity (K tokens, one-hot): y[m][n] = operand(w[n][m]) exactly,
     # since every other product is 0 * w. Rows holding a NaN code are NaN.
