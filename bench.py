@@ -415,7 +415,8 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": f"bf16 dense burst, {peak_src}",
                          "traffic": profile_traffic(),
-                         "kernel": "gemm_pair_kernel<FP8> (tcgen05.mma cta_group::2, dequantised weights in TMEM)",
+                         "kernel": "gemm_ss_pair_kernel (tcgen05.mma cta_group::2, both operands TMA-staged in "
+                                   "shared memory) after dequant_bf16_kernel<FP8>; achieved counts both kernels' time",
                          "per_linear": per_kernel},
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),

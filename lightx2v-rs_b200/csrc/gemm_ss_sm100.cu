@@ -20,9 +20,11 @@
 // next. Persistent grid of CTA pairs, tiles strided over pairs, token tile
 // fastest (neighbouring pairs share the weight tile in L2).
 //
-// Warp roles (256 threads per CTA): warp 0 TMA producer (both CTAs), warp 1
-// MMA issuer (leader CTA) and TMEM allocation, warps 4-7 epilogue (both
-// CTAs; gemm_common.cuh epilogue_tile).
+// Warp roles (384 threads per CTA): warp 0 TMA producer (both CTAs), warp 1
+// MMA issuer (leader CTA) and TMEM allocation, warps 4-11 epilogue (both
+// CTAs): warp w reads TMEM lanes 32 (w % 4) .. + 31 of token columns
+// [BT/2 h, BT/2 h + BT/2), h = (w - 4) / 4, and stores straight from
+// registers (epilogue_direct), so shared memory holds only the ring.
 //
 // Synchronisation (all waits bounded, ptx.cuh), per group of GRP k-blocks:
 //   full[g]      leader; 1 arrival (the leader producer's expect_tx) plus the
@@ -30,7 +32,7 @@
 //   empty[g]     each CTA; multicast tcgen05.commit once the group's MMAs
 //                completed: frees both CTAs' stages of the group
 //   acc_full[b]  each CTA; multicast commit after a tile's last group
-//   acc_empty[b] leader; 8 arrivals (4 epilogue warps x 2 CTAs)
+//   acc_empty[b] leader; 16 arrivals (8 epilogue warps x 2 CTAs)
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -44,8 +46,7 @@ struct SsCfg {
     static constexpr int XH_BYTES = (BT / 2) * BK * 2;  // this CTA's half of the x tile
     static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's 128 weight rows
     static constexpr int OFF_A = SS * XH_BYTES;
-    static constexpr int OFF_STG = OFF_A + SS * A_BYTES;
-    static constexpr int OFF_BAR = OFF_STG + STG_TOTAL;
+    static constexpr int OFF_BAR = OFF_A + SS * A_BYTES;
     static constexpr int NUM_BARS = 2 * SS + 2 * ACC + 1;
     static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
     static_assert(ACC * BT <= TMEM_COLS, "TMEM budget");
@@ -54,12 +55,95 @@ struct SsCfg {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-constexpr int SS_THREADS = 256;
+constexpr int SS_EPI_WARPS = 8;
+constexpr int SS_THREADS = 32 * (4 + SS_EPI_WARPS);
 
 struct SsCtl {
     uint32_t tmem_base;
-    int epi_ok;
 };
+
+// One 32-token chunk of the epilogue: v[j] = the f32 accumulator of token
+// tok0 + j for this thread's feature f. Bias, GELU and gate in f32 exactly as
+// epilogue_tile does them; each store of a warp covers one token's 32
+// consecutive features.
+__device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t (&v)[32], int tok0, int f, bool fok,
+                                           float2 bias2, float2 gate2) {
+    const int nt = min(32, p.M - tok0);
+    const int64_t n = p.N;
+    const int64_t off0 = ((int64_t)p.y_row + tok0) * n + f;
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float2 t = __fadd2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), bias2);
+        if (p.act == 1) t = gelu2(t);
+        if (p.gate) t = __fmul2_rn(t, gate2);
+        o[2 * i] = t.x;
+        o[2 * i + 1] = t.y;
+    }
+    if (p.out_f32) {
+        float *dst = reinterpret_cast<float *>(p.y) + off0;
+        if (!p.reduce) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (fok && j < nt) dst[j * n] = o[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (fok && j < nt)
+                    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(dst + j * n), "f"(o[j]) : "memory");
+        }
+    } else {
+        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.y) + off0;
+        if (!p.reduce) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (fok && j < nt) dst[j * n] = __float2bfloat16_rn(o[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (fok && j < nt) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(o[j]);
+                    asm volatile("red.global.add.noftz.bf16 [%0], %1;" ::"l"(dst + j * n),
+                                 "h"(*reinterpret_cast<const unsigned short *>(&h))
+                                 : "memory");
+                }
+        }
+    }
+    __syncwarp();  // the next tcgen05 instruction is warp-collective
+}
+
+// Epilogue of `ntok` accumulator columns from `acc_addr` (this thread: TMEM
+// lane = output feature f; tokens m0 .., m0 < M) without a staging copy: the
+// next 32-column TMEM load is in flight while a chunk is stored. `release`
+// runs once the last load has completed.
+template <typename Release>
+__device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t acc_addr, int ntok, int f, int m0,
+                                                Release release) {
+    const bool fok = f < p.N;
+    float bias_f = 0.0f, gate_f = 1.0f;
+    if (fok) {
+        if (p.bias) bias_f = p.bias_f32 ? reinterpret_cast<const float *>(p.bias)[f]
+                                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.bias)[f]);
+        if (p.gate) gate_f = p.gate_f32 ? reinterpret_cast<const float *>(p.gate)[f]
+                                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.gate)[f]);
+    }
+    const float2 bias2 = make_float2(bias_f, bias_f), gate2 = make_float2(gate_f, gate_f);
+    const int nld = min(ntok / 32, (p.M - m0 + 31) / 32);
+    uint32_t a[32], b[32];
+    tmem_ld_32x32b_x32(acc_addr, a);
+    for (int c = 0; c < nld; c += 2) {
+        tmem_wait_ld_regs(a);
+        if (c + 1 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 1) * 32), b);
+        else release();
+        store_chunk(p, a, m0 + c * 32, f, fok, bias2, gate2);
+        if (c + 1 < nld) {
+            tmem_wait_ld_regs(b);
+            if (c + 2 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 2) * 32), a);
+            else release();
+            store_chunk(p, b, m0 + (c + 1) * 32, f, fok, bias2, gate2);
+        }
+    }
+}
 
 template <int BT, int ACC, int SS, int GRP>
 __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __grid_constant__ GemmParams p) {
@@ -95,7 +179,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
         }
         for (int b = 0; b < ACC; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 8);
+            mbar_init(&acc_empty[b], 2 * SS_EPI_WARPS);
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -176,23 +260,28 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
         __syncwarp();
     } else if (warp >= 4) {
         // ---------------- epilogue (both CTAs) ----------------
-        const int q = warp - 4;
-        const bool leader_thread = threadIdx.x == 128;
+        const int q = warp & 3, half = (warp - 4) >> 2;
         Ring ab;
         for (int t = pair; t < n_tiles; t += npairs) {
             const int mt = t % n_mt, ft = t / n_mt;
-            if (leader_thread) ctl->epi_ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
-            named_bar_sync(1, EPI_THREADS);
-            if (!ctl->epi_ok) break;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            if (!ok) break;
             tc_fence_after();
-            const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT);
             const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
-            epilogue_tile<false>(p, acc_addr, BT, ft * 256 + (int)rank * 128, mt * BT, q, lane, smem + C::OFF_STG,
-                                 [&] {
-                                     tc_fence_before();
-                                     __syncwarp();
-                                     if (lane == 0) mbar_arrive_cluster(rel);
-                                 });
+            auto release = [&] {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(rel);
+            };
+            const int m0 = mt * BT + half * (BT / 2);
+            if (m0 < p.M) {
+                const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT + half * (BT / 2));
+                epilogue_direct(p, acc_addr, BT / 2, ft * 256 + (int)rank * 128 + q * 32 + lane, m0, release);
+            } else {
+                release();  // no token of this half exists
+            }
             ab.next<ACC>();
         }
     }
@@ -205,9 +294,13 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
 
 // ---- host launcher --------------------------------------------------------
 // Ring depth: as many 64-wide k-block stages as shared memory holds (at most
-// 8), even so that groups of two k-blocks tile it.
+// 8), rounded down to even so that groups of two k-blocks (one ready wait and
+// one commit per group) tile it. Depth pays (the k-loop waits on L2 latency:
+// with 256-token tiles, 4 stages measured 13-24 % slower than 6 on the 1.3B
+// chunk's linears), but not at the price of single k-block groups (7 stages
+// of one k-block measured up to 10 % slower than 6 in groups of two).
 constexpr int ss_stages(int bt) {
-    const int budget = 227 * 1024 - 1024 - STG_TOTAL - 512;
+    const int budget = 227 * 1024 - 1024 - 512;
     const int stage = (bt / 2) * BK * 2 + 128 * BK * 2;
     const int n = budget / stage > 8 ? 8 : budget / stage;
     return n - n % 2;
@@ -249,7 +342,9 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
 template <int BT, int ACC>
 static cudaError_t ss_launch_bt(const GemmParams &p, int num_sms, cudaStream_t st) {
     constexpr int SS = ss_stages(BT);
-    if (p.kgroup == 2) return ss_launch_t<BT, ACC, SS, 2>(p, num_sms, st);
+    if constexpr (SS % 2 == 0) {
+        if (p.kgroup == 2) return ss_launch_t<BT, ACC, SS, 2>(p, num_sms, st);
+    }
     return ss_launch_t<BT, ACC, SS, 1>(p, num_sms, st);
 }
 
