@@ -29,12 +29,13 @@ struct alignas(64) GemmParams {
     int bias_f32, gate_f32;   // element types of bias / gate
     int sgrp;                 // scale groups per k-block box (1, 2 or 4)
     int gshift;               // log2(group) when group < 64, else 6
-    // Stream-K (pair kernel): when streamk != 0 the tiles' k-blocks are split
+    // Stream-K (pair kernels): when streamk != 0 the tiles' k-blocks are split
     // into equal contiguous ranges, one per CTA pair. A pair whose range
     // starts inside a tile writes that partial tile's f32 accumulator to
     // partials[(pair * 2 + rank) * 128 * bt ...] and publishes `epoch` in
-    // flags[pair * 2 + rank]; the pair holding the tile's first k-block adds
-    // those partials in its epilogue.
+    // flags[pair * 2 + rank] (two-pass kernel: one flag per epilogue warp,
+    // flags[(pair * 2 + rank) * 8 + warp]); the pair holding the tile's first
+    // k-block adds those partials in its epilogue.
     int streamk;
     int epoch;
     int kgroup;               // pair kernel: k-blocks per MMA group (1, or 2 when K % 128 == 0)

@@ -138,6 +138,35 @@ __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t 
     }
 }
 
+// The work of one CTA pair as a list of segments: k-blocks [kb0, kb1) of a
+// tile. Whole tiles: tiles pair, pair + npairs, ... Stream-K: the
+// n_tiles * KB k-blocks split into npairs equal contiguous ranges; a range
+// may start and end inside a tile.
+struct PairWork {
+    long long lo = 0, hi = 0;  // stream-K k-block range
+    int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
+    bool sk = false;
+    __device__ __forceinline__ int count() const {
+        if (!sk) return my_tiles;
+        return hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0;
+    }
+    __device__ __forceinline__ long long total_kb() const { return sk ? hi - lo : (long long)my_tiles * KB; }
+    __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
+        if (!sk) {
+            tile = pair + idx * npairs;
+            kb0 = 0;
+            kb1 = KB;
+            return;
+        }
+        const long long t = lo / KB + idx;
+        const long long start = lo > t * KB ? lo : t * KB;
+        const long long end = hi < (t + 1) * KB ? hi : (t + 1) * KB;
+        tile = (int)t;
+        kb0 = (int)(start - t * KB);
+        kb1 = (int)(end - t * KB);
+    }
+};
+
 // Partial-tile traffic of a stream-K epilogue (see GemmParams::streamk).
 struct PartialIO {
     float *write = nullptr;        // non-null: store the raw accumulator here, nothing else

@@ -63,35 +63,6 @@ struct PairCtl {
     int epi_ok;
 };
 
-// The work of one CTA pair as a list of segments: k-blocks [kb0, kb1) of a
-// tile. Whole tiles: tiles pair, pair + npairs, ... Stream-K: the
-// n_tiles * KB k-blocks split into npairs equal contiguous ranges; a range
-// may start and end inside a tile.
-struct PairWork {
-    long long lo = 0, hi = 0;  // stream-K k-block range
-    int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
-    bool sk = false;
-    __device__ __forceinline__ int count() const {
-        if (!sk) return my_tiles;
-        return hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0;
-    }
-    __device__ __forceinline__ long long total_kb() const { return sk ? hi - lo : (long long)my_tiles * KB; }
-    __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
-        if (!sk) {
-            tile = pair + idx * npairs;
-            kb0 = 0;
-            kb1 = KB;
-            return;
-        }
-        const long long t = lo / KB + idx;
-        const long long start = lo > t * KB ? lo : t * KB;
-        const long long end = hi < (t + 1) * KB ? hi : (t + 1) * KB;
-        tile = (int)t;
-        kb0 = (int)(start - t * KB);
-        kb1 = (int)(end - t * KB);
-    }
-};
-
 template <int FMT, int BT, int ACC, int SS, int AS, int DQW, bool SK, int GRP>
 __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = PairCfg<FMT, BT, ACC, SS, AS>;

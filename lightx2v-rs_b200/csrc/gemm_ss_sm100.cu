@@ -62,19 +62,49 @@ struct SsCtl {
     uint32_t tmem_base;
 };
 
+// Stream-K partial tiles of one epilogue warp (GemmParams::streamk). A
+// partial tile is this CTA's raw f32 accumulator, [token column][128
+// features], so a warp's accesses for one token are 128 contiguous bytes.
+struct SkIO {
+    float *write = nullptr;      // non-null: store the raw accumulator here, nothing else
+    const float *add = nullptr;  // add n_add partial tiles from here (stride apart) before the epilogue
+    int n_add = 0;
+    int64_t stride = 0;
+};
+
 // One 32-token chunk of the epilogue: v[j] = the f32 accumulator of token
-// tok0 + j for this thread's feature f. Bias, GELU and gate in f32 exactly as
-// epilogue_tile does them; each store of a warp covers one token's 32
-// consecutive features.
+// tok0 + j (tile column col0 + j) for this thread's feature f (feature fl of
+// the CTA's 128). Bias, GELU and gate in f32 exactly as epilogue_tile does
+// them; each store of a warp covers one token's 32 consecutive features.
+template <bool SK>
 __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t (&v)[32], int tok0, int f, bool fok,
-                                           float2 bias2, float2 gate2) {
+                                           float2 bias2, float2 gate2, const SkIO &io, int col0, int fl) {
     const int nt = min(32, p.M - tok0);
     const int64_t n = p.N;
     const int64_t off0 = ((int64_t)p.y_row + tok0) * n + f;
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
+    if (SK) {
+        if (io.write) {
+            float *dst = io.write + (int64_t)col0 * 128 + fl;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) __stcg(dst + j * 128, acc[j]);
+            __syncwarp();
+            return;
+        }
+        for (int part = 0; part < io.n_add; ++part) {
+            const float *src = io.add + part * io.stride + (int64_t)col0 * 128 + fl;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) acc[j] += __ldcg(src + j * 128);
+        }
+    }
     float o[32];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        float2 t = __fadd2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), bias2);
+        float2 t = __fadd2_rn(make_float2(acc[2 * i], acc[2 * i + 1]), bias2);
         if (p.act == 1) t = gelu2(t);
         if (p.gate) t = __fmul2_rn(t, gate2);
         o[2 * i] = t.x;
@@ -116,9 +146,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t 
 // lane = output feature f; tokens m0 .., m0 < M) without a staging copy: the
 // next 32-column TMEM load is in flight while a chunk is stored. `release`
 // runs once the last load has completed.
-template <typename Release>
+template <bool SK, typename Release>
 __device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t acc_addr, int ntok, int f, int m0,
-                                                Release release) {
+                                                Release release, const SkIO &io, int col0, int fl) {
     const bool fok = f < p.N;
     float bias_f = 0.0f, gate_f = 1.0f;
     if (fok) {
@@ -135,17 +165,17 @@ __device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t ac
         tmem_wait_ld_regs(a);
         if (c + 1 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 1) * 32), b);
         else release();
-        store_chunk(p, a, m0 + c * 32, f, fok, bias2, gate2);
+        store_chunk<SK>(p, a, m0 + c * 32, f, fok, bias2, gate2, io, col0 + c * 32, fl);
         if (c + 1 < nld) {
             tmem_wait_ld_regs(b);
             if (c + 2 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 2) * 32), a);
             else release();
-            store_chunk(p, b, m0 + (c + 1) * 32, f, fok, bias2, gate2);
+            store_chunk<SK>(p, b, m0 + (c + 1) * 32, f, fok, bias2, gate2, io, col0 + (c + 1) * 32, fl);
         }
     }
 }
 
-template <int BT, int ACC, int SS, int GRP>
+template <int BT, int ACC, int SS, int GRP, bool SK>
 __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __grid_constant__ GemmParams p) {
     using C = SsCfg<BT, ACC, SS>;
     static_assert(SS % GRP == 0, "k-block groups tile the ring");
@@ -168,6 +198,16 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
     const int n_ft = (p.N + 255) / 256;
     const int n_tiles = n_mt * n_ft;
     const int KG = ((p.K + BK - 1) / BK) / GRP;  // groups per tile (the host keeps K a multiple of GRP k-blocks)
+    PairWork work;
+    work.KB = KG;
+    work.pair = pair;
+    work.npairs = npairs;
+    work.my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+    work.sk = SK;
+    const long long units = (long long)n_tiles * KG;
+    work.lo = units * pair / npairs;
+    work.hi = units * (pair + 1) / npairs;
+    const int n_seg = work.count();
     int *err = p.err;
     const uint64_t lim = p.wait_limit_ns;
     const uint64_t drain_lim = lim > 500000000ull ? lim : 500000000ull;
@@ -200,11 +240,13 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             constexpr uint32_t tx = GRP * 2 * (C::XH_BYTES + C::A_BYTES);
             Ring gs;
             bool ok = true;
-            for (int t = pair; t < n_tiles && ok; t += npairs) {
+            for (int j = 0; j < n_seg && ok; ++j) {
+                int t, kb0, kb1;
+                work.seg(j, t, kb0, kb1);
                 const int mt = t % n_mt, ft = t / n_mt;
                 const int row0 = ft * 256 + (int)rank * 128;
                 const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
-                for (int gr = 0; gr < KG; ++gr) {
+                for (int gr = kb0; gr < kb1; ++gr) {
                     if (!mbar_wait_cluster_bounded(&empty[gs.s], gs.ph ^ 1, err, lim)) { ok = false; break; }
                     if (lead) mbar_arrive_expect_tx(&full[gs.s], tx);
                     const uint32_t fbar = mapa_shared(smem_u32(&full[gs.s]), 0);
@@ -231,11 +273,13 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             const uint32_t idesc = idesc_bf16_f32(256, BT);
             Ring gs, ab;
             bool ok = true;
-            for (int t = pair; t < n_tiles && ok; t += npairs) {
+            for (int j = 0; j < n_seg && ok; ++j) {
+                int t, kb0, kb1;
+                work.seg(j, t, kb0, kb1);
                 if (!mbar_wait_cluster_bounded(&acc_empty[ab.s], ab.ph ^ 1, err, lim)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + (uint32_t)(ab.s * BT);
-                for (int gr = 0; gr < KG; ++gr) {
+                for (int gr = kb0; gr < kb1; ++gr) {
                     if (!mbar_wait_cluster_bounded(&full[gs.s], gs.ph, err, lim)) { ok = false; break; }
                     tc_fence_after();
 #pragma unroll
@@ -246,10 +290,10 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)
                             mma_ss_f16_pair(d_tmem, a_desc + (uint64_t)(kk * 2), b_desc + (uint64_t)(kk * 2), idesc,
-                                            (gr != 0 || h != 0 || kk != 0) ? 1u : 0u);
+                                            (gr != kb0 || h != 0 || kk != 0) ? 1u : 0u);
                     }
                     mma_commit_pair(&empty[gs.s], 0x3);
-                    if (gr == KG - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
+                    if (gr == kb1 - 1) mma_commit_pair(&acc_full[ab.s], 0x3);
                     gs.next<NG>();
                 }
                 ab.next<ACC>();
@@ -260,14 +304,43 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
         __syncwarp();
     } else if (warp >= 4) {
         // ---------------- epilogue (both CTAs) ----------------
-        const int q = warp & 3, half = (warp - 4) >> 2;
+        const int q = warp & 3, half = (warp - 4) >> 2, wi = warp - 4;
+        const int64_t part_floats = (int64_t)128 * BT;  // one CTA's partial tile
         Ring ab;
-        for (int t = pair; t < n_tiles; t += npairs) {
+        for (int j = 0; j < n_seg; ++j) {
+            int t, kb0, kb1;
+            work.seg(j, t, kb0, kb1);
             const int mt = t % n_mt, ft = t / n_mt;
+            SkIO io;
+            int n_add = 0;
+            if (!SK) {
+            } else if (kb0 > 0) {
+                // the tail of a split tile: the pair holding its head adds it
+                io.write = p.partials + (int64_t)(pair * 2 + (int)rank) * part_floats;
+            } else if (kb1 < KG) {
+                // the head of a split tile: the pairs after this one hold the rest
+                const long long tile_end = (long long)(t + 1) * KG;
+                while (pair + 1 + n_add < npairs && units * (pair + 1 + n_add) / npairs < tile_end) ++n_add;
+            }
             int ok = 1;
-            if (lane == 0) ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+            if (lane == 0) {
+                ok = mbar_wait_cluster_bounded(&acc_full[ab.s], ab.ph, err, lim) ? 1 : 0;
+                // each warp waits for the same warp of the tail pairs: they
+                // wrote exactly the lanes and columns it reads
+                for (int a = 0; SK && a < n_add && ok; ++a)
+                    ok = flag_wait_bounded(p.flags + ((pair + 1 + a) * 2 + (int)rank) * SS_EPI_WARPS + wi, p.epoch,
+                                           err, lim)
+                             ? 1
+                             : 0;
+            }
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             if (!ok) break;
+            if (SK && n_add > 0) {
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                io.add = p.partials + (int64_t)((pair + 1) * 2 + (int)rank) * part_floats;
+                io.n_add = n_add;
+                io.stride = 2 * part_floats;
+            }
             tc_fence_after();
             const uint32_t rel = mapa_shared(smem_u32(&acc_empty[ab.s]), 0);
             auto release = [&] {
@@ -278,9 +351,15 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             const int m0 = mt * BT + half * (BT / 2);
             if (m0 < p.M) {
                 const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT + half * (BT / 2));
-                epilogue_direct(p, acc_addr, BT / 2, ft * 256 + (int)rank * 128 + q * 32 + lane, m0, release);
+                epilogue_direct<SK>(p, acc_addr, BT / 2, ft * 256 + (int)rank * 128 + q * 32 + lane, m0, release, io,
+                                    half * (BT / 2), q * 32 + lane);
             } else {
                 release();  // no token of this half exists
+            }
+            if (SK && io.write) {
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) flag_publish(p.flags + (pair * 2 + (int)rank) * SS_EPI_WARPS + wi, p.epoch);
             }
             ab.next<ACC>();
         }
@@ -306,10 +385,10 @@ constexpr int ss_stages(int bt) {
     return n - n % 2;
 }
 
-template <int BT, int ACC, int SS, int GRP>
+template <int BT, int ACC, int SS, int GRP, bool SK>
 static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = SsCfg<BT, ACC, SS>;
-    auto kern = gemm_ss_pair_kernel<BT, ACC, SS, GRP>;
+    auto kern = gemm_ss_pair_kernel<BT, ACC, SS, GRP, SK>;
     static int max_pairs = 0;
     const int smem = C::SMEM_BYTES;
     cudaLaunchConfig_t cfg;
@@ -334,7 +413,10 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
         max_pairs = clusters > 0 ? clusters : 1;
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
-    const int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+    // stream-K: every pair gets at least one group (the host checked
+    // n_tiles * groups >= pairs)
+    const long long work = SK ? (long long)n_tiles * (((p.K + BK - 1) / BK) / GRP) : n_tiles;
+    const int pairs = work < max_pairs ? (int)work : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
@@ -343,9 +425,12 @@ template <int BT, int ACC>
 static cudaError_t ss_launch_bt(const GemmParams &p, int num_sms, cudaStream_t st) {
     constexpr int SS = ss_stages(BT);
     if constexpr (SS % 2 == 0) {
-        if (p.kgroup == 2) return ss_launch_t<BT, ACC, SS, 2>(p, num_sms, st);
+        if (p.kgroup == 2)
+            return p.streamk ? ss_launch_t<BT, ACC, SS, 2, true>(p, num_sms, st)
+                             : ss_launch_t<BT, ACC, SS, 2, false>(p, num_sms, st);
     }
-    return ss_launch_t<BT, ACC, SS, 1>(p, num_sms, st);
+    return p.streamk ? ss_launch_t<BT, ACC, SS, 1, true>(p, num_sms, st)
+                     : ss_launch_t<BT, ACC, SS, 1, false>(p, num_sms, st);
 }
 
 cudaError_t gemm_ss_pair_launch(int bt, const GemmParams &p, int num_sms, cudaStream_t st) {

@@ -153,7 +153,8 @@ static void resolve_profile(lx2v_ctx *ctx) {
 // pairs x 2 publication flags (zeroed when the workspace is allocated; they
 // hold launch epochs, so they never need clearing afterwards).
 static lx2v_status ensure_sk_workspace(lx2v_ctx *ctx, int pairs, int bt, float **partials, int **flags) {
-    const size_t flag_bytes = (size_t)ctx->num_sms * 2 * sizeof(int);  // >= pairs x 2 flags
+    // >= pairs x 2 CTAs x 8 flags (the two-pass kernel has one per epilogue warp)
+    const size_t flag_bytes = (size_t)ctx->num_sms * 2 * 8 * sizeof(int);
     const size_t part_bytes = (size_t)pairs * 2 * 128 * bt * sizeof(float);
     if (ctx->sk_ws_bytes < part_bytes + flag_bytes) {
         if (ctx->sk_ws) {
@@ -667,6 +668,20 @@ static lx2v_status make_map(lx2v_ctx *ctx, CUtensorMap *map, const void *base, C
 // read per pair. With several waves of tiles it measured slower than whole
 // tiles on B200 (FFN2 of the 1.3B chunk: 762 vs 804 TFLOP/s), so it is only
 // taken when it at least shortens the critical path by 40%.
+// Stream-K for the two-pass kernel, on request only (lx2v_set_split_mode 2).
+// It balances the 1.3B chunk's N = 1536 linears (114 tiles on 74 pairs, 1.54
+// waves) but measured slower on B200 (out 431 vs 614, FFN2 1023 vs 1076
+// TFLOP/s): the k-loop is bound by L2 traffic that all pairs share, which
+// idle pairs in a short last wave do not waste, while the partial tiles add
+// to it.
+static bool use_streamk_ss(const lx2v_ctx *ctx, int M, int N, int K, int bt, int kgroup) {
+    if (ctx->split_mode != 2) return false;
+    const int pairs = ctx->num_sms / 2;
+    const long long tiles = (long long)((M + bt - 1) / bt) * ((N + 255) / 256);
+    const long long kg = ((K + 63) / 64) / kgroup;
+    return tiles * kg >= pairs;  // every pair needs at least one group
+}
+
 // Rows from which the two-pass linear (decode the weight once to bf16, then a
 // GEMM with both operands in shared memory) is the automatic choice for
 // quantized weights: below it the one-pass kernel's per-tile decode is
@@ -786,6 +801,13 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
         p.out_f32 = y->dtype == LX2V_F32;
         p.reduce = mods ? 1 : 0;
         p.kgroup = K % 128 == 0 ? 2 : 1;
+        if (use_streamk_ss(ctx, (int)rows, (int)N, (int)K, bt, p.kgroup)) {
+            s = ensure_sk_workspace(ctx, ctx->num_sms / 2, bt, &p.partials, &p.flags);
+            if (s) return s;
+            p.streamk = 1;
+            if (++ctx->sk_epoch <= 0) ctx->sk_epoch = 1;
+            p.epoch = ctx->sk_epoch;
+        }
         CUDA_TRY(ctx, gemm_ss_pair_launch(bt, p, ctx->num_sms, ctx->stream));
         ctx->launches++;
         return LX2V_OK;

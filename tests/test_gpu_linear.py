@@ -460,7 +460,8 @@ def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
 @pytest.mark.parametrize("fmt", ["fp8", "q8", "q4", "native"])
 @pytest.mark.parametrize("M,N,K,bt", [(4680, 1536, 1536, 256), (1000, 512, 8960, 256), (700, 640, 4480, 192),
                                       (2500, 1552, 704, 128)])
-def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt):
+@pytest.mark.parametrize("path", [4, 5])
+def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt, path):
     # tiles split over several CTA pairs, several partial tiles added into one
     # (1000 x 512 x 8960: ~10 pairs per tile), ragged M and N
     w, q = make_weight(fmt, N, K, seed=101 + K, oracle=oracle)
@@ -470,7 +471,7 @@ def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt):
     xb, bb = be.upload(x), be.upload(b)
     outs = {}
     try:
-        be.set_linear_path(4)
+        be.set_linear_path(path)
         be.set_token_tile(bt)
         for mode in (2, 1):
             be.set_split_mode(mode)
@@ -490,7 +491,8 @@ def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt):
     assert rel_l2(outs[(2, 0)][rows], want) <= REL_L2
 
 
-def test_stream_k_gated_residual_with_offsets(be, oracle):
+@pytest.mark.parametrize("path", [4, 5])
+def test_stream_k_gated_residual_with_offsets(be, oracle, path):
     M, N, K = 1800, 768, 4096
     w, q = make_weight("fp8", N, K, seed=111, oracle=oracle)
     dw = be.weight_fp8(q)
@@ -500,7 +502,7 @@ def test_stream_k_gated_residual_with_offsets(be, oracle):
     xb, mb = be.upload(x), be.upload(mods, F32)
     hb = be.upload(h0, F32)
     try:
-        be.set_linear_path(4)
+        be.set_linear_path(path)
         be.set_split_mode(2)
         be.linear_gate_residual(xb, 40, M, dw, None, Act.NONE, hb, 7, mb, 5)
     finally:
