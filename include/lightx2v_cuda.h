@@ -86,10 +86,22 @@ LX2V_API lx2v_status lx2v_buf_alloc(lx2v_ctx *ctx, size_t len, int dtype, lx2v_b
 /* Backend::upload: a new buffer holding `data` converted to `dtype`. */
 LX2V_API lx2v_status lx2v_buf_upload_f32(lx2v_ctx *ctx, const float *data, size_t len, int dtype,
                                 lx2v_buf **out);
-/* Backend::write: overwrite the first `len` elements. */
+/* Backend::write: overwrite the first `len` elements. Calls queued after it
+ * see the new contents. The copy itself runs on a second stream of the
+ * context and starts as soon as the last queued operation that used `buf`
+ * is done, so it overlaps kernels queued before it that do not touch `buf`.
+ * From pageable host memory `data` may be reused when the call returns; from
+ * page-locked memory the copy is asynchronous: keep `data` unchanged until
+ * the next lx2v_sync or blocking call. */
 LX2V_API lx2v_status lx2v_buf_write_f32(lx2v_ctx *ctx, lx2v_buf *buf, const float *data, size_t len);
 /* Backend::download: blocking read of the first `len` elements as f32. */
 LX2V_API lx2v_status lx2v_buf_download_f32(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len);
+/* No counterpart in the reference (its download always blocks): the same read
+ * queued on the context's stream without waiting for it. `out` holds the data
+ * after the next lx2v_sync (or blocking call); with page-locked `out` the
+ * copy overlaps host -> device writes queued later, which is how a caller
+ * pipelines consecutive steps. */
+LX2V_API lx2v_status lx2v_buf_download_f32_async(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len);
 /* Backend::buf_len. */
 LX2V_API lx2v_status lx2v_buf_len(lx2v_ctx *ctx, const lx2v_buf *buf, size_t *len);
 /* Element type and device address of a buffer (for tests and benchmarks). */

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <mutex>
 #include <string>
@@ -57,6 +58,15 @@ struct lx2v_ctx {
     std::vector<cudaEvent_t> event_pool;
     void *staging = nullptr;
     size_t staging_bytes = 0;
+    // Host -> device copies of lx2v_buf_write_f32 / upload run on their own
+    // stream, so that they overlap kernels queued before them: each copy
+    // waits only for the last kernel that used its destination, and the
+    // compute stream waits for the copy before anything queued after it.
+    cudaStream_t h2d = nullptr;
+    void *wstage = nullptr;            // f32 landing area of writes into bf16 buffers
+    size_t wstage_bytes = 0;
+    cudaEvent_t wstage_ev = nullptr;   // the last convert that read wstage
+    bool wstage_used = false;
     std::string last_err;
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
 };
@@ -65,6 +75,7 @@ struct lx2v_buf {
     void *ptr = nullptr;
     size_t len = 0;
     int dtype = LX2V_BF16;
+    cudaEvent_t last_use = nullptr;  // recorded on the compute stream after each op that touches the buffer
 };
 
 struct lx2v_weight {
@@ -98,6 +109,25 @@ static lx2v_status fail(lx2v_ctx *ctx, lx2v_status code, const char *fmt, ...) {
     } while (0)
 
 static size_t esize(int dtype) { return dtype == LX2V_F32 ? 4 : 2; }
+
+// Record that work just queued on the compute stream reads or writes `b`
+// (a later host -> device copy into `b` waits for this point).
+static cudaError_t note_use(lx2v_ctx *ctx, const lx2v_buf *b) {
+    if (!b) return cudaSuccess;
+    lx2v_buf *m = const_cast<lx2v_buf *>(b);
+    if (!m->last_use) {
+        cudaError_t e = cudaEventCreateWithFlags(&m->last_use, cudaEventDisableTiming);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaEventRecord(m->last_use, ctx->stream);
+}
+static cudaError_t note_uses(lx2v_ctx *ctx, std::initializer_list<const lx2v_buf *> bufs) {
+    for (const lx2v_buf *b : bufs) {
+        cudaError_t e = note_use(ctx, b);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 static lx2v_status enter(lx2v_ctx *ctx) {
     if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
@@ -247,6 +277,8 @@ extern "C" lx2v_status lx2v_init(int device, lx2v_ctx **out) {
     ctx->num_sms = prop.multiProcessorCount;
     cudaError_t e = cudaSetDevice(device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->wstage_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->err_dev, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->err_dev, 0, sizeof(int));
     if (e != cudaSuccess) {
@@ -277,7 +309,11 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
         cudaEventDestroy(p.b);
     }
     for (auto e : ctx->event_pool) cudaEventDestroy(e);
+    if (ctx->h2d) cudaStreamSynchronize(ctx->h2d);
     if (ctx->staging) cudaFree(ctx->staging);
+    if (ctx->wstage) cudaFree(ctx->wstage);
+    if (ctx->wstage_ev) cudaEventDestroy(ctx->wstage_ev);
+    if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
     if (ctx->dq_ws) cudaFree(ctx->dq_ws);
@@ -339,6 +375,7 @@ extern "C" lx2v_status lx2v_buf_alloc(lx2v_ctx *ctx, size_t len, int dtype, lx2v
     if (len) {
         cudaError_t e = cudaMalloc(&b->ptr, len * esize(dtype));
         if (e == cudaSuccess) e = cudaMemsetAsync(b->ptr, 0, len * esize(dtype), ctx->stream);
+        if (e == cudaSuccess) e = note_use(ctx, b);
         if (e != cudaSuccess) {
             if (b->ptr) cudaFree(b->ptr);
             delete b;
@@ -350,17 +387,43 @@ extern "C" lx2v_status lx2v_buf_alloc(lx2v_ctx *ctx, size_t len, int dtype, lx2v
     return LX2V_OK;
 }
 
+// Host -> device: the copy runs on the h2d stream once the last kernel that
+// used its destination is done (so it overlaps any other queued work), and
+// the compute stream waits for it before whatever is queued next. bf16
+// buffers land in f32 in `wstage` and are converted on the compute stream.
 static lx2v_status write_f32(lx2v_ctx *ctx, lx2v_buf *b, const float *data, size_t len) {
     if (len == 0) return LX2V_OK;
-    if (b->dtype == LX2V_F32) {
-        CUDA_TRY(ctx, cudaMemcpyAsync(b->ptr, data, len * 4, cudaMemcpyHostToDevice, ctx->stream));
-        return LX2V_OK;
+    void *dst = b->ptr;
+    if (b->dtype != LX2V_F32) {
+        if (ctx->wstage_bytes < len * 4) {
+            CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+            CUDA_TRY(ctx, cudaStreamSynchronize(ctx->h2d));
+            if (ctx->wstage) cudaFree(ctx->wstage);
+            ctx->wstage = nullptr;
+            ctx->wstage_bytes = 0;
+            ctx->wstage_used = false;
+            CUDA_TRY(ctx, cudaMalloc(&ctx->wstage, len * 4));
+            ctx->wstage_bytes = len * 4;
+        }
+        if (ctx->wstage_used) CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->wstage_ev, 0));
+        dst = ctx->wstage;
+    } else if (b->last_use) {
+        CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->h2d, b->last_use, 0));
     }
-    lx2v_status s = ensure_staging(ctx, len * 4);
-    if (s) return s;
-    CUDA_TRY(ctx, cudaMemcpyAsync(ctx->staging, data, len * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CUDA_TRY(ctx, convert_launch(ctx->staging, 1, b->ptr, 0, len, ctx->stream));
-    ctx->launches++;
+    cudaEvent_t done = nullptr;
+    CUDA_TRY(ctx, cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    cudaError_t e = cudaMemcpyAsync(dst, data, len * 4, cudaMemcpyHostToDevice, ctx->h2d);
+    if (e == cudaSuccess) e = cudaEventRecord(done, ctx->h2d);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, done, 0);
+    cudaEventDestroy(done);  // released once recorded work completes
+    CUDA_TRY(ctx, e);
+    if (b->dtype != LX2V_F32) {
+        CUDA_TRY(ctx, convert_launch(ctx->wstage, 1, b->ptr, 0, len, ctx->stream));
+        ctx->launches++;
+        CUDA_TRY(ctx, cudaEventRecord(ctx->wstage_ev, ctx->stream));
+        ctx->wstage_used = true;
+    }
+    CUDA_TRY(ctx, note_use(ctx, b));
     return LX2V_OK;
 }
 
@@ -391,6 +454,22 @@ extern "C" lx2v_status lx2v_buf_write_f32(lx2v_ctx *ctx, lx2v_buf *buf, const fl
     return write_f32(ctx, buf, data, len);
 }
 
+// Device -> host on the compute stream (after everything queued before).
+static lx2v_status queue_download(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len) {
+    if (len == 0) return LX2V_OK;
+    if (buf->dtype == LX2V_F32) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(out, buf->ptr, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    } else {
+        lx2v_status s = ensure_staging(ctx, len * 4);
+        if (s) return s;
+        CUDA_TRY(ctx, convert_launch(buf->ptr, 0, ctx->staging, 1, len, ctx->stream));
+        ctx->launches++;
+        CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->staging, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    CUDA_TRY(ctx, note_use(ctx, buf));
+    return LX2V_OK;
+}
+
 extern "C" lx2v_status lx2v_buf_download_f32(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len) {
     lx2v_status s = enter(ctx);
     if (s) return s;
@@ -398,20 +477,20 @@ extern "C" lx2v_status lx2v_buf_download_f32(lx2v_ctx *ctx, const lx2v_buf *buf,
     if (len > buf->len) return fail(ctx, LX2V_ERR_INVALID, "download of %zu elements from a buffer of %zu", len, buf->len);
     {
         OpScope ps(ctx, "download");
-        if (len) {
-            if (buf->dtype == LX2V_F32) {
-                CUDA_TRY(ctx, cudaMemcpyAsync(out, buf->ptr, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
-            } else {
-                s = ensure_staging(ctx, len * 4);
-                if (s) return s;
-                CUDA_TRY(ctx, convert_launch(buf->ptr, 0, ctx->staging, 1, len, ctx->stream));
-                ctx->launches++;
-                CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->staging, len * 4, cudaMemcpyDeviceToHost, ctx->stream));
-            }
-        }
+        s = queue_download(ctx, buf, out, len);
+        if (s) return s;
     }
     CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return check_device_error(ctx);
+}
+
+extern "C" lx2v_status lx2v_buf_download_f32_async(lx2v_ctx *ctx, const lx2v_buf *buf, float *out, size_t len) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!buf || (len && !out)) return fail(ctx, LX2V_ERR_INVALID, "null buffer or output");
+    if (len > buf->len) return fail(ctx, LX2V_ERR_INVALID, "download of %zu elements from a buffer of %zu", len, buf->len);
+    OpScope ps(ctx, "download_async");
+    return queue_download(ctx, buf, out, len);
 }
 
 extern "C" lx2v_status lx2v_buf_len(lx2v_ctx *ctx, const lx2v_buf *buf, size_t *len) {
@@ -446,6 +525,7 @@ extern "C" lx2v_status lx2v_buf_copy(lx2v_ctx *ctx, const lx2v_buf *src, size_t 
         CUDA_TRY(ctx, convert_launch(sp, src->dtype == LX2V_F32, dp, dst->dtype == LX2V_F32, len, ctx->stream));
         ctx->launches++;
     }
+    CUDA_TRY(ctx, note_uses(ctx, {src, dst}));
     return LX2V_OK;
 }
 
@@ -456,6 +536,7 @@ extern "C" void lx2v_buf_free(lx2v_ctx *ctx, lx2v_buf *buf) {
         cudaStreamSynchronize(ctx->stream);
     }
     if (buf->ptr) cudaFree(buf->ptr);
+    if (buf->last_use) cudaEventDestroy(buf->last_use);
     delete buf;
 }
 
@@ -701,7 +782,7 @@ static bool use_streamk(const lx2v_ctx *ctx, int M, int N, int K, int bt) {
     return split < 0.6 * whole;
 }
 
-static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf *x, size_t x_row,
+static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_buf *x, size_t x_row,
                                size_t rows, const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
                                size_t y_row, const lx2v_buf *mods, size_t gate) {
     if (!x || !w || !y) return fail(ctx, LX2V_ERR_INVALID, "null x, weight or output");
@@ -883,6 +964,17 @@ static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf
     return LX2V_OK;
 }
 
+// linear_queue, then the buffers it touched are marked used (for host -> device
+// copies queued later).
+static lx2v_status linear_impl(lx2v_ctx *ctx, const char *opname, const lx2v_buf *x, size_t x_row,
+                               size_t rows, const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
+                               size_t y_row, const lx2v_buf *mods, size_t gate) {
+    lx2v_status s = linear_queue(ctx, opname, x, x_row, rows, w, bias, act, y, y_row, mods, gate);
+    if (s) return s;
+    CUDA_TRY(ctx, note_uses(ctx, {x, bias, y, mods}));
+    return LX2V_OK;
+}
+
 extern "C" lx2v_status lx2v_linear(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
                                    const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
                                    size_t y_row) {
@@ -913,6 +1005,7 @@ extern "C" lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v
     CUDA_TRY(ctx, gate_residual_launch(h->ptr, h->dtype == LX2V_F32, a->ptr, a->dtype == LX2V_F32, g,
                                        mods->dtype == LX2V_F32, rows, dim, ctx->stream));
     ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {h, a, mods}));
     return LX2V_OK;
 }
 
@@ -1115,5 +1208,6 @@ extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, siz
     p.partials = (float *)((char *)scratch + LX2V_NOALLOC_FLAG_BYTES);
     CUDA_TRY(ctx, gemm_pair_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
     ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {x, bias, y}));
     return LX2V_OK;
 }

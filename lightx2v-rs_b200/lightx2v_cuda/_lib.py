@@ -46,6 +46,7 @@ SIGNATURES = {
     "lx2v_buf_upload_f32": (_st, [_vp, _vp, _sz, ctypes.c_int, _pp]),
     "lx2v_buf_write_f32": (_st, [_vp, _vp, _vp, _sz]),
     "lx2v_buf_download_f32": (_st, [_vp, _vp, _vp, _sz]),
+    "lx2v_buf_download_f32_async": (_st, [_vp, _vp, _vp, _sz]),
     "lx2v_buf_len": (_st, [_vp, _vp, ctypes.POINTER(_sz)]),
     "lx2v_buf_info": (_st, [_vp, _vp, ctypes.POINTER(ctypes.c_int), _pp]),
     "lx2v_buf_copy": (_st, [_vp, _vp, _sz, _vp, _sz, _sz]),

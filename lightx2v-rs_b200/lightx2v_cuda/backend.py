@@ -152,6 +152,11 @@ class CudaBackend:
     def download_ptr(self, buf: Buf, host_ptr: int, length: int):
         self._check(self._lib.lx2v_buf_download_f32(self._ctx, buf.handle, host_ptr, length))
 
+    def download_ptr_async(self, buf: Buf, host_ptr: int, length: int):
+        """download_ptr() queued without waiting: the host memory holds the data
+        after the next sync() (no reference counterpart; for pipelined steps)."""
+        self._check(self._lib.lx2v_buf_download_f32_async(self._ctx, buf.handle, host_ptr, length))
+
     def buf_len(self, buf: Buf) -> int:
         n = ctypes.c_size_t()
         self._check(self._lib.lx2v_buf_len(self._ctx, buf.handle, ctypes.byref(n)))

@@ -1,0 +1,119 @@
+"""Host <-> device transfers under overlap: lx2v_buf_write_f32 copies on a second
+stream that waits only for the last queued operation using the destination,
+and lx2v_buf_download_f32_async queues the read without blocking. These tests
+check that the ordering the reference's blocking Backend::write / download
+give (backend.rs:160-177) still holds: an operation queued before a write
+sees the old contents, one queued after it the new contents, and pipelined
+steps give the results of the same steps run one at a time.
+"""
+import numpy as np
+import pytest
+import torch
+
+from lightx2v_cuda import BF16, F32, Act, quant
+
+pytestmark = pytest.mark.gpu
+
+
+def _pinned(a):
+    t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).pin_memory()
+    return t, t.data_ptr()
+
+
+@pytest.mark.parametrize("xdt", [BF16, F32])
+def test_write_waits_for_earlier_readers_and_later_ops_see_it(be, oracle, xdt):
+    # a large x keeps the first linear busy while the write is queued
+    M, N, K = 4096, 4608, 1536
+    w = oracle.normal(301, N * K, 0.02)
+    dw = be.weight_q8(quant.Q8.quantize(w, N, K))
+    x0 = oracle.normal(302, M * K)
+    x1 = oracle.normal(303, M * K)
+    p1, ptr1 = _pinned(x1)
+    if xdt == F32:
+        # the tensor-core path takes bf16 x: route through a bf16 copy
+        xf = be.upload(x0, F32)
+        xb = be.alloc(M * K, BF16)
+        be.copy(xf, 0, xb, 0, M * K)
+        y0 = be.alloc(M * N, F32)
+        be.linear(xb, 0, M, dw, None, Act.NONE, y0, 0)
+        be.write_ptr(xf, ptr1, M * K)          # must not overtake the copy above
+        be.copy(xf, 0, xb, 0, M * K)
+    else:
+        xb = be.upload(x0, BF16)
+        y0 = be.alloc(M * N, F32)
+        be.linear(xb, 0, M, dw, None, Act.NONE, y0, 0)
+        be.write_ptr(xb, ptr1, M * K)          # must not overtake the linear above
+    y1 = be.alloc(M * N, F32)
+    be.linear(xb, 0, M, dw, None, Act.NONE, y1, 0)
+    got0, got1 = be.download(y0), be.download(y1)
+    # the same two products computed with nothing in flight
+    r0 = be.alloc(M * N, F32)
+    be.linear(be.upload(x0, BF16), 0, M, dw, None, Act.NONE, r0, 0)
+    r1 = be.alloc(M * N, F32)
+    be.linear(be.upload(x1, BF16), 0, M, dw, None, Act.NONE, r1, 0)
+    assert np.array_equal(got0, be.download(r0))
+    assert np.array_equal(got1, be.download(r1))
+    del p1
+
+
+def test_pipelined_steps_match_steps_run_one_at_a_time(be, oracle):
+    # the bench's end-to-end loop: per step write x and h from page-locked
+    # memory, four linears, read h back without blocking; h alternates
+    # between two device buffers so step i+1's upload overlaps step i
+    M, D, F = 1200, 768, 3072
+    # Q8 weights: the FP8 quantizer's NaN codes would make whole FFN rows NaN
+    lin = {name: (be.weight_q8(quant.Q8.quantize(oracle.normal(310 + i, n * k, 0.02), n, k)), n, k)
+           for i, (name, n, k) in enumerate([("qkv", 3 * D, D), ("out", D, D), ("ffn1", F, D), ("ffn2", D, F)])}
+    mods = be.upload(oracle.normal(320, 6 * D, 0.5))
+    steps = 4
+    xs = [oracle.normal(330 + s, M * D) for s in range(steps)]
+    hs = [oracle.normal(340 + s, M * D) for s in range(steps)]
+    xb = be.alloc(M * D, BF16)
+    qkv, tmp, hid = be.alloc(M * 3 * D), be.alloc(M * D), be.alloc(M * F)
+
+    def run(step_h, async_mode):
+        pins = [(_pinned(xs[s]), _pinned(hs[s])) for s in range(steps)]
+        outs = [torch.empty(M * D, dtype=torch.float32).pin_memory() for _ in range(steps)]
+        for s in range(steps):
+            hb = step_h[s % len(step_h)]
+            be.write_ptr(xb, pins[s][0][1], M * D)
+            be.linear(xb, 0, M, lin["qkv"][0], None, Act.NONE, qkv, 0)
+            be.linear(xb, 0, M, lin["out"][0], None, Act.NONE, tmp, 0)
+            be.linear(xb, 0, M, lin["ffn1"][0], None, Act.GELU_TANH, hid, 0)
+            be.write_ptr(hb, pins[s][1][1], M * D)
+            be.linear_gate_residual(hid, 0, M, lin["ffn2"][0], None, Act.NONE, hb, 0, mods, 5)
+            if async_mode:
+                be.download_ptr_async(hb, outs[s].data_ptr(), M * D)
+            else:
+                be.download_ptr(hb, outs[s].data_ptr(), M * D)
+        be.sync()
+        return [o.numpy().copy() for o in outs], be.download(qkv), be.download(tmp)
+
+    piped, pq, pt = run([be.alloc(M * D, F32), be.alloc(M * D, F32)], True)
+    seq, sq, st = run([be.alloc(M * D, F32)], False)
+    for s in range(steps):
+        assert np.array_equal(piped[s], seq[s], equal_nan=True), s
+    assert np.array_equal(pq, sq, equal_nan=True) and np.array_equal(pt, st, equal_nan=True)
+    # and the last step against the oracle on a few rows
+    rows = [0, 517, M - 1]
+    for r in rows:
+        x = xs[-1][r * D:(r + 1) * D]
+        h = hs[-1][r * D:(r + 1) * D]
+        wq = lambda name: be.weight_dequant_f32(lin[name][0]).reshape(lin[name][1], lin[name][2])  # noqa: E731
+        a = oracle.linear(x, 1, wq("ffn1").reshape(-1), F, D, act=1, threads=4)
+        f2 = oracle.linear(a.reshape(-1), 1, wq("ffn2").reshape(-1), D, F, threads=4)
+        want = oracle.gate_residual(h.reshape(1, D).copy(), f2, 1, D, be.download(mods), 5)
+        got = piped[-1].reshape(M, D)[r]
+        want = want.reshape(-1)
+        rel = np.linalg.norm(got - want) / np.linalg.norm(want - h)
+        assert rel <= 2e-2, (r, rel)
+
+
+def test_async_download_of_bf16_buffer(be, oracle):
+    n = 1 << 20
+    v = oracle.normal(350, n)
+    b = be.upload(v, BF16)
+    out = torch.empty(n, dtype=torch.float32).pin_memory()
+    be.download_ptr_async(b, out.data_ptr(), n)
+    be.sync()
+    assert np.array_equal(out.numpy(), be.download(b))
