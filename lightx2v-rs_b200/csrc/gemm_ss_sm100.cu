@@ -17,8 +17,9 @@
 // [BT/2 r, BT/2 r + BT/2) of x (B) into its own shared memory, both 128-byte
 // swizzled K-major; the leader issues the MMAs. Accumulators: ACC buffers of
 // BT TMEM columns, so the epilogue of one tile overlaps the k-loop of the
-// next. Persistent grid of CTA pairs, tiles strided over pairs, token tile
-// fastest (neighbouring pairs share the weight tile in L2).
+// next. Persistent grid of CTA pairs, tiles strided over pairs, feature tile
+// fastest (pairs running at the same time share x tiles; measured 3 % faster
+// than token tile fastest on the 1.3B chunk's QKV and FFN2).
 //
 // Warp roles (384 threads per CTA): warp 0 TMA producer (both CTAs), warp 1
 // MMA issuer (leader CTA) and TMEM allocation, warps 4-11 epilogue (both
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             for (int j = 0; j < n_seg && ok; ++j) {
                 int t, kb0, kb1;
                 work.seg(j, t, kb0, kb1);
-                const int mt = t % n_mt, ft = t / n_mt;
+                const int mt = t / n_ft, ft = t % n_ft;
                 const int row0 = ft * 256 + (int)rank * 128;
                 const int xrow = p.x_row + mt * BT + (int)rank * (BT / 2);
                 for (int gr = kb0; gr < kb1; ++gr) {
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
         for (int j = 0; j < n_seg; ++j) {
             int t, kb0, kb1;
             work.seg(j, t, kb0, kb1);
-            const int mt = t % n_mt, ft = t / n_mt;
+            const int mt = t / n_ft, ft = t % n_ft;
             SkIO io;
             int n_add = 0;
             if (!SK) {
