@@ -13,6 +13,7 @@ struct alignas(64) GemmParams {
     CUtensorMap tmap_w;  // weight codes [N rows], box {one 64-wide k-block, 128 rows}
     CUtensorMap tmap_s;  // scale words [G][N] (4 bytes each), box {128 rows, sgrp groups}
     CUtensorMap tmap_f;  // FP8 block flags [ceil(K/32)][N] bytes, box {128 rows, 2}
+    CUtensorMap tmap_y;  // two-pass kernel with tma_y: y [y_row + M][N] (bf16 or f32), box {32, 32}
     void *y;                  // output (or h for the gated residual)
     const uint8_t *codes;     // weight codes in the reference layout (dequant.cuh)
     const float *scales_t;    // Q8/FP8 scales, [G][N]
@@ -39,6 +40,7 @@ struct alignas(64) GemmParams {
     int streamk;
     int epoch;
     int kgroup;               // pair kernel: k-blocks per MMA group (1, or 2 when K % 128 == 0)
+    int tma_y;                // two-pass kernel: y written by TMA tensor stores (reduce-add for f32 residuals)
     float *partials;
     int *flags;
 };

@@ -139,26 +139,43 @@ __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t 
 }
 
 // The work of one CTA pair as a list of segments: k-blocks [kb0, kb1) of a
-// tile. Whole tiles: tiles pair, pair + npairs, ... Stream-K: the
-// n_tiles * KB k-blocks split into npairs equal contiguous ranges; a range
-// may start and end inside a tile.
+// tile. Whole tiles: tiles pair, pair + npairs, ... Stream-K: the first `dp`
+// tiles as whole tiles in that order (dp is a multiple of npairs: full waves,
+// so the pairs running at the same time keep sharing operand tiles in L2),
+// then the remaining tiles' k-blocks split into npairs equal contiguous
+// ranges [lo, hi) (counted from tile 0); a range may start and end inside a
+// tile. dp = 0 splits everything.
 struct PairWork {
     long long lo = 0, hi = 0;  // stream-K k-block range
     int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
+    int dp = 0, my_dp = 0;     // whole tiles before the split range (all pairs / this pair)
     bool sk = false;
+    __device__ __forceinline__ void init_split(int n_tiles, int dp_tiles) {
+        dp = dp_tiles;
+        my_dp = pair < dp ? (dp - 1 - pair) / npairs + 1 : 0;
+        const long long rem = (long long)(n_tiles - dp) * KB;
+        lo = (long long)dp * KB + rem * pair / npairs;
+        hi = (long long)dp * KB + rem * (pair + 1) / npairs;
+    }
+    // first k-block (counted from tile 0) of pair q's split range
+    __device__ __forceinline__ long long split_start(int n_tiles, int q) const {
+        return (long long)dp * KB + (long long)(n_tiles - dp) * KB * q / npairs;
+    }
     __device__ __forceinline__ int count() const {
         if (!sk) return my_tiles;
-        return hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0;
+        return my_dp + (hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0);
     }
-    __device__ __forceinline__ long long total_kb() const { return sk ? hi - lo : (long long)my_tiles * KB; }
+    __device__ __forceinline__ long long total_kb() const {
+        return sk ? (long long)my_dp * KB + (hi - lo) : (long long)my_tiles * KB;
+    }
     __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
-        if (!sk) {
+        if (!sk || idx < my_dp) {
             tile = pair + idx * npairs;
             kb0 = 0;
             kb1 = KB;
             return;
         }
-        const long long t = lo / KB + idx;
+        const long long t = lo / KB + (idx - my_dp);
         const long long start = lo > t * KB ? lo : t * KB;
         const long long end = hi < (t + 1) * KB ? hi : (t + 1) * KB;
         tile = (int)t;

@@ -105,8 +105,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
     work.my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
     work.sk = SK;
     const long long units = (long long)n_tiles * KB;
-    work.lo = units * pair / npairs;
-    work.hi = units * (pair + 1) / npairs;
+    work.init_split(n_tiles, 0);
     const int n_seg = work.count();
     const int total_gr = (int)work.total_kb();   // groups this pair runs, over all its segments
     const int total_kb = total_gr * GRP;          // k-blocks

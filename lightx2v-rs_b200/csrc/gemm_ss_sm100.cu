@@ -24,8 +24,11 @@
 // Warp roles (384 threads per CTA): warp 0 TMA producer (both CTAs), warp 1
 // MMA issuer (leader CTA) and TMEM allocation, warps 4-11 epilogue (both
 // CTAs): warp w reads TMEM lanes 32 (w % 4) .. + 31 of token columns
-// [BT/2 h, BT/2 h + BT/2), h = (w - 4) / 4, and stores straight from
-// registers (epilogue_direct), so shared memory holds only the ring.
+// [BT/2 h, BT/2 h + BT/2), h = (w - 4) / 4. Per 32-token chunk a warp puts
+// its 32 features x 32 tokens into its own shared-memory box and one lane
+// writes the box with a TMA tensor store (a TMA reduce-add for the f32
+// gated residual): stores of two bytes per thread from registers measured
+// ~6 us of a ~8 us tile epilogue, as long as the k-loop of a K = 1536 tile.
 //
 // Synchronisation (all waits bounded, ptx.cuh), per group of GRP k-blocks:
 //   full[g]      leader; 1 arrival (the leader producer's expect_tx) plus the
@@ -42,12 +45,17 @@
 
 namespace lx2v {
 
+constexpr int SS_EPI_WARPS = 8;
+constexpr int SS_STG_BOX = 32 * 32 * 4;                   // bytes of one warp's staging box
+constexpr int SS_STG_BYTES = SS_EPI_WARPS * SS_STG_BOX;
+
 template <int BT, int ACC, int SS>
 struct SsCfg {
     static constexpr int XH_BYTES = (BT / 2) * BK * 2;  // this CTA's half of the x tile
     static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's 128 weight rows
     static constexpr int OFF_A = SS * XH_BYTES;
-    static constexpr int OFF_BAR = OFF_A + SS * A_BYTES;
+    static constexpr int OFF_STG = OFF_A + SS * A_BYTES;      // per epilogue warp: one 32 x 32 f32 box
+    static constexpr int OFF_BAR = OFF_STG + SS_STG_BYTES;
     static constexpr int NUM_BARS = 2 * SS + 2 * ACC + 1;
     static constexpr int SMEM_BYTES = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
     static_assert(ACC * BT <= TMEM_COLS, "TMEM budget");
@@ -56,7 +64,6 @@ struct SsCfg {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-constexpr int SS_EPI_WARPS = 8;
 constexpr int SS_THREADS = 32 * (4 + SS_EPI_WARPS);
 
 struct SsCtl {
@@ -79,7 +86,8 @@ struct SkIO {
 // them; each store of a warp covers one token's 32 consecutive features.
 template <bool SK>
 __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t (&v)[32], int tok0, int f, bool fok,
-                                           float2 bias2, float2 gate2, const SkIO &io, int col0, int fl) {
+                                           float2 bias2, float2 gate2, const SkIO &io, int col0, int fl,
+                                           uint8_t *stg, int lane) {
     const int nt = min(32, p.M - tok0);
     const int64_t n = p.N;
     const int64_t off0 = ((int64_t)p.y_row + tok0) * n + f;
@@ -110,6 +118,31 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t 
         if (p.gate) t = __fmul2_rn(t, gate2);
         o[2 * i] = t.x;
         o[2 * i + 1] = t.y;
+    }
+    if (p.tma_y) {
+        // [32 tokens][32 features] row-major box, as the tensor map reads it
+        if (lane == 0) bulk_wait_read<0>();  // the previous box has been read out
+        __syncwarp();
+        if (p.out_f32) {
+            float *b = reinterpret_cast<float *>(stg);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) b[j * 32 + lane] = o[j];
+        } else {
+            __nv_bfloat16 *b = reinterpret_cast<__nv_bfloat16 *>(stg);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) b[j * 32 + lane] = __float2bfloat16_rn(o[j]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int c0 = f - lane, c1 = p.y_row + tok0;  // c0: this warp's first feature, a multiple of 32
+        if (lane == 0 && c0 < p.N) {
+            // rows past y_row + M and columns past N fall outside the map and are not written
+            if (p.reduce) tma_reduce_add_2d(&p.tmap_y, stg, c0, c1);
+            else tma_store_2d(&p.tmap_y, stg, c0, c1);
+            bulk_commit();
+        }
+        __syncwarp();
+        return;
     }
     if (p.out_f32) {
         float *dst = reinterpret_cast<float *>(p.y) + off0;
@@ -149,7 +182,8 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t 
 // runs once the last load has completed.
 template <bool SK, typename Release>
 __device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t acc_addr, int ntok, int f, int m0,
-                                                Release release, const SkIO &io, int col0, int fl) {
+                                                Release release, const SkIO &io, int col0, int fl, uint8_t *stg,
+                                                int lane) {
     const bool fok = f < p.N;
     float bias_f = 0.0f, gate_f = 1.0f;
     if (fok) {
@@ -166,12 +200,12 @@ __device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t ac
         tmem_wait_ld_regs(a);
         if (c + 1 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 1) * 32), b);
         else release();
-        store_chunk<SK>(p, a, m0 + c * 32, f, fok, bias2, gate2, io, col0 + c * 32, fl);
+        store_chunk<SK>(p, a, m0 + c * 32, f, fok, bias2, gate2, io, col0 + c * 32, fl, stg, lane);
         if (c + 1 < nld) {
             tmem_wait_ld_regs(b);
             if (c + 2 < nld) tmem_ld_32x32b_x32(acc_addr + (uint32_t)((c + 2) * 32), a);
             else release();
-            store_chunk<SK>(p, b, m0 + (c + 1) * 32, f, fok, bias2, gate2, io, col0 + (c + 1) * 32, fl);
+            store_chunk<SK>(p, b, m0 + (c + 1) * 32, f, fok, bias2, gate2, io, col0 + (c + 1) * 32, fl, stg, lane);
         }
     }
 }
@@ -205,9 +239,8 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
     work.npairs = npairs;
     work.my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
     work.sk = SK;
-    const long long units = (long long)n_tiles * KG;
-    work.lo = units * pair / npairs;
-    work.hi = units * (pair + 1) / npairs;
+    // stream-K: full waves of whole tiles first, the rest split
+    work.init_split(n_tiles, (n_tiles / npairs) * npairs);
     const int n_seg = work.count();
     int *err = p.err;
     const uint64_t lim = p.wait_limit_ns;
@@ -321,7 +354,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             } else if (kb1 < KG) {
                 // the head of a split tile: the pairs after this one hold the rest
                 const long long tile_end = (long long)(t + 1) * KG;
-                while (pair + 1 + n_add < npairs && units * (pair + 1 + n_add) / npairs < tile_end) ++n_add;
+                while (pair + 1 + n_add < npairs && work.split_start(n_tiles, pair + 1 + n_add) < tile_end) ++n_add;
             }
             int ok = 1;
             if (lane == 0) {
@@ -353,7 +386,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             if (m0 < p.M) {
                 const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT + half * (BT / 2));
                 epilogue_direct<SK>(p, acc_addr, BT / 2, ft * 256 + (int)rank * 128 + q * 32 + lane, m0, release, io,
-                                    half * (BT / 2), q * 32 + lane);
+                                    half * (BT / 2), q * 32 + lane, smem + C::OFF_STG + wi * SS_STG_BOX, lane);
             } else {
                 release();  // no token of this half exists
             }
@@ -364,6 +397,8 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             }
             ab.next<ACC>();
         }
+        if (lane == 0) bulk_wait<0>();  // this warp's tensor stores have completed
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -380,7 +415,7 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
 // chunk's linears), but not at the price of single k-block groups (7 stages
 // of one k-block measured up to 10 % slower than 6 in groups of two).
 constexpr int ss_stages(int bt) {
-    const int budget = 227 * 1024 - 1024 - 512;
+    const int budget = 227 * 1024 - 1024 - 512 - SS_STG_BYTES;
     const int stage = (bt / 2) * BK * 2 + 128 * BK * 2;
     const int n = budget / stage > 8 ? 8 : budget / stage;
     return n - n % 2;

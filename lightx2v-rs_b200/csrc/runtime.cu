@@ -749,12 +749,16 @@ static lx2v_status make_map(lx2v_ctx *ctx, CUtensorMap *map, const void *base, C
 // read per pair. With several waves of tiles it measured slower than whole
 // tiles on B200 (FFN2 of the 1.3B chunk: 762 vs 804 TFLOP/s), so it is only
 // taken when it at least shortens the critical path by 40%.
-// Stream-K for the two-pass kernel, on request only (lx2v_set_split_mode 2).
-// It balances the 1.3B chunk's N = 1536 linears (114 tiles on 74 pairs, 1.54
-// waves) but measured slower on B200 (out 431 vs 614, FFN2 1023 vs 1076
-// TFLOP/s): the k-loop is bound by L2 traffic that all pairs share, which
-// idle pairs in a short last wave do not waste, while the partial tiles add
-// to it.
+// Stream-K for the two-pass kernel, on request only (lx2v_set_split_mode 2):
+// full waves of whole tiles, then the remaining tiles' k-blocks spread evenly
+// over all pairs (PairWork::init_split). It would balance the 1.3B chunk's
+// N = 1536 linears (114 tiles on 74 pairs) but measured slower on B200 (out
+// 423 vs 654, FFN2 1058 vs 1132 TFLOP/s): the partial tiles go through
+// per-thread global stores and loads, the traffic the tensor-store epilogue
+// avoids, and they sit on the critical path at the end of each pair's work.
+// (Splitting every tile into one contiguous range per pair was slower still:
+// pairs running at the same time then touch x tiles spread over the whole
+// output, which do not fit in L2 together.)
 static bool use_streamk_ss(const lx2v_ctx *ctx, int M, int N, int K, int bt, int kgroup) {
     if (ctx->split_mode != 2) return false;
     const int pairs = ctx->num_sms / 2;
@@ -882,6 +886,15 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
         p.out_f32 = y->dtype == LX2V_F32;
         p.reduce = mods ? 1 : 0;
         p.kgroup = K % 128 == 0 ? 2 : 1;
+        // y through TMA tensor stores (reduce-add for an f32 residual); a
+        // bf16 residual keeps the kernel's per-element reductions
+        if (!(p.reduce && !p.out_f32)) {
+            s = make_map(ctx, &p.tmap_y, y->ptr,
+                         p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         p.out_f32 ? 4 : 2, N, y_row + rows, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (s) return s;
+            p.tma_y = 1;
+        }
         if (use_streamk_ss(ctx, (int)rows, (int)N, (int)K, bt, p.kgroup)) {
             s = ensure_sk_workspace(ctx, ctx->num_sms / 2, bt, &p.partials, &p.flags);
             if (s) return s;
