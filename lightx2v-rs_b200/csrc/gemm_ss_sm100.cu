@@ -265,6 +265,13 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
+    // Launched as a programmatic dependent: everything above overlapped the
+    // previous kernel (the weight decode); from here on this kernel reads its
+    // output (and x, y written earlier in the stream). Once past the wait,
+    // the next kernel in the stream may start (the next linear's decode,
+    // which touches nothing this one reads).
+    griddep_wait();
+    griddep_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -429,11 +436,13 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
     const int smem = C::SMEM_BYTES;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(SS_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -454,6 +463,7 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
     const long long work = SK ? (long long)n_tiles * (((p.K + BK - 1) / BK) / GRP) : n_tiles;
     const int pairs = work < max_pairs ? (int)work : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 

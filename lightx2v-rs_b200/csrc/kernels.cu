@@ -8,8 +8,10 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstring>
 #include "dequant.cuh"
 #include "gemm.h"
+#include "ptx.cuh"
 
 namespace lx2v {
 
@@ -108,8 +110,14 @@ __global__ void dequant_elems_kernel(WeightView w, float *out) {
 // choosing the hardware, fixed-up or reference decode), so both kinds of
 // kernel multiply identical operands. Thread = one 16-value unit; consecutive
 // threads take consecutive units of a row (16-byte code loads, 32-byte stores).
+// Launched as a programmatic dependent of the previous kernel in the stream:
+// it reads only the weight, so it runs beside that kernel's last tiles, lets
+// the GEMM that consumes it launch (and set up) right away, and before
+// exiting waits for the previous kernel, so that whatever follows this pass
+// in the stream also follows everything before it.
 template <int FMT>
 __global__ void __launch_bounds__(256) dequant_bf16_kernel(WeightView w, __nv_bfloat16 *out) {
+    griddep_launch_dependents();
     const int units_per_row = w.k / 16;
     const int64_t total = (int64_t)w.n * units_per_row;
     for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
@@ -131,6 +139,7 @@ __global__ void __launch_bounds__(256) dequant_bf16_kernel(WeightView w, __nv_bf
         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
         dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
     }
+    griddep_wait();
 }
 
 cudaError_t dequant_bf16_launch(int fmt, const uint8_t *codes, const float *scales_t, const uint32_t *sz_t,
@@ -139,13 +148,21 @@ cudaError_t dequant_bf16_launch(int fmt, const uint8_t *codes, const float *scal
     WeightView w{fmt, N, K, group, codes, scales_t, sz_t, flags};
     if ((size_t)N * K == 0) return cudaSuccess;
     if (fmt == FMT_BF16 || !unit_path_ok(fmt, K, group)) return cudaErrorInvalidValue;
-    const int g = grid_for((size_t)N * K / 16, 256);
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid_for((size_t)N * K / 16, 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (fmt) {
-        case FMT_Q8: dequant_bf16_kernel<FMT_Q8><<<g, 256, 0, st>>>(w, out); break;
-        case FMT_Q4: dequant_bf16_kernel<FMT_Q4><<<g, 256, 0, st>>>(w, out); break;
-        default: dequant_bf16_kernel<FMT_FP8><<<g, 256, 0, st>>>(w, out); break;
+        case FMT_Q8: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_Q8>, w, out);
+        case FMT_Q4: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_Q4>, w, out);
+        default: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_FP8>, w, out);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scales_t,

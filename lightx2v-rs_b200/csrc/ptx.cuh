@@ -99,6 +99,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+// ---- programmatic dependent launch ----------------------------------------
+// Wait until the grids this one depends on (the previous kernel in the
+// stream, when launched with programmatic stream serialization) have
+// completed and their memory is visible; a no-op otherwise.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel in the stream launch once every CTA of this grid has
+// executed this (or exited).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- cluster (CTA pair) ----------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

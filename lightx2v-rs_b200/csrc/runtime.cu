@@ -46,8 +46,12 @@ struct lx2v_ctx {
     size_t sk_ws_bytes = 0;
     int sk_epoch = 0;
     float *gemv_ws = nullptr;    // few-token kernel: split-K partials + arrival counters
-    void *dq_ws = nullptr;       // two-pass linear: the weight decoded to bf16
+    // Two-pass linear: the weight decoded to bf16, in two buffers used in
+    // turn (a call's decode runs while the previous call's GEMM still reads
+    // the other one).
+    void *dq_ws[2] = {nullptr, nullptr};
     size_t dq_ws_bytes = 0;
+    int dq_next = 0;
     size_t gemv_ws_floats = 0;
     int *gemv_arrivals = nullptr;
     size_t gemv_tiles = 0;
@@ -227,17 +231,24 @@ static lx2v_status ensure_gemv_workspace(lx2v_ctx *ctx, int N, int K) {
     return LX2V_OK;
 }
 
-// Two-pass linear workspace: one bf16 [N][K] weight (grow-only; a call
-// reuses it once the previous call's GEMM has read it, by stream order).
+// Two-pass linear workspace: two bf16 [N][K] buffers (grow-only). The
+// decode of call n writes buffer n % 2 while the GEMM of call n - 1 may
+// still read the other; the GEMM of call n - 2, the last reader of buffer
+// n % 2, has completed by then (each decode waits for its predecessor in the
+// stream before it exits, and each GEMM for its decode before it lets the
+// next kernel start).
 static lx2v_status ensure_dq_workspace(lx2v_ctx *ctx, size_t bytes) {
     if (ctx->dq_ws_bytes >= bytes) return LX2V_OK;
-    if (ctx->dq_ws) {
+    if (ctx->dq_ws[0] || ctx->dq_ws[1]) {
         CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-        cudaFree(ctx->dq_ws);
-        ctx->dq_ws = nullptr;
+        for (void *&b : ctx->dq_ws) {
+            if (b) cudaFree(b);
+            b = nullptr;
+        }
         ctx->dq_ws_bytes = 0;
     }
-    CUDA_TRY(ctx, cudaMalloc(&ctx->dq_ws, bytes));
+    CUDA_TRY(ctx, cudaMalloc(&ctx->dq_ws[0], bytes));
+    CUDA_TRY(ctx, cudaMalloc(&ctx->dq_ws[1], bytes));
     ctx->dq_ws_bytes = bytes;
     return LX2V_OK;
 }
@@ -316,7 +327,8 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
-    if (ctx->dq_ws) cudaFree(ctx->dq_ws);
+    for (void *b : ctx->dq_ws)
+        if (b) cudaFree(b);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -857,11 +869,12 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
         if (w->fmt != LX2V_W_BF16) {
             lx2v_status s = ensure_dq_workspace(ctx, N * K * 2);
             if (s) return s;
+            void *buf = ctx->dq_ws[ctx->dq_next];
+            ctx->dq_next ^= 1;
             CUDA_TRY(ctx, dequant_bf16_launch(w->fmt, (const uint8_t *)w->codes, w->scales_t, w->sz_t, w->flags,
-                                              (int)N, (int)K, (int)w->group, (__nv_bfloat16 *)ctx->dq_ws,
-                                              ctx->stream));
+                                              (int)N, (int)K, (int)w->group, (__nv_bfloat16 *)buf, ctx->stream));
             ctx->launches++;
-            wa = ctx->dq_ws;
+            wa = buf;
         }
         GemmParams p;
         memset(&p, 0, sizeof p);
