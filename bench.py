@@ -442,6 +442,129 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------------
+def config_arm(args, local_rank: int):
+    """The other BASELINE configs as single-GPU parity/throughput cases, one JSON
+    line per shape: C1 (Q8 FFN up-projection, M = 1560) and the C3 Q4 sweep
+    (M in {1, 16, 256, 1560, 4680, 18720} at K x N = 1536 x 8960 and
+    8960 x 1536). Device-resident inputs, one CUDA-event pair per call on the
+    library's stream, L2 flushed (256 MB write) before every call outside the
+    timed region. M <= 16 is judged against HBM bandwidth (weight bytes + x +
+    y per call), larger M against the bf16 dense tensor peak."""
+    import torch
+    from lightx2v_cuda import BF16, F32, CudaBackend, quant, rng
+
+    torch.cuda.set_device(local_rank)
+    be = CudaBackend(local_rank)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    peak, hbm, src = measured_peaks()
+    if args.config == "c1":
+        cases = [("q8", 1560, 1536, 8960)]
+    else:
+        cases = [("q4", m, k, n) for (k, n) in ((1536, 8960), (8960, 1536))
+                 for m in (1, 16, 256, 1560, 4680, 18720)]
+    weights, hostq = {}, {}
+    for fmt, m, k, n in cases:
+        if (fmt, k, n) in weights:
+            continue
+        w = rng.normal(7 + k, n * k, 0.02)
+        if fmt == "q8":
+            q = quant.Q8.quantize(w, n, k)
+            wbytes = n * k + n * (k // q.group) * 4
+            weights[(fmt, k, n)] = (be.weight_q8(q), wbytes, "Q8 (reference quantizer)")
+        else:
+            # HQQ refinement changes the scale/zero values, not the packed
+            # format or the kernel's work; skipped to keep the run short
+            q = quant.Q4.quantize(w, n, k, 64, False)
+            wbytes = n * k // 2 + n * (k // 64) * 4
+            weights[(fmt, k, n)] = (be.weight_q4(q), wbytes, "Q4 group 64 (reference quantizer, HQQ off)")
+        hostq[(fmt, k, n)] = q
+    for fmt, m, k, n in cases:
+        dw, wbytes, wdesc = weights[(fmt, k, n)]
+        xb = be.upload(rng.normal(11, m * k))
+        bb = be.upload(rng.normal(12, n, 0.01), F32)
+        y_f32 = fmt == "q8"
+        yb = be.alloc(m * n, F32 if y_f32 else BF16)
+        for _ in range(max(args.warmup, 3)):
+            be.linear(xb, 0, m, dw, bb, 0, yb, 0)
+        be.sync()
+        evs = []
+        steps = args.steps if m < 4680 else max(3, args.steps // 4)
+        for _ in range(steps):
+            with torch.cuda.stream(ext):
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(ext)
+            be.linear(xb, 0, m, dw, bb, 0, yb, 0)
+            b.record(ext)
+            evs.append((a, b))
+        be.sync()
+        ms = float(np.median([a.elapsed_time(b) for a, b in evs]))
+        flops = 2.0 * m * n * k
+        nbytes = wbytes + m * k * 2 + m * n * (4 if y_f32 else 2) + n * 4
+        tflops = flops / (ms * 1e-3) / 1e12
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        small = m <= 16
+        line = {"config": args.config, "workload": f"{fmt} linear M={m} K={k} N={n}", "weights": wdesc,
+                "ms": ms, "tflops": tflops, "gbs": gbs, "steps": steps, "data": "synthetic",
+                "l2": "flushed (256 MB write) before every call, outside the timed region",
+                "path": "few-token kernel" if small else ("two-pass (decode + gemm_ss_pair_kernel)"
+                                                          if m >= 1024 else "tensor-core single-CTA kernel"),
+                "roofline": {"bound": "hbm" if small else "tensor",
+                             "achieved": gbs if small else tflops,
+                             "peak": hbm if small else peak, "unit": "GB/s" if small else "TFLOP/s",
+                             "frac": (gbs / hbm) if small else (tflops / peak), "peak_source": src,
+                             "bytes_per_call": nbytes}}
+        if small and fmt == "q4" and (fmt, 8960, 1536) in hostq and (fmt, 1536, 8960) in hostq and k == 1536:
+            line["chain"] = q4_chain(be, ext, hostq, m, hbm)
+        print(json.dumps(line), flush=True)
+        del xb, bb, yb
+
+
+def q4_chain(be, ext, hostq, m, hbm):
+    """Sustained few-token throughput: a dependent chain of 40 Q4 linears
+    alternating 1536 -> 8960 and 8960 -> 1536 (each reads the previous one's
+    output, as consecutive layers of a decode step do), over 20 device copies
+    of each weight (310 MB of weights, more than L2 holds, so every launch
+    streams its weights from HBM), replayed as one CUDA graph."""
+    import torch
+    from lightx2v_cuda import BF16, rng
+    ups = [be.weight_q4(hostq[("q4", 1536, 8960)]) for _ in range(20)]
+    downs = [be.weight_q4(hostq[("q4", 8960, 1536)]) for _ in range(20)]
+    a_buf = be.upload(rng.normal(21, m * 1536), BF16)
+    b_buf = be.alloc(m * 8960, BF16)
+
+    def chain():
+        for i in range(20):
+            be.linear(a_buf, 0, m, ups[i], None, 0, b_buf, 0)
+            be.linear(b_buf, 0, m, downs[i], None, 0, a_buf, 0)
+
+    chain()
+    be.sync()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=ext):
+        chain()
+    with torch.cuda.stream(ext):  # replay() launches on the current stream
+        for _ in range(3):
+            g.replay()
+        torch.cuda.current_stream().synchronize()
+        evs = []
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ext)
+            g.replay()
+            e1.record(ext)
+            evs.append((e0, e1))
+    be.sync()
+    ms = float(np.median([e0.elapsed_time(e1) for e0, e1 in evs]))
+    wbytes = 20 * (8960 * 1536 // 2 + 8960 * (1536 // 64) * 4) * 2
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    del g
+    return {"launches": 40, "ms": ms, "us_per_launch": ms * 1e3 / 40, "weight_gbs": gbs, "frac_hbm": gbs / hbm,
+            "note": "one CUDA graph of 40 dependent linears; weight bytes only in the GB/s"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -450,12 +573,17 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
+                    help="c2 (default): the headline FP8 linear set; c1 / c3: the other configs, one line per shape")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+    elif args.config != "c2":
+        if rank == 0:
+            config_arm(args, local_rank)
     else:
         cuda_arm(args, rank, world, local_rank)
 

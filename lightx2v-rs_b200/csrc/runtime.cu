@@ -784,6 +784,11 @@ static bool use_streamk_ss(const lx2v_ctx *ctx, int M, int N, int K, int bt, int
 // quantized weights: below it the one-pass kernel's per-tile decode is
 // cheaper than the extra pass over N x K.
 static constexpr int TWO_PASS_MIN_ROWS = 1024;
+// ... and below that, when the call has so few 256 x 256 output tiles that
+// most SMs idle whatever the kernel (measured on B200, K = 8960, N = 1536:
+// 135 vs 94 TFLOP/s at 256 rows, 270 vs 226 at 512 rows; with N = 8960 the
+// one-pass kernels stay ahead).
+static constexpr size_t TWO_PASS_MAX_FEW_TILES = 24;
 
 static bool use_streamk(const lx2v_ctx *ctx, int M, int N, int K, int bt) {
     if (ctx->split_mode == 1) return false;
@@ -844,7 +849,10 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
     int path = ctx->path;
     if (path == 0) {
         if (rows <= 16 && gemv_ok) path = 2;
-        else if (ss_ok && N >= 256 && rows >= (w->fmt == LX2V_W_BF16 ? 512u : (size_t)TWO_PASS_MIN_ROWS)) path = 5;
+        else if (ss_ok && N >= 256 &&
+                 (rows >= (w->fmt == LX2V_W_BF16 ? 512u : (size_t)TWO_PASS_MIN_ROWS) ||
+                  ((rows + 255) / 256) * ((N + 255) / 256) <= TWO_PASS_MAX_FEW_TILES))
+            path = 5;
         else if (tc_ok) path = rows >= 512 && N >= 256 ? 4 : 1;
         else path = 3;
     }
