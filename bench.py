@@ -565,6 +565,73 @@ def q4_chain(be, ext, hostq, m, hbm):
             "note": "one CUDA graph of 40 dependent linears; weight bytes only in the GB/s"}
 
 
+# ---------------------------------------------------------------------------------------------
+def tpffn_arm(args, rank: int, world: int, local_rank: int):
+    """The chunk's FFN (M = 4680, 1536 -> 8960 GELU -> 1536 + gated residual, Q8)
+    tensor-parallel over the torchrun ranks (lightx2v_cuda/tp.py: FFN1
+    column-split, FFN2 row-split, one NCCL all-reduce through the C ABI):
+    strong scaling, the same total work at every N. Time per step = max over
+    ranks of CUDA-event times on each library stream, L2 flushed before every
+    step outside the timed region."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from lightx2v_cuda import BF16, F32, CudaBackend, quant, rng
+    from lightx2v_cuda.tp import TensorParallelFFN
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))  # id exchange and timing max
+    be = CudaBackend(local_rank)
+    if world > 1:
+        uid = [be.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.comm_init(uid[0], rank, world)
+    m = M_TOKENS
+    # Q8 (quantized in well under a second; the kernels' work per element is
+    # the same as FP8's apart from the decode pass)
+    w1 = quant.Q8.quantize(rng.normal(103, FFN * DIM, 0.02), FFN, DIM)
+    w2 = quant.Q8.quantize(rng.normal(104, DIM * FFN, 0.02), DIM, FFN)
+    ffn = TensorParallelFFN(be, rank, world, w1, rng.normal(1103, FFN, 0.01), w2, rng.normal(1104, DIM, 0.01))
+    xb = be.upload(rng.normal(11, m * DIM), BF16)
+    hb = be.upload(rng.normal(12, m * DIM), F32)
+    mb = be.upload(rng.normal(13, 6 * DIM, 0.01), F32)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    for _ in range(max(args.warmup, 3)):
+        ffn.forward(xb, m, hb, mb, GATE_FFN)
+    be.sync()
+    if world > 1:
+        dist.barrier()
+    evs = []
+    for _ in range(args.steps):
+        with torch.cuda.stream(ext):
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(ext)
+        ffn.forward(xb, m, hb, mb, GATE_FFN)
+        b.record(ext)
+        evs.append((a, b))
+    be.sync()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2.0 * 2.0 * m * DIM * FFN
+    if rank == 0:
+        print(json.dumps({"config": "tpffn", "metric": "tp_ffn_tflops", "value": flops / (ms * 1e-3) / 1e12,
+                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "ms_per_step": ms,
+                          "scaling": "strong", "dtype": "bf16", "data": "synthetic",
+                          "workload": f"FFN of the 1.3B chunk, M={m}: {DIM}->{FFN} GELU -> {DIM} + gated residual, "
+                                      "Q8 weights; FFN1 column-split, FFN2 row-split, NCCL all-reduce (f32)",
+                          "timing": "max over ranks of the mean CUDA-event time per step; L2 flushed before each"}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -573,14 +640,17 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
-                    help="c2 (default): the headline FP8 linear set; c1 / c3: the other configs, one line per shape")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "tpffn"],
+                    help="c2 (default): the headline FP8 linear set; c1 / c3: the other configs, one line per "
+                         "shape; tpffn: the chunk's FFN tensor-parallel over the torchrun ranks")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+    elif args.config == "tpffn":
+        tpffn_arm(args, rank, world, local_rank)
     elif args.config != "c2":
         if rank == 0:
             config_arm(args, local_rank)

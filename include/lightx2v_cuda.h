@@ -200,11 +200,26 @@ LX2V_API lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, size_
                                          const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
                                          size_t y_row);
 
+/* ---- tensor parallelism ---------------------------------------------------- */
+/* No counterpart in the reference (its backends run on one device). One
+ * process per GPU: rank 0 makes an id, every rank of the group passes the
+ * same bytes to lx2v_comm_init (exchanged by the caller, e.g. through its
+ * launcher's store), and lx2v_all_reduce_sum then sums a buffer over the
+ * group on the context's stream (NCCL over NVLink; f32 or bf16). NCCL is
+ * opened on first use (libnccl.so.2); without it these calls return
+ * LX2V_ERR_UNSUPPORTED. */
+#define LX2V_COMM_ID_BYTES 128
+LX2V_API lx2v_status lx2v_comm_unique_id(unsigned char *out, size_t cap);
+LX2V_API lx2v_status lx2v_comm_init(lx2v_ctx *ctx, const unsigned char *id, int rank, int world);
+/* buf[0..len) = sum over the group's ranks of their buf[0..len), in place. */
+LX2V_API lx2v_status lx2v_all_reduce_sum(lx2v_ctx *ctx, lx2v_buf *buf, size_t len);
+
 /* ---- knobs for tests and benchmarks -------------------------------------- */
 /* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05, one
  * CTA per tile), 2 = small-M GEMV, 3 = generic CUDA-core kernel, 4 = tensor-
- * core GEMM on CTA pairs (tcgen05 cta_group::2). A forced choice that cannot
- * run the shape returns LX2V_ERR_UNSUPPORTED. */
+ * core GEMM on CTA pairs (tcgen05 cta_group::2), 5 = two-pass (weight decoded
+ * to bf16, then a CTA-pair GEMM with both operands in shared memory). A
+ * forced choice that cannot run the shape returns LX2V_ERR_UNSUPPORTED. */
 LX2V_API lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path);
 /* Token tile of the tensor-core kernel: 0 = automatic, else 128, 192 or 256
  * tokens per tile (each tile is 128 output features wide). */

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <chrono>
 #include <cmath>
@@ -35,6 +37,8 @@ struct PendingEvent {
 
 struct lx2v_ctx {
     int dev = 0;
+    ncclComm_t comm = nullptr;   // tensor-parallel group (lx2v_comm_init)
+    int comm_rank = 0, comm_world = 1;
     int num_sms = 0;
     cudaStream_t stream = nullptr;
     int *err_dev = nullptr;
@@ -311,10 +315,13 @@ extern "C" lx2v_status lx2v_init(int device, lx2v_ctx **out) {
     return LX2V_OK;
 }
 
+static void comm_destroy(lx2v_ctx *ctx);
+
 extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->dev);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    comm_destroy(ctx);
     for (auto &p : ctx->pending) {
         cudaEventDestroy(p.a);
         cudaEventDestroy(p.b);
@@ -1243,5 +1250,99 @@ extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, siz
     CUDA_TRY(ctx, gemm_pair_launch(w->fmt, bt, p, ctx->num_sms, ctx->stream));
     ctx->launches++;
     CUDA_TRY(ctx, note_uses(ctx, {x, bias, y}));
+    return LX2V_OK;
+}
+
+// ---- tensor-parallel collectives (NCCL) ------------------------------------------------------
+// NCCL is opened on first use (dlopen of libnccl.so.2, the library the host
+// process already uses when it has one), so that single-GPU callers of this
+// library do not depend on it. The all-reduce runs on the context's stream,
+// ordered like every other call.
+namespace {
+struct NcclApi {
+    bool ok = false;
+    std::string err;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+
+NcclApi &nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char *e = dlerror();
+            api.err = std::string("cannot open libnccl.so.2: ") + (e ? e : "?");
+            return;
+        }
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+        if (!api.ok) api.err = "libnccl.so.2 lacks an expected symbol";
+    });
+    return api;
+}
+}  // namespace
+
+static void comm_destroy(lx2v_ctx *ctx) {
+    if (ctx->comm && nccl().ok) nccl().comm_destroy(ctx->comm);
+    ctx->comm = nullptr;
+    ctx->comm_rank = 0;
+    ctx->comm_world = 1;
+}
+
+static_assert(sizeof(ncclUniqueId) == LX2V_COMM_ID_BYTES, "NCCL unique id size");
+
+extern "C" lx2v_status lx2v_comm_unique_id(unsigned char *out, size_t cap) {
+    if (!out || cap < LX2V_COMM_ID_BYTES) return fail(nullptr, LX2V_ERR_INVALID, "need %d bytes for the id", LX2V_COMM_ID_BYTES);
+    NcclApi &api = nccl();
+    if (!api.ok) return fail(nullptr, LX2V_ERR_UNSUPPORTED, "%s", api.err.c_str());
+    ncclUniqueId id;
+    const ncclResult_t r = api.get_unique_id(&id);
+    if (r != ncclSuccess) return fail(nullptr, LX2V_ERR_CUDA, "ncclGetUniqueId: %s", api.error_string(r));
+    memcpy(out, &id, sizeof id);
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_comm_init(lx2v_ctx *ctx, const unsigned char *id, int rank, int world) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!id || world < 1 || rank < 0 || rank >= world)
+        return fail(ctx, LX2V_ERR_INVALID, "bad comm arguments (rank %d of %d)", rank, world);
+    NcclApi &api = nccl();
+    if (!api.ok) return fail(ctx, LX2V_ERR_UNSUPPORTED, "%s", api.err.c_str());
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    comm_destroy(ctx);
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof uid);
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = api.comm_init_rank(&comm, world, uid, rank);
+    if (r != ncclSuccess) return fail(ctx, LX2V_ERR_CUDA, "ncclCommInitRank: %s", api.error_string(r));
+    ctx->comm = comm;
+    ctx->comm_rank = rank;
+    ctx->comm_world = world;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_all_reduce_sum(lx2v_ctx *ctx, lx2v_buf *buf, size_t len) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!buf || len > buf->len) return fail(ctx, LX2V_ERR_INVALID, "all-reduce range out of bounds");
+    if (!ctx->comm) return fail(ctx, LX2V_ERR_INVALID, "no communicator: call lx2v_comm_init first");
+    if (len == 0) return LX2V_OK;
+    OpScope ps(ctx, "all_reduce");
+    const ncclResult_t r = nccl().all_reduce(buf->ptr, buf->ptr, len,
+                                             buf->dtype == LX2V_F32 ? ncclFloat32 : ncclBfloat16, ncclSum,
+                                             ctx->comm, ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LX2V_ERR_CUDA, "ncclAllReduce: %s", nccl().error_string(r));
+    CUDA_TRY(ctx, note_use(ctx, buf));
     return LX2V_OK;
 }

@@ -71,7 +71,12 @@ SIGNATURES = {
     "lx2v_set_split_mode": (_st, [_vp, ctypes.c_int]),
     "lx2v_set_wait_limit_ns": (_st, [_vp, ctypes.c_uint64]),
     "lx2v_launch_count": (_st, [_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "lx2v_comm_unique_id": (_st, [_vp, _sz]),
+    "lx2v_comm_init": (_st, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    "lx2v_all_reduce_sum": (_st, [_vp, _vp, _sz]),
 }
+
+COMM_ID_BYTES = 128
 
 _lib = None
 

@@ -267,9 +267,25 @@ class CudaBackend:
         self._check(self._lib.lx2v_gate_residual(self._ctx, h.handle, a.handle, rows, dim,
                                                  mods.handle, gate))
 
+    # ---- tensor parallelism (no reference counterpart) -----------------------------
+    def comm_unique_id(self) -> bytes:
+        """NCCL id for a new tensor-parallel group (made on one rank, passed to all)."""
+        buf = ctypes.create_string_buffer(L.COMM_ID_BYTES)
+        self._check(self._lib.lx2v_comm_unique_id(buf, L.COMM_ID_BYTES))
+        return buf.raw
+
+    def comm_init(self, uid: bytes, rank: int, world: int):
+        assert len(uid) == L.COMM_ID_BYTES
+        self._check(self._lib.lx2v_comm_init(self._ctx, uid, rank, world))
+
+    def all_reduce_sum(self, buf: Buf, length: int | None = None):
+        """In place: buf[:length] = sum over the group (on this context's stream)."""
+        self._check(self._lib.lx2v_all_reduce_sum(self._ctx, buf.handle, buf.len if length is None else length))
+
     # ---- knobs ---------------------------------------------------------------------
     def set_linear_path(self, path: int):
-        """0 automatic, 1 tensor-core GEMM, 2 small-M GEMV, 3 generic CUDA-core kernel."""
+        """0 automatic, 1 tensor-core GEMM, 2 small-M GEMV, 3 generic CUDA-core kernel,
+        4 CTA-pair tensor-core GEMM, 5 two-pass (bf16 decode + CTA-pair GEMM)."""
         self._check(self._lib.lx2v_set_linear_path(self._ctx, path))
 
     def set_token_tile(self, tokens: int):
