@@ -3,9 +3,21 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <atomic>
 #include <cstdint>
 
 namespace lx2v {
+
+// A launcher's one-time set-up (the shared-memory opt-in, which is per
+// device, and the occupancy it yields), cached per device: 0 until the first
+// launch on that device. A device index past the table gets no cache (the
+// set-up runs every launch).
+constexpr int LX2V_MAX_DEVICES = 64;
+inline std::atomic<int> *device_slot(std::atomic<int> (&cache)[LX2V_MAX_DEVICES]) {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= LX2V_MAX_DEVICES) return nullptr;
+    return &cache[d];
+}
 
 // Everything one linear launch needs; passed by value as a __grid_constant__.
 struct alignas(64) GemmParams {

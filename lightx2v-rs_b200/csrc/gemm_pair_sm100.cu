@@ -354,7 +354,9 @@ static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t
     using C = PairCfg<FMT, BT, ACC, SS, AS>;
     auto kern = gemm_pair_kernel<FMT, BT, ACC, SS, AS, DQW, SK, GRP>;
     constexpr int PAIR_THREADS = 32 * (8 + 4 * DQW);
-    static int max_pairs = 0;
+    static std::atomic<int> max_pairs_dev[LX2V_MAX_DEVICES];
+    std::atomic<int> *slot = device_slot(max_pairs_dev);
+    int max_pairs = slot ? slot->load(std::memory_order_relaxed) : 0;
     const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
@@ -376,6 +378,7 @@ static cudaError_t pair_launch_sk(const GemmParams &p, int num_sms, cudaStream_t
         e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
         if (e != cudaSuccess) return e;
         max_pairs = clusters > 0 ? clusters : 1;
+        if (slot) slot->store(max_pairs, std::memory_order_relaxed);
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
     // stream-K: every pair gets at least one k-block (the host checked

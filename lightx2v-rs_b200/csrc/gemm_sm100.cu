@@ -266,15 +266,16 @@ template <int FMT, int BT, int ACC, int SS, int AS, int DQW = 4>
 static cudaError_t launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = Cfg<FMT, BT, ACC, SS, AS>;
     constexpr int NUM_THREADS = 32 * (8 + 4 * DQW);
-    static bool attr_set = false;
+    static std::atomic<int> attr_set_dev[LX2V_MAX_DEVICES];
+    std::atomic<int> *slot = device_slot(attr_set_dev);
     // Keep the footprint large enough that only one CTA fits per SM: each
     // CTA allocates all 512 TMEM columns.
     const int smem = C::SMEM_BYTES > 120 * 1024 ? C::SMEM_BYTES : 120 * 1024;
-    if (!attr_set) {
+    if (!slot || slot->load(std::memory_order_relaxed) == 0) {
         cudaError_t e = cudaFuncSetAttribute(gemm_dq_kernel<FMT, BT, ACC, SS, AS, DQW>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        if (slot) slot->store(1, std::memory_order_relaxed);
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 127) / 128);
     const int grid = n_tiles < num_sms ? n_tiles : num_sms;

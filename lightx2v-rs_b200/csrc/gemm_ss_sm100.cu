@@ -432,7 +432,9 @@ template <int BT, int ACC, int SS, int GRP, bool SK>
 static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st) {
     using C = SsCfg<BT, ACC, SS>;
     auto kern = gemm_ss_pair_kernel<BT, ACC, SS, GRP, SK>;
-    static int max_pairs = 0;
+    static std::atomic<int> max_pairs_dev[LX2V_MAX_DEVICES];
+    std::atomic<int> *slot = device_slot(max_pairs_dev);
+    int max_pairs = slot ? slot->load(std::memory_order_relaxed) : 0;
     const int smem = C::SMEM_BYTES;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
@@ -456,6 +458,7 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
         e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
         if (e != cudaSuccess) return e;
         max_pairs = clusters > 0 ? clusters : 1;
+        if (slot) slot->store(max_pairs, std::memory_order_relaxed);
     }
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
     // stream-K: every pair gets at least one group (the host checked

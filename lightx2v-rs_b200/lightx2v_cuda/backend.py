@@ -271,7 +271,9 @@ class CudaBackend:
     def comm_unique_id(self) -> bytes:
         """NCCL id for a new tensor-parallel group (made on one rank, passed to all)."""
         buf = ctypes.create_string_buffer(L.COMM_ID_BYTES)
-        self._check(self._lib.lx2v_comm_unique_id(buf, L.COMM_ID_BYTES))
+        st = self._lib.lx2v_comm_unique_id(buf, L.COMM_ID_BYTES)
+        if st != L.OK:  # a context-free call: its message is the library-wide one
+            raise L.Lx2vError(st, self._lib.lx2v_last_error(None).decode())
         return buf.raw
 
     def comm_init(self, uid: bytes, rank: int, world: int):
