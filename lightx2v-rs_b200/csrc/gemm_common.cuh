@@ -150,7 +150,12 @@ struct PairWork {
     int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
     int dp = 0, my_dp = 0;     // whole tiles before the split range (all pairs / this pair)
     bool sk = false;
-    __device__ __forceinline__ void init_split(int n_tiles, int dp_tiles) {
+    __host__ __device__ __forceinline__ void init_split(int n_tiles, int dp_tiles) {
+        // The split range must give every pair at least one k-block: a pair
+        // with an empty range would be counted by the head of a tile it has
+        // no part of. When the leftover tiles are too few, split one more
+        // wave as well (dp stays a multiple of npairs).
+        if (dp_tiles >= npairs && (long long)(n_tiles - dp_tiles) * KB < npairs) dp_tiles -= npairs;
         dp = dp_tiles;
         my_dp = pair < dp ? (dp - 1 - pair) / npairs + 1 : 0;
         const long long rem = (long long)(n_tiles - dp) * KB;
@@ -158,17 +163,17 @@ struct PairWork {
         hi = (long long)dp * KB + rem * (pair + 1) / npairs;
     }
     // first k-block (counted from tile 0) of pair q's split range
-    __device__ __forceinline__ long long split_start(int n_tiles, int q) const {
+    __host__ __device__ __forceinline__ long long split_start(int n_tiles, int q) const {
         return (long long)dp * KB + (long long)(n_tiles - dp) * KB * q / npairs;
     }
-    __device__ __forceinline__ int count() const {
+    __host__ __device__ __forceinline__ int count() const {
         if (!sk) return my_tiles;
         return my_dp + (hi > lo ? (int)((hi - 1) / KB - lo / KB + 1) : 0);
     }
-    __device__ __forceinline__ long long total_kb() const {
+    __host__ __device__ __forceinline__ long long total_kb() const {
         return sk ? (long long)my_dp * KB + (hi - lo) : (long long)my_tiles * KB;
     }
-    __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
+    __host__ __device__ __forceinline__ void seg(int idx, int &tile, int &kb0, int &kb1) const {
         if (!sk || idx < my_dp) {
             tile = pair + idx * npairs;
             kb0 = 0;

@@ -459,11 +459,14 @@ def test_gemm_operands_are_bf16_of_exact_dequant(be, oracle, fmt, path):
 # ---- stream-K work split of the CTA-pair kernel ------------------------------------------
 @pytest.mark.parametrize("fmt", ["fp8", "q8", "q4", "native"])
 @pytest.mark.parametrize("M,N,K,bt", [(4680, 1536, 1536, 256), (1000, 512, 8960, 256), (700, 640, 4480, 192),
-                                      (2500, 1552, 704, 128)])
+                                      (2500, 1552, 704, 128), (19200, 256, 768, 256)])
 @pytest.mark.parametrize("path", [4, 5])
 def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt, path):
     # tiles split over several CTA pairs, several partial tiles added into one
-    # (1000 x 512 x 8960: ~10 pairs per tile), ragged M and N
+    # (1000 x 512 x 8960: ~10 pairs per tile), ragged M and N; 19200 x 256 x
+    # 768: 75 tiles on 74 pairs, whose leftover tile alone has fewer k-block
+    # groups than there are pairs (the two-pass kernel then splits one more
+    # wave)
     w, q = make_weight(fmt, N, K, seed=101 + K, oracle=oracle)
     dw = upload_weight(be, fmt, q, w, N, K)
     x = oracle.normal(102, M * K)
