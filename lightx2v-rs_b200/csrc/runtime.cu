@@ -856,7 +856,7 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
     int path = ctx->path;
     if (path == 0) {
         if (rows <= 16 && gemv_ok) path = 2;
-        else if (ss_ok && N >= 256 &&
+        else if (ss_ok && N >= 256 && K % 64 == 0 &&  // whole 64-wide k-blocks, the shapes it is tested on
                  (rows >= (w->fmt == LX2V_W_BF16 ? 512u : (size_t)TWO_PASS_MIN_ROWS) ||
                   ((rows + 255) / 256) * ((N + 255) / 256) <= TWO_PASS_MAX_FEW_TILES))
             path = 5;
