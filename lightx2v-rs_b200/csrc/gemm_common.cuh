@@ -300,6 +300,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t acc_
 __device__ __forceinline__ void flag_publish(int *flag, int value) {
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
 }
+// Back to 0 once the flag's owner has consumed what it announced; the next
+// launch on the stream sees it (kernel boundaries order the store).
+__device__ __forceinline__ void flag_clear(int *flag) {
+    asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(0) : "memory");
+}
 __device__ __forceinline__ int flag_read(const int *flag) {
     int v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");

@@ -282,6 +282,14 @@ __global__ void __launch_bounds__(32 * (8 + 4 * DQW), 1) gemm_pair_kernel(const 
                 named_bar_sync(1, EPI_THREADS);
                 if (leader_thread) flag_publish(p.flags + pair * 2 + (int)rank, p.epoch);
             }
+            if (SK && n_add > 0) {
+                // every epilogue thread has read the tail pairs' partials:
+                // clear their flags, so that a later launch with the same
+                // epoch (a replayed CUDA graph) waits for fresh partials
+                named_bar_sync(1, EPI_THREADS);
+                if (leader_thread)
+                    for (int a = 0; a < n_add; ++a) flag_clear(p.flags + (pair + 1 + a) * 2 + (int)rank);
+            }
             ab.next<ACC>();
         }
     } else if (warp >= 8) {

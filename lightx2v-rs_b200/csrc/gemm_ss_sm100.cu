@@ -402,6 +402,15 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
                 __syncwarp();
                 if (lane == 0) flag_publish(p.flags + (pair * 2 + (int)rank) * SS_EPI_WARPS + wi, p.epoch);
             }
+            if (SK && n_add > 0) {
+                // the warp has read the tail pairs' partials: clear their
+                // flags, so that a later launch with the same epoch (a
+                // replayed CUDA graph) waits for fresh partials
+                __syncwarp();
+                if (lane == 0)
+                    for (int a = 0; a < n_add; ++a)
+                        flag_clear(p.flags + ((pair + 1 + a) * 2 + (int)rank) * SS_EPI_WARPS + wi);
+            }
             ab.next<ACC>();
         }
         if (lane == 0) bulk_wait<0>();  // this warp's tensor stores have completed

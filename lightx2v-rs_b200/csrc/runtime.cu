@@ -271,6 +271,20 @@ static lx2v_status ensure_staging(lx2v_ctx *ctx, size_t bytes) {
     return LX2V_OK;
 }
 
+// Workspaces a linear on an N x K weight may need, sized when the weight is
+// uploaded (a blocking call) so that no linear allocates or synchronises:
+// the two-pass decode buffers, the few-token split-K partials and the
+// stream-K partial tiles. They only grow; lx2v_linear still grows them if a
+// caller forces a path or tile the upload did not plan for.
+static lx2v_status plan_workspaces(lx2v_ctx *ctx, int fmt, size_t rows, size_t cols) {
+    lx2v_status s = LX2V_OK;
+    if (fmt != LX2V_W_BF16 && (s = ensure_dq_workspace(ctx, rows * cols * 2))) return s;
+    if (cols % 64 == 0 && (s = ensure_gemv_workspace(ctx, (int)rows, (int)cols))) return s;
+    float *partials = nullptr;
+    int *flags = nullptr;
+    return ensure_sk_workspace(ctx, ctx->num_sms / 2, 256, &partials, &flags);
+}
+
 // ---- context -------------------------------------------------------------------
 extern "C" lx2v_status lx2v_init(int device, lx2v_ctx **out) {
     if (!out) return fail(nullptr, LX2V_ERR_INVALID, "null output pointer");
@@ -358,11 +372,16 @@ extern "C" lx2v_status lx2v_name(lx2v_ctx *ctx, char *buf, size_t cap) {
     return LX2V_OK;
 }
 
+static cudaError_t clear_split_flags(lx2v_ctx *ctx);
+
 static lx2v_status check_device_error(lx2v_ctx *ctx) {
     int h = 0;
     CUDA_TRY(ctx, cudaMemcpyAsync(&h, ctx->err_dev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     if (h != 0) {
+        // a stopped stream-K launch may have left flags set that no owner
+        // consumed; clear them so that no later launch reads stale partials
+        CUDA_TRY(ctx, clear_split_flags(ctx));
         CUDA_TRY(ctx, cudaMemsetAsync(ctx->err_dev, 0, sizeof(int), ctx->stream));
         CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
         return fail(ctx, LX2V_ERR_DEVICE,
@@ -604,6 +623,7 @@ extern "C" lx2v_status lx2v_weight_f32(lx2v_ctx *ctx, const float *data, size_t 
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     ctx->launches++;
     if (e != cudaSuccess) { weight_release(w); return fail(ctx, LX2V_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e)); }
+    if ((s = plan_workspaces(ctx, LX2V_W_BF16, rows, cols))) { weight_release(w); return s; }
     *out = w;
     return LX2V_OK;
 }
@@ -637,6 +657,7 @@ extern "C" lx2v_status lx2v_weight_q8(lx2v_ctx *ctx, const int8_t *q, const floa
     w->fmt = LX2V_W_Q8; w->rows = rows; w->cols = cols; w->group = group;
     auto st = transpose_scales(scales, rows, cols / group);
     if ((s = upload_codes_scales(ctx, w, q, rows * cols, &st, nullptr))) { weight_release(w); return s; }
+    if ((s = plan_workspaces(ctx, LX2V_W_Q8, rows, cols))) { weight_release(w); return s; }
     *out = w;
     return LX2V_OK;
 }
@@ -672,6 +693,7 @@ extern "C" lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const fl
         return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA, "weight upload: %s",
                     cudaGetErrorString(e));
     }
+    if ((s = plan_workspaces(ctx, LX2V_W_FP8, rows, cols))) { weight_release(w); return s; }
     *out = w;
     return LX2V_OK;
 }
@@ -706,6 +728,7 @@ extern "C" lx2v_status lx2v_weight_q4(lx2v_ctx *ctx, const uint8_t *packed, cons
     auto *w = new lx2v_weight();
     w->fmt = LX2V_W_Q4; w->rows = rows; w->cols = cols; w->group = group;
     if ((s = upload_codes_scales(ctx, w, packed, (rows * cols + 1) / 2, nullptr, &sz))) { weight_release(w); return s; }
+    if ((s = plan_workspaces(ctx, LX2V_W_Q4, rows, cols))) { weight_release(w); return s; }
     *out = w;
     return LX2V_OK;
 }
@@ -1166,6 +1189,24 @@ static lx2v_status noalloc_scratch(lx2v_ctx *ctx, void **ptr, int *epoch) {
     return LX2V_OK;
 }
 
+// Stream-K flags of this context's workspace and of the device's static
+// scratch back to zero (after a kernel stopped on an expired wait).
+static cudaError_t clear_split_flags(lx2v_ctx *ctx) {
+    if (ctx->sk_ws) {
+        const size_t flag_bytes = (size_t)ctx->num_sms * 2 * 8 * sizeof(int);
+        cudaError_t e = cudaMemsetAsync((char *)ctx->sk_ws + (ctx->sk_ws_bytes - flag_bytes), 0, flag_bytes,
+                                        ctx->stream);
+        if (e != cudaSuccess) return e;
+    }
+    void *scratch = nullptr;
+    if (ctx->dev >= 0 && ctx->dev < LX2V_NOALLOC_MAX_DEVICES) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        scratch = g_noalloc[ctx->dev].scratch;
+    }
+    if (scratch) return cudaMemsetAsync(scratch, 0, LX2V_NOALLOC_FLAG_BYTES, ctx->stream);
+    return cudaSuccess;
+}
+
 extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, size_t x_row, size_t rows,
                                            const lx2v_weight *w, const lx2v_buf *bias, int act, lx2v_buf *y,
                                            size_t y_row) {
@@ -1184,6 +1225,7 @@ extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, siz
     if (bias && bias->len < N) return fail(ctx, LX2V_ERR_INVALID, "bias has %zu elements, need %zu", bias->len, N);
     if (rows == 0) return LX2V_OK;
     if (rows > (1u << 30)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "too many rows");
+    OpScope ps(ctx, "linear_noalloc");
     const size_t grp = w->group;
     const bool groups_ok = w->fmt == LX2V_W_BF16 || grp % 64 == 0 ||
                            (w->fmt == LX2V_W_Q4 && (grp == 16 || grp == 32));
@@ -1243,6 +1285,7 @@ extern "C" lx2v_status lx2v_linear_noalloc(lx2v_ctx *ctx, const lx2v_buf *x, siz
     p.x_row = (int)x_row; p.y_row = (int)y_row;
     p.act = act;
     p.out_f32 = y->dtype == LX2V_F32;
+    p.kgroup = K % 128 == 0 ? 2 : 1;
     p.streamk = 1;
     p.epoch = epoch;
     p.flags = (int *)scratch;

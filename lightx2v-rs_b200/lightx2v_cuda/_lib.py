@@ -1,7 +1,7 @@
 """ctypes binding of liblightx2v_cuda.so (the C ABI in include/lightx2v_cuda.h).
 
-This is the reference-side binding a host language would add; the Rust
-version of the same declarations is in INTEGRATION.md. There is no fallback:
+This is the binding a host language adds to call the library; a Rust crate
+declares the same functions in an `extern "C"` block. There is no fallback:
 if the shared library is missing, importing the backend raises.
 """
 from __future__ import annotations

@@ -268,6 +268,20 @@ class Fp8E4M3:
     def dequantize(self) -> np.ndarray:
         return (_E4M3[self.q].reshape(-1, self.group) * self.scales[:, None]).astype(_F32).reshape(-1)
 
+    @staticmethod
+    def concat(parts) -> "Fp8E4M3":
+        """Rows of several FP8 matrices stacked, codes then scales in part
+        order, with the first part's cols and group: the fused QKV / KV
+        stacking of load_linear (crates/lightx2v-model/src/dit.rs:127-147),
+        which has no method of its own in quant.rs. Unlike Q8/Q4 concat the
+        reference does not assert that cols and group agree; a stack whose
+        parts differ would be mis-shaped, so this mirror rejects it."""
+        a = parts[0]
+        for b in parts[1:]:
+            assert (a.cols, a.group) == (b.cols, b.group)
+        return Fp8E4M3(np.concatenate([p.q for p in parts]), np.concatenate([p.scales for p in parts]),
+                       sum(p.rows for p in parts), a.cols, a.group)
+
     def bytes(self) -> int:
         return self.q.size + 4 * self.scales.size
 

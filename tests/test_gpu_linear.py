@@ -562,3 +562,57 @@ def test_few_token_kernel_is_the_automatic_choice_and_fuses_the_gate(be, oracle)
     lin = oracle.linear(x, M, oracle_dequant(oracle, "q4", q, None), N, K, threads=8)
     want = oracle.gate_residual(h0.reshape(M, N).copy(), lin, M, N, mods, 5)
     assert rel_l2(got - h0.reshape(M, N), want - h0.reshape(M, N)) <= REL_L2
+
+
+# ---- CUDA graph replay of stream-K launches ----------------------------------------------
+def replay_follows_inputs(be, run, xb, x_sets, yb, wants, replays=3):
+    """Capture `run` (which reads xb and writes yb) on the library's stream,
+    then replay it with the inputs switched between replays: every replay must
+    equal the eager result for the inputs it saw. A stream-K launch whose
+    flags still held the previous replay's epoch would add partial tiles left
+    from the earlier inputs (or still being written) and fail this."""
+    import torch
+    ext = torch.cuda.ExternalStream(be.stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=ext):
+        run()
+    try:
+        for r in range(replays):
+            i = r % len(x_sets)
+            be.copy(x_sets[i], 0, xb, 0, be.buf_len(xb))
+            with torch.cuda.stream(ext):
+                g.replay()
+            got = be.download(yb)
+            assert np.array_equal(got, wants[i], equal_nan=True), (r, i)
+    finally:
+        del g
+
+
+@pytest.mark.parametrize("path", [4, 5])
+def test_stream_k_linear_replays_in_a_cuda_graph(be, oracle, path):
+    M, N, K = 1000, 1536, 1536
+    w, q = make_weight("fp8", N, K, seed=81, oracle=oracle)
+    dw = be.weight_fp8(q)
+    x_sets = [be.upload(oracle.normal(82 + i, M * K)) for i in range(2)]
+    xb = be.alloc(M * K)
+    bb = be.upload(oracle.normal(84, N, 0.01), F32)
+    yb = be.alloc(M * N, F32)
+    try:
+        be.set_linear_path(path)
+        be.set_split_mode(2)
+
+        def run():
+            be.linear(xb, 0, M, dw, bb, Act.GELU_TANH, yb, 0)
+
+        wants = []
+        for xs in x_sets:  # eager: also the first call that sizes every workspace
+            be.copy(xs, 0, xb, 0, M * K)
+            run()
+            wants.append(be.download(yb))
+        be.sync()
+        replay_follows_inputs(be, run, xb, x_sets, yb, wants)
+    finally:
+        be.set_linear_path(0)
+        be.set_split_mode(0)
+    want = oracle.linear(be.download(x_sets[0]), M, q.dequantize(), N, K, bias=be.download(bb), act=1, threads=8)
+    assert rel_l2(wants[0].reshape(M, N), want) <= REL_L2

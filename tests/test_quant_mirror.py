@@ -85,3 +85,35 @@ def test_weight_quant_parse_and_for_key():
     assert q.for_key("blocks.3.attn1.to_q") == WQ("int8")
     assert q.for_key("blocks.3.norm2") == WQ("native")
     assert q.for_key("proj_out") == WQ("native")
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4", "fp8"])
+def test_concat_stacks_rows_like_load_linear(oracle, fmt):
+    # fused QKV: parts quantized one by one and stacked by rows, codes then
+    # scales (quant.rs:189-199, 339-350; FP8 inline in dit.rs:127-147)
+    rows, cols = 8, 256
+    ws = [oracle.normal(40 + i, rows * cols, 0.02) for i in range(3)]
+    if fmt == "q8":
+        parts = [quant.Q8.quantize(w, rows, cols) for w in ws]
+        st = quant.Q8.concat(parts)
+    elif fmt == "q4":
+        parts = [quant.Q4.quantize(w, rows, cols, 64, True) for w in ws]
+        st = quant.Q4.concat(parts)
+        assert np.array_equal(st.zeros, np.concatenate([p.zeros for p in parts]))
+    else:
+        parts = [quant.Fp8E4M3.quantize(w, rows, cols) for w in ws]
+        st = quant.Fp8E4M3.concat(parts)
+    assert (st.rows, st.cols, st.group) == (3 * rows, cols, parts[0].group)
+    assert np.array_equal(st.q, np.concatenate([p.q for p in parts]))
+    assert np.array_equal(st.scales, np.concatenate([p.scales for p in parts]))
+    deq = st.dequantize()
+    want = np.concatenate([p.dequantize() for p in parts])
+    assert np.array_equal(np.isnan(deq), np.isnan(want))
+    assert np.array_equal(deq[~np.isnan(want)], want[~np.isnan(want)])
+
+
+def test_fp8_concat_rejects_mismatched_parts(oracle):
+    a = quant.Fp8E4M3.quantize(oracle.normal(1, 4 * 256), 4, 256)
+    b = quant.Fp8E4M3.quantize(oracle.normal(2, 4 * 128), 4, 128)
+    with pytest.raises(AssertionError):
+        quant.Fp8E4M3.concat([a, b])
