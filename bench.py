@@ -10,17 +10,22 @@ tokens, dim 1536:
     FFN2  8960 -> 1536, + gated residual into h (dit.rs:748-760)
 Weights N(0, 0.02) quantized with the reference's FP8 quantizer (group-128
 scales along K), activations bf16 N(0, 1), all seeded (lightx2v-core Rng).
-One step = those four linears. Every arithmetic op is bf16 x bf16 -> f32 on
-tcgen05 tensor cores after exact in-register dequantisation.
+One step = those four linears. Every product is bf16 x bf16 -> f32 on
+tcgen05 tensor cores, on weights decoded exactly (the reference's arithmetic)
+and rounded to bf16.
 
 value  TFLOP/s with inputs resident in HBM, device-timed with CUDA events per
        step on the library's stream; L2 is flushed (256 MB write) before every
        timed step, outside the timed region.
 e2e    the same TFLOP/s through the C ABI with host buffers: every step uploads
        x and h from pinned f32 host memory and downloads h (f32) back.
-Multi-GPU (torchrun): weak scaling, each rank runs its own 4680-token chunk
-with replicated weights and no collective in the data path; time = max over
-ranks.
+Multi-GPU (torchrun, one process per GPU): the chunk's 4680 token rows are
+split over the ranks with the weights replicated and no collective in the
+data path (strong scaling; time = max over ranks). The same line carries
+`weak` (every rank a whole chunk of its own) and `tp_ffn` (the chunk's FFN
+tensor-parallel over the ranks, with its rel-L2 against the unsplit FFN).
+On one GPU the line also carries `configs`: C1 (Q8 1560 x 1536 -> 8960) and
+the C3 Q4 sweep at M in {1, 16, 4680} with the few-token chain.
 
 --impl reference times the reference's CPU implementation of the path
 (CpuBackend::linear, restated in C under oracle/ because the Rust reference
@@ -263,9 +268,72 @@ def reference_arm(args, rank: int, world: int):
 
 
 # ---------------------------------------------------------------------------------------------
-def cuda_arm(args, rank: int, world: int, local_rank: int):
+# ---------------------------------------------------------------------------------------------
+def ev():
     import torch
-    from lightx2v_cuda import BF16, F32, CudaBackend
+    return torch.cuda.Event(enable_timing=True)
+
+
+def chunk_rows(total: int, rank: int, world: int):
+    """Rank r's token rows [r0, r1) of a chunk split over `world` ranks."""
+    return total * rank // world, total * (rank + 1) // world
+
+
+class LinearSet:
+    """The chunk's four FP8 linears on rows [0, m) of device buffers."""
+
+    def __init__(self, be, dw, m, x_host, h_host, mods):
+        from lightx2v_cuda import F32
+        self.be, self.dw, self.m = be, dw, m
+        self.xb = be.upload(x_host)           # bf16 activations (the CUDA backend's precision)
+        self.hb = be.upload(h_host, F32)      # f32 residual stream
+        self.mb = be.upload(mods)
+        self.qkv = be.alloc(m * 3 * DIM)
+        self.tmp = be.alloc(m * DIM)
+        self.hid = be.alloc(m * FFN)
+
+    def linear(self, name, hb=None):
+        be, dw, m = self.be, self.dw, self.m
+        if name == "qkv":
+            be.linear(self.xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, self.qkv, 0)
+        elif name == "out":
+            be.linear(self.xb, 0, m, dw["out"][0], dw["out"][1], 0, self.tmp, 0)
+        elif name == "ffn1":
+            be.linear(self.xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, self.hid, 0)
+        else:
+            be.linear_gate_residual(self.hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0,
+                                    self.hb if hb is None else hb, 0, self.mb, GATE_FFN)
+
+    def step(self):
+        for name, *_ in LINEARS:
+            self.linear(name)
+
+
+def timed_steps(be, ext, flush, fn, steps):
+    """CUDA-event time (ms) of each of `steps` calls of fn on the library's
+    stream, L2 flushed (256 MB write) before each, outside the event pair."""
+    import torch
+    pairs = []
+    for _ in range(steps):
+        with torch.cuda.stream(ext):
+            flush.zero_()
+        a, b = ev(), ev()
+        a.record(ext)
+        fn()
+        b.record(ext)
+        pairs.append((a, b))
+    be.sync()
+    return [a.elapsed_time(b) for a, b in pairs]
+
+
+def cuda_arm(args, rank: int, world: int, local_rank: int):
+    """The headline: the C2 chunk (M = 4680 token rows) through the four FP8
+    linears. With N ranks the chunk's rows are split (rank r takes rows
+    [r M / N, (r + 1) M / N), weights replicated, no collective in the data
+    path: strong scaling); `weak` adds each rank running a whole chunk of
+    its own, and `tp_ffn` the chunk's FFN tensor-parallel over the ranks."""
+    import torch
+    from lightx2v_cuda import F32, CudaBackend
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -278,36 +346,16 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
 
     be = CudaBackend(local_rank)
     ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
-    m = M_TOKENS
-    ws, x, h, mods, _ = make_inputs(m, seed_offset=rank)
-    dw = {name: (be.weight_fp8(q), be.upload(b)) for name, (q, b) in ws.items()}
-    xb = be.upload(x)                     # bf16 activations (the CUDA backend's precision)
-    hb = be.upload(h, F32)                # f32 residual stream
-    mb = be.upload(mods)
-    qkv = be.alloc(m * 3 * DIM)
-    tmp = be.alloc(m * DIM)
-    hid = be.alloc(m * FFN)
-
-    def step():
-        be.linear(xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, qkv, 0)
-        be.linear(xb, 0, m, dw["out"][0], dw["out"][1], 0, tmp, 0)
-        be.linear(xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, hid, 0)
-        be.linear_gate_residual(hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0, hb, 0, mb, GATE_FFN)
-
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    M = M_TOKENS
+    r0, r1 = chunk_rows(M, rank, world)
+    m = r1 - r0
+    ws, x, h, mods, _ = make_inputs(M)
+    dw = {name: (be.weight_fp8(q), be.upload(b)) for name, (q, b) in ws.items()}
+    xs = x.reshape(M, DIM)[r0:r1].reshape(-1)
+    hs = h.reshape(M, DIM)[r0:r1].reshape(-1)
+    strong = LinearSet(be, dw, m, xs, hs, mods)
 
-    def flush_l2():
-        with torch.cuda.stream(ext):
-            flush.zero_()
-
-    def ev():
-        return torch.cuda.Event(enable_timing=True)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    be.sync()
-
-    # --- device-resident timing -----------------------------------------------------------
     def barrier():
         be.sync()
         torch.cuda.synchronize()
@@ -315,75 +363,75 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(vals):
+        if not dist:
+            return [float(v) for v in vals]
+        t = torch.tensor(vals, dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    for _ in range(max(args.warmup, 3)):
+        strong.step()
     barrier()
+
+    # --- device-resident timing (strong: the chunk's rows split over the ranks) ---------
     launches0 = be.launch_count()
-    pairs = []
     with ClockSampler(local_rank) as clk:
         time.sleep(0.01)  # first NVML samples before the region
         clk.start_region()
-        for _ in range(args.steps):
-            flush_l2()
-            a, b = ev(), ev()
-            a.record(ext)
-            step()
-            b.record(ext)
-            pairs.append((a, b))
-        be.sync()
+        step_ms = timed_steps(be, ext, flush, strong.step, args.steps)
         clk.end_region()
     barrier()
     launches = be.launch_count() - launches0
-    step_ms = [a.elapsed_time(b) for a, b in pairs]
     total_ms = float(sum(step_ms))
 
-    # --- per-kernel timing for the roofline (same launches, one event pair each) ----------
+    # --- weak scaling: every rank a whole chunk of its own -------------------------------
+    full = strong if world == 1 else None
+    weak_ms = total_ms
+    if world > 1:
+        from lightx2v_cuda import rng
+        full = LinearSet(be, dw, M, rng.normal(11 + rank, M * DIM), rng.normal(12 + rank, M * DIM), mods)
+        for _ in range(max(args.warmup, 3)):
+            full.step()
+        barrier()
+        weak_ms = float(sum(timed_steps(be, ext, flush, full.step, args.steps)))
+        barrier()
+
+    # --- per-linear timing on a whole chunk, for the roofline ----------------------------
     kern_ms = {name: [] for name, *_ in LINEARS}
     for _ in range(max(3, min(args.steps, 20))):
-        for name, n, k, act, _s in LINEARS:
-            flush_l2()
-            a, b = ev(), ev()
-            a.record(ext)
-            if name == "qkv":
-                be.linear(xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, qkv, 0)
-            elif name == "out":
-                be.linear(xb, 0, m, dw["out"][0], dw["out"][1], 0, tmp, 0)
-            elif name == "ffn1":
-                be.linear(xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, hid, 0)
-            else:
-                be.linear_gate_residual(hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0, hb, 0, mb, GATE_FFN)
-            b.record(ext)
-            kern_ms[name].append((a, b))
-    be.sync()
+        for name, *_ in LINEARS:
+            kern_ms[name] += timed_steps(be, ext, flush, lambda: full.linear(name), 1)
     per_kernel = {}
     for name, n, k, act, _s in LINEARS:
-        ms = float(np.mean([a.elapsed_time(b) for a, b in kern_ms[name]]))
-        per_kernel[name] = {"ms": ms, "tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12}
+        ms = float(np.mean(kern_ms[name]))
+        per_kernel[name] = {"ms": ms, "tflops": 2.0 * M * n * k / (ms * 1e-3) / 1e12}
     gemm_ms = sum(v["ms"] for v in per_kernel.values())
 
-    # --- end to end through the C ABI with host buffers ------------------------------------
-    # Every step writes x and h from page-locked host memory, runs the four
-    # linears and reads h back. Steps are pipelined the way a serving loop
-    # would run them: the writes go out on the library's copy stream as soon
-    # as the buffers they overwrite are free, the read-back is queued without
-    # blocking, and h alternates between two device buffers, so step i+1's
-    # uploads overlap step i's kernels and read-back.
-    x_host = torch.from_numpy(x).pin_memory()
-    h_host = torch.from_numpy(h).pin_memory()
+    # --- end to end through the C ABI with host buffers (strong split) ------------------
+    # Every step writes this rank's x and h rows from page-locked host memory,
+    # runs the four linears and reads h back. Steps are pipelined the way a
+    # serving loop would run them: the writes go out on the library's copy
+    # stream as soon as the buffers they overwrite are free, the read-back is
+    # queued without blocking, and h alternates between two device buffers,
+    # so step i+1's uploads overlap step i's kernels and read-back.
+    x_host = torch.from_numpy(np.ascontiguousarray(xs)).pin_memory()
+    h_host = torch.from_numpy(np.ascontiguousarray(hs)).pin_memory()
     h_outs = [torch.empty(m * DIM, dtype=torch.float32).pin_memory() for _ in range(2)]
-    hbs = [hb, be.alloc(m * DIM, F32)]
+    hbs = [strong.hb, be.alloc(m * DIM, F32)]
 
     def e2e_step(i):
         hbi = hbs[i % 2]
-        be.write_ptr(xb, x_host.data_ptr(), m * DIM)
-        be.linear(xb, 0, m, dw["qkv"][0], dw["qkv"][1], 0, qkv, 0)
-        be.linear(xb, 0, m, dw["out"][0], dw["out"][1], 0, tmp, 0)
-        be.linear(xb, 0, m, dw["ffn1"][0], dw["ffn1"][1], 1, hid, 0)
+        be.write_ptr(strong.xb, x_host.data_ptr(), m * DIM)
+        strong.linear("qkv")
+        strong.linear("out")
+        strong.linear("ffn1")
         be.write_ptr(hbi, h_host.data_ptr(), m * DIM)
-        be.linear_gate_residual(hid, 0, m, dw["ffn2"][0], dw["ffn2"][1], 0, hbi, 0, mb, GATE_FFN)
+        strong.linear("ffn2", hb=hbi)
         be.download_ptr_async(hbi, h_outs[i % 2].data_ptr(), m * DIM)
 
     for i in range(2):
         e2e_step(i)
-    be.sync()
     barrier()
     e_a, e_b = ev(), ev()
     e_a.record(ext)
@@ -394,141 +442,210 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     barrier()
     e2e_ms = float(e_a.elapsed_time(e_b))
 
-    # --- max over ranks --------------------------------------------------------------------
-    if dist:
-        t = torch.tensor([total_ms, e2e_ms, gemm_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms, gemm_ms = (float(v) for v in t.tolist())
+    total_ms, weak_ms, e2e_ms, gemm_ms = max_over_ranks([total_ms, weak_ms, e2e_ms, gemm_ms])
 
-    flops_all = step_flops(m) * args.steps * world
-    value = flops_all / (total_ms * 1e-3) / 1e12
-    e2e_value = flops_all / (e2e_ms * 1e-3) / 1e12
-    peak, _hbm, peak_src = measured_peaks()
-    achieved = step_flops(m) / (gemm_ms * 1e-3) / 1e12
+    # --- the chunk's FFN tensor-parallel over the ranks ----------------------------------
+    tp = tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barrier)
 
+    flops_step = step_flops(M)
+    value = flops_step * args.steps / (total_ms * 1e-3) / 1e12
+    weak_value = flops_step * world * args.steps / (weak_ms * 1e-3) / 1e12
+    e2e_value = flops_step * args.steps / (e2e_ms * 1e-3) / 1e12
+    peak, hbm, peak_src = measured_peaks()
+    achieved = flops_step / (gemm_ms * 1e-3) / 1e12
+
+    configs = None
+    cpu = None
+    if world == 1:
+        configs = measure_configs(be, ext, flush, args, peak, hbm, peak_src)
     if rank == 0:
-        cpu = None
         if world == 1 and not args.no_cpu_baseline:
             rows = args.cpu_rows
-            idx = cpu_sample_rows(m, rows)
+            idx = cpu_sample_rows(M, rows)
             dt = run_cpu_linear_set(ws, x, idx, threads=1)
             cpu = {"value": step_flops(rows) / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
-                   "sample": f"{rows} of {m} token rows through all four linears, single thread "
+                   "sample": f"{rows} of {M} token rows through all four linears, single thread "
                              f"({dt:.1f} s); CpuBackend::linear restated in C (oracle/)"}
         clocks = clk.summary()
         line = {
             "metric": "fp8_linear_set_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens_per_gpu": m, "global_tokens": m * world, "dim": DIM,
+            "config": {"workload": WORKLOAD, "tokens": M, "tokens_per_gpu": m, "dim": DIM,
                        "ffn": FFN, "weights": "fp8-e4m3 group-128 (reference quantizer)",
                        "linears": [f"{nm} {k}->{n}{' gelu' if a else ''}" for nm, n, k, a, _ in LINEARS]
                        + ["ffn2 fused gated residual into f32 h"],
                        "l2": "flushed (256 MB write) before every timed step, outside the timed region",
-                       "parallelism": f"dp{world} (token rows; weights replicated; no collective)"},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * m * DIM * 4,
-                    "d2h_bytes_per_step": m * DIM * 4,
-                    "path": "C ABI, steps pipelined: lx2v_buf_write_f32 x and h from pinned host (copy "
+                       "parallelism": f"dp{world}: the chunk's token rows split over the ranks, weights "
+                                      f"replicated, no collective in the data path"},
+            "weak": {"value": weak_value, "unit": "TFLOP/s", "ms_per_step": weak_ms / args.steps,
+                     "note": "every rank runs a whole 4680-token chunk of its own (independent replicas)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * M * DIM * 4,
+                    "d2h_bytes_per_step": M * DIM * 4,
+                    "path": "C ABI, steps pipelined: lx2v_buf_write_f32 x and h rows from pinned host (copy "
                             "stream), 4 linears, lx2v_buf_download_f32_async h; h alternates between two "
                             "device buffers; one event pair around all steps, no L2 flush (each step's "
-                            "inputs arrive from the host)"},
+                            "inputs arrive from the host); bytes summed over ranks"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": f"bf16 dense burst, {peak_src}",
                          "traffic": profile_traffic(),
                          "kernel": "gemm_ss_pair_kernel (tcgen05.mma cta_group::2, both operands TMA-staged in "
-                                   "shared memory) after dequant_bf16_kernel<FP8>; achieved counts both kernels' time",
+                                   "shared memory) after dequant_bf16_kernel<FP8>; achieved counts both kernels' "
+                                   "time, on a whole 4680-token chunk",
                          "per_linear": per_kernel},
+            "tp_ffn": tp,
+            "configs": configs,
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
 
-    del pairs
     if dist:
         dist.barrier()
         dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------------------------
-def config_arm(args, local_rank: int):
-    """The other BASELINE configs as single-GPU parity/throughput cases, one JSON
-    line per shape: C1 (Q8 FFN up-projection, M = 1560) and the C3 Q4 sweep
-    (M in {1, 16, 256, 1560, 4680, 18720} at K x N = 1536 x 8960 and
-    8960 x 1536). Device-resident inputs, one CUDA-event pair per call on the
-    library's stream, L2 flushed (256 MB write) before every call outside the
-    timed region. M <= 16 is judged against HBM bandwidth (weight bytes + x +
-    y per call), larger M against the bf16 dense tensor peak."""
-    import torch
-    from lightx2v_cuda import BF16, F32, CudaBackend, quant, rng
+def tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barrier):
+    """The chunk's FFN (M = 4680: 1536 -> 8960 GELU -> 1536 + gated residual,
+    Q8 weights) tensor-parallel over the ranks (lightx2v_cuda/tp.py: FFN1
+    column-split, FFN2 row-split, the partials summed over NVLink): strong
+    scaling, the same total work at every N. Time per step = max over ranks
+    of the mean CUDA-event time, L2 flushed before each step. Rank 0 also runs
+    the unsplit FFN on its own GPU and reports the rel-L2 of the split one's
+    h update against it."""
+    from lightx2v_cuda import BF16, F32, Act, quant, rng
+    from lightx2v_cuda.tp import TensorParallelFFN
+    if world > 1:
+        uid = [be.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.comm_init(uid[0], rank, world)
+    m = M_TOKENS
+    # Q8: the kernels' work per element is the FP8 set's apart from the decode
+    # pass, and the reference's FP8 quantizer's NaN codes would make every
+    # row of the summed h NaN (nothing left to compare)
+    w1 = quant.Q8.quantize(rng.normal(103, FFN * DIM, 0.02), FFN, DIM)
+    w2 = quant.Q8.quantize(rng.normal(104, DIM * FFN, 0.02), DIM, FFN)
+    b1, b2 = rng.normal(1103, FFN, 0.01), rng.normal(1104, DIM, 0.01)
+    ffn = TensorParallelFFN(be, rank, world, w1, b1, w2, b2)
+    x, h0 = rng.normal(11, m * DIM), rng.normal(12, m * DIM)
+    xb = be.upload(x, BF16)
+    hb = be.upload(h0, F32)
+    mb = be.upload(rng.normal(13, 6 * DIM, 0.01), F32)
+    for _ in range(max(args.warmup, 3)):
+        ffn.forward(xb, m, hb, mb, GATE_FFN)
+    barrier()
+    ms = float(np.mean(timed_steps(be, ext, flush, lambda: ffn.forward(xb, m, hb, mb, GATE_FFN), args.steps)))
+    barrier()
+    # parity: one more step from a fresh h on every rank, against the unsplit FFN
+    be.write(hb, h0)
+    ffn.forward(xb, m, hb, mb, GATE_FFN)
+    got = be.download(hb)
+    rel = None
+    if rank == 0:
+        d1, d2 = be.weight_q8(w1), be.weight_q8(w2)
+        hid = be.alloc(m * FFN, BF16)
+        be.linear(xb, 0, m, d1, be.upload(b1, F32), Act.GELU_TANH, hid, 0)
+        hr = be.upload(h0, F32)
+        be.linear_gate_residual(hid, 0, m, d2, be.upload(b2, F32), Act.NONE, hr, 0, mb, GATE_FFN)
+        want = be.download(hr) - h0
+        upd = got - h0
+        fin = ~np.isnan(want)
+        rel = float(np.linalg.norm(upd[fin] - want[fin]) / np.linalg.norm(want[fin]))
+    (ms,) = max_over_ranks([ms])
+    flops = 2.0 * 2.0 * m * DIM * FFN
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "scaling": "strong",
+            "n_gpus": world, "rel_l2_vs_one_gpu": rel,
+            "collective": ffn.collective_desc(),
+            "workload": f"FFN of the 1.3B chunk, M={m}: {DIM}->{FFN} GELU -> {DIM} + gated residual into f32 h, "
+                        "Q8 weights; FFN1 column-split, FFN2 row-split",
+            "timing": "max over ranks of the mean CUDA-event time per step; L2 flushed before each"}
 
-    torch.cuda.set_device(local_rank)
-    be = CudaBackend(local_rank)
-    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
-    peak, hbm, src = measured_peaks()
-    if args.config == "c1":
-        cases = [("q8", 1560, 1536, 8960)]
-    else:
-        cases = [("q4", m, k, n) for (k, n) in ((1536, 8960), (8960, 1536))
-                 for m in (1, 16, 256, 1560, 4680, 18720)]
+
+# ---------------------------------------------------------------------------------------------
+def measure_configs(be, ext, flush, args, peak, hbm, src, which=("c1", "c3")):
+    """The other BASELINE configs on one GPU: C1 (Q8 FFN up-projection,
+    M = 1560, bias, f32 out) and the C3 Q4 sweep (group 64, HQQ on, quantized
+    once) at M in {1, 16, 4680} (`--config c3` runs the whole sweep) at
+    K x N = 1536 x 8960 and 8960 x 1536. Device-resident inputs, one
+    CUDA-event pair per call on the library's stream, L2 flushed (256 MB
+    write) before every call outside the timed region. M <= 16 is judged
+    against HBM bandwidth (weight bytes + x + y per call), larger M against
+    the bf16 dense tensor peak. The few-token entries add a dependent chain of
+    40 linears replayed as a CUDA graph."""
+    from lightx2v_cuda import BF16, F32, quant, rng
+    cases = []
+    if "c1" in which:
+        cases.append(("c1", "q8", 1560, 1536, 8960))
+    if "c3" in which:
+        ms_ = (1, 16, 4680) if "c3full" not in which else (1, 16, 256, 1560, 4680, 18720)
+        if getattr(args, "m", None):
+            ms_ = tuple(m for m in ms_ if m in args.m)
+        cases += [("c3", "q4", m, k, n) for (k, n) in ((1536, 8960), (8960, 1536)) for m in ms_]
     weights, hostq = {}, {}
-    for fmt, m, k, n in cases:
+    for _c, fmt, m, k, n in cases:
         if (fmt, k, n) in weights:
             continue
-        w = rng.normal(7 + k, n * k, 0.02)
-        if fmt == "q8":
-            q = quant.Q8.quantize(w, n, k)
+        if fmt == "q8":  # C1: W seed 2, N(0, 0.02)
+            q = quant.Q8.quantize(rng.normal(2, n * k, 0.02), n, k)
             wbytes = n * k + n * (k // q.group) * 4
             weights[(fmt, k, n)] = (be.weight_q8(q), wbytes, "Q8 (reference quantizer)")
         else:
-            # HQQ refinement changes the scale/zero values, not the packed
-            # format or the kernel's work; skipped to keep the run short
-            q = quant.Q4.quantize(w, n, k, 64, False)
+            q = quant.Q4.quantize(rng.normal(7 + k, n * k, 0.02), n, k, 64, True)
             wbytes = n * k // 2 + n * (k // 64) * 4
-            weights[(fmt, k, n)] = (be.weight_q4(q), wbytes, "Q4 group 64 (reference quantizer, HQQ off)")
+            weights[(fmt, k, n)] = (be.weight_q4(q), wbytes, "Q4 group 64, HQQ on (reference quantizer)")
         hostq[(fmt, k, n)] = q
-    for fmt, m, k, n in cases:
+    out = {}
+    for cname, fmt, m, k, n in cases:
         dw, wbytes, wdesc = weights[(fmt, k, n)]
-        xb = be.upload(rng.normal(11, m * k))
-        bb = be.upload(rng.normal(12, n, 0.01), F32)
+        if cname == "c1":
+            xb, bb = be.upload(rng.normal(1, m * k)), be.upload(rng.normal(3, n, 0.01), F32)
+        else:
+            xb, bb = be.upload(rng.normal(11, m * k)), be.upload(rng.normal(12, n, 0.01), F32)
         y_f32 = fmt == "q8"
         yb = be.alloc(m * n, F32 if y_f32 else BF16)
         for _ in range(max(args.warmup, 3)):
             be.linear(xb, 0, m, dw, bb, 0, yb, 0)
         be.sync()
-        evs = []
-        steps = args.steps if m < 4680 else max(3, args.steps // 4)
-        for _ in range(steps):
-            with torch.cuda.stream(ext):
-                flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(ext)
-            be.linear(xb, 0, m, dw, bb, 0, yb, 0)
-            b.record(ext)
-            evs.append((a, b))
-        be.sync()
-        ms = float(np.median([a.elapsed_time(b) for a, b in evs]))
+        steps = args.steps if m < 4680 else max(3, args.steps // 2)
+        ms = float(np.median(timed_steps(be, ext, flush, lambda: be.linear(xb, 0, m, dw, bb, 0, yb, 0), steps)))
         flops = 2.0 * m * n * k
         nbytes = wbytes + m * k * 2 + m * n * (4 if y_f32 else 2) + n * 4
         tflops = flops / (ms * 1e-3) / 1e12
         gbs = nbytes / (ms * 1e-3) / 1e9
         small = m <= 16
-        line = {"config": args.config, "workload": f"{fmt} linear M={m} K={k} N={n}", "weights": wdesc,
-                "ms": ms, "tflops": tflops, "gbs": gbs, "steps": steps, "data": "synthetic",
-                "l2": "flushed (256 MB write) before every call, outside the timed region",
-                "path": "few-token kernel" if small else ("two-pass (decode + gemm_ss_pair_kernel)"
-                                                          if m >= 1024 else "tensor-core single-CTA kernel"),
-                "roofline": {"bound": "hbm" if small else "tensor",
-                             "achieved": gbs if small else tflops,
-                             "peak": hbm if small else peak, "unit": "GB/s" if small else "TFLOP/s",
-                             "frac": (gbs / hbm) if small else (tflops / peak), "peak_source": src,
-                             "bytes_per_call": nbytes}}
-        if small and fmt == "q4" and (fmt, 8960, 1536) in hostq and (fmt, 1536, 8960) in hostq and k == 1536:
-            line["chain"] = q4_chain(be, ext, hostq, m, hbm)
-        print(json.dumps(line), flush=True)
+        entry = {"workload": f"{fmt} linear M={m} K={k} N={n}", "weights": wdesc, "ms": ms, "tflops": tflops,
+                 "gbs": gbs, "steps": steps,
+                 "path": "few-token kernel (gemv_kernel)" if small else
+                 ("two-pass (dequant_bf16_kernel + gemm_ss_pair_kernel)" if m >= 1024 else "tensor-core"),
+                 "roofline": {"bound": "hbm" if small else "tensor", "achieved": gbs if small else tflops,
+                              "peak": hbm if small else peak, "unit": "GB/s" if small else "TFLOP/s",
+                              "frac": (gbs / hbm) if small else (tflops / peak), "peak_source": src,
+                              "bytes_per_call": nbytes}}
+        if small and fmt == "q4" and k == 1536 and ("q4", 8960, 1536) in hostq:
+            entry["chain"] = q4_chain(be, ext, hostq, m, hbm)
+        out[f"{cname}_m{m}_k{k}_n{n}"] = entry
         del xb, bb, yb
+    return out
+
+
+def config_arm(args, local_rank: int):
+    """`--config c1` / `--config c3`: one JSON line per shape (c3 runs the whole
+    M sweep, M in {1, 16, 256, 1560, 4680, 18720})."""
+    import torch
+    from lightx2v_cuda import CudaBackend
+    torch.cuda.set_device(local_rank)
+    be = CudaBackend(local_rank)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    peak, hbm, src = measured_peaks()
+    which = ("c1",) if args.config == "c1" else ("c3", "c3full")
+    for name, entry in measure_configs(be, ext, flush, args, peak, hbm, src, which).items():
+        print(json.dumps({"config": args.config, "case": name, "data": "synthetic",
+                          "l2": "flushed (256 MB write) before every call, outside the timed region", **entry}),
+              flush=True)
 
 
 def q4_chain(be, ext, hostq, m, hbm):
@@ -560,7 +677,7 @@ def q4_chain(be, ext, hostq, m, hbm):
         torch.cuda.current_stream().synchronize()
         evs = []
         for _ in range(10):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0, e1 = ev(), ev()
             e0.record(ext)
             g.replay()
             e1.record(ext)
@@ -574,92 +691,25 @@ def q4_chain(be, ext, hostq, m, hbm):
             "note": "one CUDA graph of 40 dependent linears; weight bytes only in the GB/s"}
 
 
-# ---------------------------------------------------------------------------------------------
-def tpffn_arm(args, rank: int, world: int, local_rank: int):
-    """The chunk's FFN (M = 4680, 1536 -> 8960 GELU -> 1536 + gated residual, Q8)
-    tensor-parallel over the torchrun ranks (lightx2v_cuda/tp.py: FFN1
-    column-split, FFN2 row-split, one NCCL all-reduce through the C ABI):
-    strong scaling, the same total work at every N. Time per step = max over
-    ranks of CUDA-event times on each library stream, L2 flushed before every
-    step outside the timed region."""
-    import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-    from lightx2v_cuda import BF16, F32, CudaBackend, quant, rng
-    from lightx2v_cuda.tp import TensorParallelFFN
-
-    torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("gloo", timeout=timedelta(seconds=300))  # id exchange and timing max
-    be = CudaBackend(local_rank)
-    if world > 1:
-        uid = [be.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        be.comm_init(uid[0], rank, world)
-    m = M_TOKENS
-    # Q8 (quantized in well under a second; the kernels' work per element is
-    # the same as FP8's apart from the decode pass)
-    w1 = quant.Q8.quantize(rng.normal(103, FFN * DIM, 0.02), FFN, DIM)
-    w2 = quant.Q8.quantize(rng.normal(104, DIM * FFN, 0.02), DIM, FFN)
-    ffn = TensorParallelFFN(be, rank, world, w1, rng.normal(1103, FFN, 0.01), w2, rng.normal(1104, DIM, 0.01))
-    xb = be.upload(rng.normal(11, m * DIM), BF16)
-    hb = be.upload(rng.normal(12, m * DIM), F32)
-    mb = be.upload(rng.normal(13, 6 * DIM, 0.01), F32)
-    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
-    for _ in range(max(args.warmup, 3)):
-        ffn.forward(xb, m, hb, mb, GATE_FFN)
-    be.sync()
-    if world > 1:
-        dist.barrier()
-    evs = []
-    for _ in range(args.steps):
-        with torch.cuda.stream(ext):
-            flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(ext)
-        ffn.forward(xb, m, hb, mb, GATE_FFN)
-        b.record(ext)
-        evs.append((a, b))
-    be.sync()
-    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    flops = 2.0 * 2.0 * m * DIM * FFN
-    if rank == 0:
-        print(json.dumps({"config": "tpffn", "metric": "tp_ffn_tflops", "value": flops / (ms * 1e-3) / 1e12,
-                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "ms_per_step": ms,
-                          "scaling": "strong", "dtype": "bf16", "data": "synthetic",
-                          "workload": f"FFN of the 1.3B chunk, M={m}: {DIM}->{FFN} GELU -> {DIM} + gated residual, "
-                                      "Q8 weights; FFN1 column-split, FFN2 row-split, NCCL all-reduce (f32)",
-                          "timing": "max over ranks of the mean CUDA-event time per step; L2 flushed before each"}),
-              flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "tpffn"],
-                    help="c2 (default): the headline FP8 linear set; c1 / c3: the other configs, one line per "
-                         "shape; tpffn: the chunk's FFN tensor-parallel over the torchrun ranks")
+    ap.add_argument("--m", type=int, nargs="*", default=None,
+                    help="with --config c3: only these token counts of the sweep")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
+                    help="c2 (default): the headline FP8 linear set, with C1 / C3 and the tensor-parallel FFN as "
+                         "extra keys; c1 / c3: those configs alone, one line per shape (c3: the whole M sweep)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
-    elif args.config == "tpffn":
-        tpffn_arm(args, rank, world, local_rank)
     elif args.config != "c2":
         if rank == 0:
             config_arm(args, local_rank)

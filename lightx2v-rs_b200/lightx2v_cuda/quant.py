@@ -13,6 +13,7 @@ restatement in oracle/ on BASELINE-sized matrices.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -86,6 +87,62 @@ def _f16(x: np.ndarray) -> np.ndarray:
     return x.astype(np.float16).astype(_F32)
 
 
+def _hqq_block(g: np.ndarray, is_: np.ndarray, z: np.ndarray) -> np.ndarray:
+    """HQQ zero refinement (quant.rs:248-276) of a block of groups: rows of g
+    with their inverse scales and initial zeros; returns the best zeros.
+    Each group iterates on its own, so only the groups still improving are
+    computed in each round (most stop within a few rounds)."""
+    p, kappa = _F32(0.7), _F32(1.01)
+    pm1 = np.float64(p - _F32(1.0))
+    n = _F32(g.shape[1])
+    z = z.copy()
+    best_z = z.copy()
+    best = np.full(z.shape, _F32(3.4028235e38), _F32)
+    beta = np.full(z.shape, _F32(10.0), _F32)
+    idx = np.arange(z.size)
+    for _ in range(20):
+        gi, si, zi, bi = g[idx], is_[idx], z[idx], beta[idx]
+        v = (gi * si[:, None]).astype(_F32) + zi[:, None]
+        c = np.clip(_round_away(v.astype(_F32)), _F32(0.0), _F32(15.0))
+        r = ((c - zi[:, None]) / si[:, None]).astype(_F32)
+        e = (gi - r).astype(_F32)
+        a = np.abs(e)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            pw = np.power(a.astype(np.float64), pm1).astype(_F32)
+            t = np.fmax((a - (pw / bi[:, None]).astype(_F32)).astype(_F32), _F32(0.0))
+        sh = np.where(a > 0, np.where(e > 0, t, -t), _F32(0.0)).astype(_F32)
+        term = (c - ((gi - sh).astype(_F32) * si[:, None]).astype(_F32)).astype(_F32)
+        err = np.zeros(idx.size, _F32)
+        zsum = np.zeros(idx.size, _F32)
+        for i in range(g.shape[1]):  # sequential f32 sums, as the reference
+            err = (err + a[:, i]).astype(_F32)
+            zsum = (zsum + term[:, i]).astype(_F32)
+        err = (err / n).astype(_F32)
+        upd = ~(err >= best[idx])
+        idx = idx[upd]
+        if idx.size == 0:
+            break
+        best[idx] = err[upd]
+        best_z[idx] = zi[upd]
+        z[idx] = (zsum[upd] / n).astype(_F32)
+        beta[idx] = (bi[upd] * kappa).astype(_F32)
+    return best_z
+
+
+def _hqq_zeros(g: np.ndarray, is_: np.ndarray, z: np.ndarray) -> np.ndarray:
+    """_hqq_block over blocks of groups on a thread pool (numpy's array
+    operations release the GIL); results do not depend on the split."""
+    blocks = max(1, min(os.cpu_count() or 1, 16, g.shape[0] // 4096))
+    if blocks == 1:
+        return _hqq_block(g, is_, z)
+    from concurrent.futures import ThreadPoolExecutor
+    cuts = np.linspace(0, g.shape[0], blocks + 1).astype(int)
+    with ThreadPoolExecutor(blocks) as ex:
+        parts = list(ex.map(lambda i: _hqq_block(g[cuts[i]:cuts[i + 1]], is_[cuts[i]:cuts[i + 1]],
+                                                   z[cuts[i]:cuts[i + 1]]), range(blocks)))
+    return np.concatenate(parts)
+
+
 @dataclass
 class Q4:
     """`Q4` (quant.rs:212-356): 4-bit codes (one per byte in memory) with an f16-exact
@@ -114,39 +171,7 @@ class Q4:
             return np.clip(_round_away(v.astype(_F32)), _F32(0.0), _F32(15.0))
 
         if hqq:  # quant.rs:248-276, vectorised across groups
-            p, kappa = _F32(0.7), _F32(1.01)
-            pm1 = np.float64(p - _F32(1.0))
-            beta = np.full(z.shape, _F32(10.0), _F32)
-            best = np.full(z.shape, _F32(3.4028235e38), _F32)
-            best_z = z.copy()
-            active = np.ones(z.shape, bool)
-            n = _F32(group)
-            for _ in range(20):
-                c = code(z)
-                r = ((c - z[:, None]) / is_[:, None]).astype(_F32)
-                e = (g - r).astype(_F32)
-                a = np.abs(e)
-                with np.errstate(divide="ignore", invalid="ignore"):
-                    pw = np.power(a.astype(np.float64), pm1).astype(_F32)
-                    t = np.fmax((a - (pw / beta[:, None]).astype(_F32)).astype(_F32), _F32(0.0))
-                sh = np.where(a > 0, np.where(e > 0, t, -t), _F32(0.0)).astype(_F32)
-                term = (c - ((g - sh).astype(_F32) * is_[:, None]).astype(_F32)).astype(_F32)
-                err = np.zeros(z.shape, _F32)
-                zsum = np.zeros(z.shape, _F32)
-                for i in range(group):  # sequential f32 sums, as the reference
-                    err = (err + a[:, i]).astype(_F32)
-                    zsum = (zsum + term[:, i]).astype(_F32)
-                err = (err / n).astype(_F32)
-                stop = err >= best
-                upd = active & ~stop
-                best = np.where(upd, err, best)
-                best_z = np.where(upd, z, best_z)
-                z = np.where(upd, (zsum / n).astype(_F32), z)
-                beta = np.where(upd, (beta * kappa).astype(_F32), beta)
-                active = upd
-                if not active.any():
-                    break
-            z = best_z
+            z = _hqq_zeros(g, is_, z)
         q = _as_u8(code(z))
         scales = _f16((_F32(1.0) / is_).astype(_F32))
         zeros = _f16(z)

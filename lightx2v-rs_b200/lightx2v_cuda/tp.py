@@ -89,6 +89,12 @@ class TensorParallelFFN:
         self.b2 = be.upload(np.asarray(b2, np.float32), L.F32) if rank == 0 else None
         self._bufs = {}
 
+    def collective_desc(self) -> str:
+        if self.world == 1:
+            return "none (one rank)"
+        return (f"one NCCL all-reduce (sum) of the f32 [rows, {self.dim}] FFN2 partials per step, on the "
+                "backend's stream")
+
     def _scratch(self, rows: int):
         if rows not in self._bufs:
             self._bufs[rows] = (self.be.alloc(rows * self.local, L.BF16), self.be.alloc(rows * self.dim, L.F32))
