@@ -691,6 +691,44 @@ def q4_chain(be, ext, hostq, m, hbm):
             "note": "one CUDA graph of 40 dependent linears; weight bytes only in the GB/s"}
 
 
+def attention_arm(args, local_rank: int):
+    """`--config attn`: the causal attention of one 1.3B chunk layer (12 heads x
+    128, 4680 queries of latent frames 9-11 against a 12-frame cache of 18720
+    keys, key visible when its frame <= the query's: the MemRoPE mask of
+    dit.rs:645-657) through lx2v_causal_attention_temporal; bf16 q/k/v,
+    device-resident, CUDA events per call, L2 flushed before each. FLOPs:
+    4 * d per visible (query, key) pair and head (QK^T and PV)."""
+    import torch
+    from lightx2v_cuda import BF16, CudaBackend, rng
+    torch.cuda.set_device(local_rank)
+    be = CudaBackend(local_rank)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    heads, d, frame = 12, 128, 1560
+    sq, sk = 3 * frame, 12 * frame
+    qb = be.upload(rng.normal(71, heads * sq * d), BF16)
+    kb = be.upload(rng.normal(72, heads * sk * d), BF16)
+    vb = be.upload(rng.normal(73, heads * sk * d), BF16)
+    ob = be.alloc(sq * heads * d, BF16)
+    tq = (9 + np.arange(sq) // frame).astype(np.int32)
+    tk = (np.arange(sk) // frame).astype(np.int32)
+    visible = int(sum(int(np.sum(tk <= t)) for t in (9, 10, 11)) * frame)
+    for _ in range(max(args.warmup, 3)):
+        be.causal_attention_temporal(qb, kb, vb, heads, sq, sk, d, tq, tk, ob)
+    be.sync()
+    ms = float(np.median(timed_steps(be, ext, flush, lambda: be.causal_attention_temporal(
+        qb, kb, vb, heads, sq, sk, d, tq, tk, ob), args.steps)))
+    peak, _hbm, src = measured_peaks()
+    flops = 4.0 * d * heads * visible
+    dense = 4.0 * d * heads * sq * sk
+    print(json.dumps({"config": "attn", "workload": "causal attention, 1.3B chunk layer: 12 heads x 128, sq 4680, "
+                                                   "sk 18720, frame-causal mask", "ms": ms,
+                      "tflops": flops / (ms * 1e-3) / 1e12, "dense_equivalent_tflops": dense / (ms * 1e-3) / 1e12,
+                      "visible_fraction": visible / (sq * sk), "roofline": {"bound": "tensor", "peak": peak,
+                      "frac": flops / (ms * 1e-3) / 1e12 / peak, "peak_source": src}, "steps": args.steps}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -701,7 +739,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--m", type=int, nargs="*", default=None,
                     help="with --config c3: only these token counts of the sweep")
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn"],
                     help="c2 (default): the headline FP8 linear set, with C1 / C3 and the tensor-parallel FFN as "
                          "extra keys; c1 / c3: those configs alone, one line per shape (c3: the whole M sweep)")
     args = ap.parse_args()
@@ -710,6 +748,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+    elif args.config == "attn":
+        if rank == 0:
+            attention_arm(args, local_rank)
     elif args.config != "c2":
         if rank == 0:
             config_arm(args, local_rank)

@@ -164,6 +164,32 @@ LX2V_API lx2v_status lx2v_linear_gate_residual(lx2v_ctx *ctx, const lx2v_buf *x,
 LX2V_API lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_buf *a, size_t rows,
                                size_t dim, const lx2v_buf *mods, size_t gate);
 
+/* ---- attention (backend.rs:275-307) ------------------------------------- */
+/* Backend::attention: softmax attention, scale 1/sqrt(head_dim), no mask.
+ * q is [heads, sq, head_dim], k and v [heads, sk, head_dim]; out is written
+ * with the heads merged, [sq, heads * head_dim] (CPU reference
+ * crates/lightx2v-cpu/src/lib.rs:171-208). head_dim 128 with bf16 q/k/v runs
+ * on the tensor cores; other head_dims (<= 256) and f32 buffers run a
+ * CUDA-core kernel (at most 51,168 keys). */
+LX2V_API lx2v_status lx2v_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k, const lx2v_buf *v,
+                                    size_t heads, size_t sq, size_t sk, size_t head_dim, lx2v_buf *out);
+/* Backend::causal_attention: the same with a block mask. `mask` is host
+ * memory, [sq][sk] row-major, one byte per pair (nonzero = allowed, the
+ * reference's `true`), or NULL (no mask). A query that may see no key gets
+ * NaN, as the reference's softmax of an all -inf row does. */
+LX2V_API lx2v_status lx2v_causal_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k,
+                                           const lx2v_buf *v, size_t heads, size_t sq, size_t sk,
+                                           size_t head_dim, const uint8_t *mask, lx2v_buf *out);
+/* No counterpart in the reference: causal_attention with the mask that
+ * LightDit::forward_chunk builds (crates/lightx2v-model/src/dit.rs:645-657),
+ * key k visible to query q when tk[k] <= tq[q], given as the temporal
+ * indices (host int32 [sq] and [sk]) instead of an sq x sk boolean array.
+ * Key blocks that no query of a tile can see are skipped. */
+LX2V_API lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k,
+                                                    const lx2v_buf *v, size_t heads, size_t sq, size_t sk,
+                                                    size_t head_dim, const int32_t *tq, const int32_t *tk,
+                                                    lx2v_buf *out);
+
 /* ---- profiling (backend.rs:192-196) -------------------------------------- */
 /* Backend::profile_report: per-op device time since the last reset, as JSON
  * {"op": {"calls": n, "ms": t}, ...}. Profiling is on when the context was

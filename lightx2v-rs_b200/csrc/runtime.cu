@@ -8,7 +8,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -23,6 +25,7 @@
 #include "../../include/lightx2v_cuda.h"
 #include "dequant.cuh"
 #include "gemm.h"
+#include "attention.h"
 
 using namespace lx2v;
 
@@ -59,6 +62,11 @@ struct lx2v_ctx {
     size_t gemv_ws_floats = 0;
     int *gemv_arrivals = nullptr;
     size_t gemv_tiles = 0;
+    void *att_ws = nullptr;      // attention: V^T copy, mask bits / temporal indices
+    size_t att_ws_bytes = 0;
+    void *att_host = nullptr;    // page-locked staging of the mask data (reused once its copy is done)
+    size_t att_host_bytes = 0;
+    cudaEvent_t att_host_ev = nullptr;
     uint64_t launches = 0;
     bool profile = false;
     std::map<std::string, ProfEntry> prof;
@@ -348,6 +356,9 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
+    if (ctx->att_ws) cudaFree(ctx->att_ws);
+    if (ctx->att_host) cudaFreeHost(ctx->att_host);
+    if (ctx->att_host_ev) cudaEventDestroy(ctx->att_host_ev);
     for (void *b : ctx->dq_ws)
         if (b) cudaFree(b);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
@@ -1071,6 +1082,217 @@ extern "C" lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v
     ctx->launches++;
     CUDA_TRY(ctx, note_uses(ctx, {h, a, mods}));
     return LX2V_OK;
+}
+
+// ---- attention (backend.rs:275-307) ------------------------------------------------------
+// Grow-only workspace of the attention calls (V^T and the mask data).
+static lx2v_status ensure_att_workspace(lx2v_ctx *ctx, size_t bytes) {
+    if (ctx->att_ws_bytes >= bytes) return LX2V_OK;
+    if (ctx->att_ws) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->att_ws);
+        ctx->att_ws = nullptr;
+        ctx->att_ws_bytes = 0;
+    }
+    CUDA_TRY(ctx, cudaMalloc(&ctx->att_ws, bytes));
+    ctx->att_ws_bytes = bytes;
+    return LX2V_OK;
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Page-locked staging for the mask data of an attention call: the copy from
+// it runs asynchronously, and the next call waits for that copy (an event)
+// before it writes the staging again.
+static lx2v_status att_host_staging(lx2v_ctx *ctx, size_t bytes, void **out) {
+    if (!ctx->att_host_ev) CUDA_TRY(ctx, cudaEventCreateWithFlags(&ctx->att_host_ev, cudaEventDisableTiming));
+    CUDA_TRY(ctx, cudaEventSynchronize(ctx->att_host_ev));
+    if (ctx->att_host_bytes < bytes) {
+        if (ctx->att_host) cudaFreeHost(ctx->att_host);
+        ctx->att_host = nullptr;
+        ctx->att_host_bytes = 0;
+        CUDA_TRY(ctx, cudaMallocHost(&ctx->att_host, bytes));
+        ctx->att_host_bytes = bytes;
+    }
+    *out = ctx->att_host;
+    return LX2V_OK;
+}
+
+// Everything the attention launch needs besides q / k / v / out: which mask,
+// and its host data (a row-major bool mask, or the temporal indices).
+struct AttnMaskArgs {
+    int mode = ATT_MASK_NONE;
+    const uint8_t *mask = nullptr;  // [sq][sk] bool, nonzero = allowed
+    const int32_t *tq = nullptr;    // [sq]
+    const int32_t *tk = nullptr;    // [sk]
+};
+
+// q [heads][q_rows][d] (the first sq rows of each head are the queries),
+// k / v [heads][k_rows][d] (the first sk rows are the keys), out [sq][heads*d].
+static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void *q, int q_f32, size_t q_rows,
+                                   const void *k, const void *v, int kv_f32, size_t k_rows, size_t heads, size_t sq,
+                                   size_t sk, size_t d, const AttnMaskArgs &m, lx2v_buf *out) {
+    if (heads == 0 || sq == 0) return LX2V_OK;
+    if (sk == 0) return fail(ctx, LX2V_ERR_INVALID, "attention over zero keys");
+    if (heads * d > (1u << 20) || sq > (1u << 24) || sk > (1u << 24))
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "attention shape too large");
+    OpScope ps(ctx, opname);
+    const bool tc = d == 128 && !q_f32 && !kv_f32;
+    const size_t sk_pad = align_up(sk, 128);
+    const size_t n_qt = (sq + 127) / 128, n_kb = sk_pad / 128;
+    // workspace: [V^T bf16 heads*128*sk_pad][mask bits sq*words u32 | tq, tk, tq ranges, tk ranges]
+    const size_t vt_bytes = tc ? align_up(heads * 128 * sk_pad * 2, 256) : 0;
+    const size_t words = (sk + 31) / 32;
+    size_t mask_bytes = 0;
+    if (m.mode == ATT_MASK_BITS) mask_bytes = sq * words * 4;
+    else if (m.mode == ATT_MASK_TEMPORAL) mask_bytes = (sq + sk) * 4 + (n_qt + n_kb) * 8;
+    lx2v_status s = ensure_att_workspace(ctx, vt_bytes + align_up(mask_bytes, 256) + 256);
+    if (s) return s;
+    char *ws = (char *)ctx->att_ws;
+    char *mws = ws + vt_bytes;
+    const uint32_t *bits_dev = nullptr;
+    const int *tq_dev = nullptr, *tk_dev = nullptr;
+    const int2 *tqr_dev = nullptr, *tkr_dev = nullptr;
+    if (m.mode == ATT_MASK_BITS) {
+        void *stage = nullptr;
+        if ((s = att_host_staging(ctx, mask_bytes, &stage))) return s;
+        uint32_t *bits = (uint32_t *)stage;
+        memset(bits, 0, mask_bytes);
+        for (size_t i = 0; i < sq; ++i)
+            for (size_t j = 0; j < sk; ++j)
+                if (m.mask[i * sk + j]) bits[i * words + j / 32] |= 1u << (j % 32);
+        CUDA_TRY(ctx, cudaMemcpyAsync(mws, bits, mask_bytes, cudaMemcpyHostToDevice, ctx->stream));
+        CUDA_TRY(ctx, cudaEventRecord(ctx->att_host_ev, ctx->stream));
+        bits_dev = (const uint32_t *)mws;
+    } else if (m.mode == ATT_MASK_TEMPORAL) {
+        void *stage = nullptr;
+        if ((s = att_host_staging(ctx, mask_bytes, &stage))) return s;
+        int32_t *host = (int32_t *)stage;
+        memcpy(host, m.tq, sq * 4);
+        memcpy(host + sq, m.tk, sk * 4);
+        int32_t *tqr = host + sq + sk, *tkr = tqr + 2 * n_qt;
+        for (size_t t = 0; t < n_qt; ++t) {
+            int32_t lo = INT32_MAX, hi = INT32_MIN;
+            for (size_t i = t * 128; i < sq && i < (t + 1) * 128; ++i) {
+                lo = std::min(lo, m.tq[i]);
+                hi = std::max(hi, m.tq[i]);
+            }
+            tqr[2 * t] = lo;
+            tqr[2 * t + 1] = hi;
+        }
+        for (size_t b = 0; b < n_kb; ++b) {
+            int32_t lo = INT32_MAX, hi = INT32_MIN;
+            for (size_t i = b * 128; i < sk && i < (b + 1) * 128; ++i) {
+                lo = std::min(lo, m.tk[i]);
+                hi = std::max(hi, m.tk[i]);
+            }
+            tkr[2 * b] = lo;
+            tkr[2 * b + 1] = hi;
+        }
+        CUDA_TRY(ctx, cudaMemcpyAsync(mws, host, mask_bytes, cudaMemcpyHostToDevice, ctx->stream));
+        CUDA_TRY(ctx, cudaEventRecord(ctx->att_host_ev, ctx->stream));
+        tq_dev = (const int *)mws;
+        tk_dev = tq_dev + sq;
+        tqr_dev = (const int2 *)(tk_dev + sk);
+        tkr_dev = tqr_dev + n_qt;
+    }
+    if (tc) {
+        __nv_bfloat16 *vt = (__nv_bfloat16 *)ws;
+        CUDA_TRY(ctx, transpose_v_launch(v, kv_f32, (int)heads, (int)k_rows, (int)sk, (int)sk_pad, vt, ctx->stream));
+        ctx->launches++;
+        AttnParams p;
+        memset(&p, 0, sizeof p);
+        if ((s = make_map(ctx, &p.tmap_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, heads * q_rows, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+            return s;
+        if ((s = make_map(ctx, &p.tmap_k, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, heads * k_rows, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+            return s;
+        if ((s = make_map(ctx, &p.tmap_vt, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sk_pad, heads * 128, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+            return s;
+        p.out = out->ptr;
+        p.out_f32 = out->dtype == LX2V_F32;
+        p.heads = (int)heads; p.sq = (int)sq; p.sk = (int)sk;
+        p.q_rows = (int)q_rows; p.k_rows = (int)k_rows;
+        p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
+        p.mask_mode = m.mode;
+        p.mask_bits = bits_dev; p.mask_words = (int)words;
+        p.tq = tq_dev; p.tk = tk_dev; p.tq_range = tqr_dev; p.tk_range = tkr_dev;
+        p.err = ctx->err_dev;
+        p.wait_limit_ns = ctx->wait_limit_ns;
+        CUDA_TRY(ctx, attention_tc_launch(p, ctx->stream));
+        ctx->launches++;
+        return LX2V_OK;
+    }
+    if (d > 256) return fail(ctx, LX2V_ERR_UNSUPPORTED, "attention head_dim %zu > 256", d);
+    if ((sk + 32) * 4 > 200 * 1024)
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "attention with head_dim != 128 or f32 operands takes at most %d keys",
+                    200 * 1024 / 4 - 32);
+    AttnSimtParams p;
+    memset(&p, 0, sizeof p);
+    p.q = q; p.k = k; p.v = v;
+    if (q_f32 != kv_f32) return fail(ctx, LX2V_ERR_UNSUPPORTED, "q and k/v must have the same element type");
+    p.qkv_f32 = q_f32;
+    p.out = out->ptr; p.out_f32 = out->dtype == LX2V_F32;
+    p.heads = (int)heads; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+    p.q_rows = (int)q_rows; p.k_rows = (int)k_rows;
+    p.mask_mode = m.mode; p.mask_bits = bits_dev; p.mask_words = (int)words;
+    p.tq = tq_dev; p.tk = tk_dev;
+    CUDA_TRY(ctx, attention_simt_launch(p, ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}
+
+static lx2v_status attention_buffers(lx2v_ctx *ctx, const char *opname, const lx2v_buf *q, const lx2v_buf *k,
+                                     const lx2v_buf *v, size_t heads, size_t sq, size_t sk, size_t d,
+                                     const AttnMaskArgs &m, lx2v_buf *out) {
+    if (!q || !k || !v || !out) return fail(ctx, LX2V_ERR_INVALID, "null q, k, v or output");
+    if (out == q || out == k || out == v) return fail(ctx, LX2V_ERR_INVALID, "output aliases an input");
+    if (k->dtype != v->dtype) return fail(ctx, LX2V_ERR_INVALID, "k and v must have the same element type");
+    if (heads * sq * d > q->len || heads * sk * d > k->len || heads * sk * d > v->len)
+        return fail(ctx, LX2V_ERR_INVALID, "q/k/v hold fewer than heads x rows x head_dim elements");
+    if (sq * heads * d > out->len) return fail(ctx, LX2V_ERR_INVALID, "output holds fewer than sq x heads x head_dim");
+    if (d == 0) return fail(ctx, LX2V_ERR_INVALID, "head_dim 0");
+    lx2v_status s = attention_queue(ctx, opname, q->ptr, q->dtype == LX2V_F32, sq, k->ptr, v->ptr,
+                                    k->dtype == LX2V_F32, sk, heads, sq, sk, d, m, out);
+    if (s) return s;
+    CUDA_TRY(ctx, note_uses(ctx, {q, k, v, out}));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k, const lx2v_buf *v,
+                                      size_t heads, size_t sq, size_t sk, size_t head_dim, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    return attention_buffers(ctx, "attention", q, k, v, heads, sq, sk, head_dim, AttnMaskArgs(), out);
+}
+
+extern "C" lx2v_status lx2v_causal_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k,
+                                             const lx2v_buf *v, size_t heads, size_t sq, size_t sk,
+                                             size_t head_dim, const uint8_t *mask, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    AttnMaskArgs m;
+    if (mask) {
+        m.mode = ATT_MASK_BITS;
+        m.mask = mask;
+    }
+    return attention_buffers(ctx, "causal_attention", q, k, v, heads, sq, sk, head_dim, m, out);
+}
+
+extern "C" lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k,
+                                                      const lx2v_buf *v, size_t heads, size_t sq, size_t sk,
+                                                      size_t head_dim, const int32_t *tq, const int32_t *tk,
+                                                      lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!tq || !tk) return fail(ctx, LX2V_ERR_INVALID, "null temporal indices");
+    AttnMaskArgs m;
+    m.mode = ATT_MASK_TEMPORAL;
+    m.tq = tq;
+    m.tk = tk;
+    return attention_buffers(ctx, "causal_attention", q, k, v, heads, sq, sk, head_dim, m, out);
 }
 
 // ---- profiling / knobs ---------------------------------------------------------------------

@@ -64,6 +64,9 @@ SIGNATURES = {
     "lx2v_linear_gate_residual": (_st, [_vp, _vp, _sz, _sz, _vp, _vp, ctypes.c_int, _vp, _sz,
                                         _vp, _sz]),
     "lx2v_gate_residual": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _sz]),
+    "lx2v_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]),
+    "lx2v_causal_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    "lx2v_causal_attention_temporal": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
     "lx2v_profile_json": (_st, [_vp, ctypes.c_char_p, _sz, ctypes.POINTER(_sz)]),
     "lx2v_profile_reset": (_st, [_vp]),
     "lx2v_set_linear_path": (_st, [_vp, ctypes.c_int]),

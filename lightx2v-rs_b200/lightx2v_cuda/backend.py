@@ -262,6 +262,33 @@ class CudaBackend:
             self._ctx, x.handle, x_row, rows, w.handle,
             bias.handle if bias is not None else None, act, h.handle, h_row, mods.handle, gate))
 
+    def attention(self, q: Buf, k: Buf, v: Buf, heads: int, sq: int, sk: int, head_dim: int, out: Buf):
+        """backend.rs:275-289: softmax(q k^T / sqrt(d)) v per head; q [heads, sq, d],
+        k/v [heads, sk, d], out [sq, heads * d]."""
+        self._check(self._lib.lx2v_attention(self._ctx, q.handle, k.handle, v.handle, heads, sq, sk,
+                                             head_dim, out.handle))
+
+    def causal_attention(self, q: Buf, k: Buf, v: Buf, heads: int, sq: int, sk: int, head_dim: int,
+                         mask, out: Buf):
+        """backend.rs:291-307: `mask` is a [sq, sk] boolean array (True = allowed) or None."""
+        m = None
+        if mask is not None:
+            m = np.ascontiguousarray(np.asarray(mask, dtype=bool).reshape(sq, sk)).view(np.uint8)
+        self._check(self._lib.lx2v_causal_attention(self._ctx, q.handle, k.handle, v.handle, heads, sq, sk,
+                                                    head_dim, m.ctypes.data if m is not None else None,
+                                                    out.handle))
+
+    def causal_attention_temporal(self, q: Buf, k: Buf, v: Buf, heads: int, sq: int, sk: int, head_dim: int,
+                                  tq, tk, out: Buf):
+        """causal_attention with the mask tk[key] <= tq[query] (the DiT's MemRoPE
+        mask, dit.rs:645-657) given by the temporal indices."""
+        tq = np.ascontiguousarray(tq, np.int32)
+        tk = np.ascontiguousarray(tk, np.int32)
+        assert tq.size == sq and tk.size == sk
+        self._check(self._lib.lx2v_causal_attention_temporal(self._ctx, q.handle, k.handle, v.handle, heads,
+                                                             sq, sk, head_dim, tq.ctypes.data,
+                                                             tk.ctypes.data, out.handle))
+
     def gate_residual(self, h: Buf, a: Buf, rows: int, dim: int, mods: Buf, gate: int):
         """In place on h: h += a * mods[gate] (backend.rs:244-253)."""
         self._check(self._lib.lx2v_gate_residual(self._ctx, h.handle, a.handle, rows, dim,

@@ -311,6 +311,139 @@ void orc_gate_residual(float *h, const float *a, size_t rows, size_t dim,
             h[r * dim + j] += a[r * dim + j] * mods[gate * dim + j];
 }
 
+/* ---------------------------------------------------------- attention ---- */
+/* softmax_row, crates/lightx2v-cpu/src/lib.rs:155-166: max by f32::max
+ * (NaN-ignoring, fmaxf), exp of the shifted scores, sequential sum, then a
+ * multiply by the reciprocal. */
+static void orc_softmax_row(float *s, size_t n) {
+    float m = -INFINITY;
+    for (size_t i = 0; i < n; i++) m = fmaxf(m, s[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        s[i] = expf(s[i] - m);
+        sum += s[i];
+    }
+    float inv = 1.0f / sum;
+    for (size_t i = 0; i < n; i++) s[i] *= inv;
+}
+
+/* attention_impl, crates/lightx2v-cpu/src/lib.rs:170-208 (both
+ * CpuBackend::attention and causal_attention, lib.rs:462-494): q is
+ * [heads, sq, d], k / v [heads, sk, d], mask [sq, sk] (nonzero = allowed) or
+ * NULL, out [sq, heads * d]. Scores are sequential-d dot products times
+ * 1/sqrt(d); a forbidden pair scores -inf. `threads` > 1 spreads the
+ * (head, query) rows over OpenMP threads; each row is computed exactly as
+ * the reference computes it. */
+void orc_attention(const float *q, const float *k, const float *v, size_t heads, size_t sq, size_t sk,
+                   size_t d, const uint8_t *mask, float *out, int threads) {
+    const float scale = 1.0f / sqrtf((float)d);
+#ifdef _OPENMP
+    int nt = threads > 0 ? threads : 1;
+#pragma omp parallel num_threads(nt)
+#endif
+    {
+        float *scores = (float *)malloc(sk * sizeof(float));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (long long row = 0; row < (long long)(heads * sq); row++) {
+            const size_t h = (size_t)row / sq, qi = (size_t)row % sq;
+            for (size_t ki = 0; ki < sk; ki++) {
+                if (mask && !mask[qi * sk + ki]) {
+                    scores[ki] = -INFINITY;
+                    continue;
+                }
+                float acc = 0.0f;
+                for (size_t j = 0; j < d; j++) acc += q[(h * sq + qi) * d + j] * k[(h * sk + ki) * d + j];
+                scores[ki] = acc * scale;
+            }
+            orc_softmax_row(scores, sk);
+            for (size_t j = 0; j < d; j++) {
+                float acc = 0.0f;
+                for (size_t ki = 0; ki < sk; ki++) acc += scores[ki] * v[(h * sk + ki) * d + j];
+                out[(qi * heads + h) * d + j] = acc;
+            }
+        }
+        free(scores);
+    }
+}
+
+/* ------------------------------------------------------------- norms ---- */
+/* CpuBackend::layer_norm, crates/lightx2v-cpu/src/lib.rs:328-362. kind 0 =
+ * NormKind::Affine (out = n * w + b), kind 1 = NormKind::Mod (out =
+ * n * (1 + mods[scale * dim + j]) + mods[shift * dim + j]). mean and var
+ * are sequential f32 sums divided by dim. */
+void orc_layer_norm(const float *x, size_t rows, size_t dim, int kind, const float *w, const float *b,
+                    const float *mods, size_t scale, size_t shift, float eps, float *out) {
+    for (size_t r = 0; r < rows; r++) {
+        const float *row = x + r * dim;
+        float sum = 0.0f;
+        for (size_t j = 0; j < dim; j++) sum += row[j];
+        const float mean = sum / (float)dim;
+        float vs = 0.0f;
+        for (size_t j = 0; j < dim; j++) {
+            const float c = row[j] - mean;
+            vs += c * c;
+        }
+        const float var = vs / (float)dim;
+        const float inv = 1.0f / sqrtf(var + eps);
+        for (size_t j = 0; j < dim; j++) {
+            const float n = (row[j] - mean) * inv;
+            out[r * dim + j] = kind == 0 ? n * w[j] + b[j]
+                                         : n * (1.0f + mods[scale * dim + j]) + mods[shift * dim + j];
+        }
+    }
+}
+
+/* CpuBackend::residual_norm, crates/lightx2v-cpu/src/lib.rs:364-392: in place
+ * h += a * mods[gate] (gate < 0: h += a * 1.0), then normed = layer_norm(h). */
+void orc_residual_norm(float *h, const float *a, size_t rows, size_t dim, const float *mods, long gate,
+                       int kind, const float *w, const float *b, size_t scale, size_t shift, float eps,
+                       float *normed) {
+    for (size_t r = 0; r < rows; r++)
+        for (size_t j = 0; j < dim; j++) {
+            const float gv = gate >= 0 ? mods[(size_t)gate * dim + j] : 1.0f;
+            h[r * dim + j] += a[r * dim + j] * gv;
+        }
+    orc_layer_norm(h, rows, dim, kind, w, b, mods, scale, shift, eps, normed);
+}
+
+/* CpuBackend::head_split, crates/lightx2v-cpu/src/lib.rs:406-459: columns
+ * [col_off, col_off + heads * head_dim) of src (row stride src_stride) ->
+ * out [heads, rows, head_dim]; with rms_w: x * (1 / sqrt(mean(x^2) + eps)) *
+ * w[j] across all heads; with cos/sin ([rows, head_dim / 2]): interleaved
+ * pairs (a, b) -> (a c - b s, a s + b c) within each head. */
+void orc_head_split(const float *src, size_t rows, size_t src_stride, size_t col_off, size_t heads,
+                    size_t head_dim, const float *rms_w, const float *cosv, const float *sinv, float eps,
+                    float *out) {
+    const size_t d = heads * head_dim;
+    float *tmp = (float *)malloc(d * sizeof(float));
+    for (size_t r = 0; r < rows; r++) {
+        const float *row = src + r * src_stride + col_off;
+        if (rms_w) {
+            float ss = 0.0f;
+            for (size_t j = 0; j < d; j++) ss += row[j] * row[j];
+            const float ms = ss / (float)d;
+            const float inv = 1.0f / sqrtf(ms + eps);
+            for (size_t j = 0; j < d; j++) tmp[j] = row[j] * inv * rms_w[j];
+        } else {
+            memcpy(tmp, row, d * sizeof(float));
+        }
+        if (cosv && sinv) {
+            for (size_t h = 0; h < heads; h++)
+                for (size_t i = 0; i < head_dim / 2; i++) {
+                    const float a = tmp[h * head_dim + 2 * i], bb = tmp[h * head_dim + 2 * i + 1];
+                    const float c = cosv[r * head_dim / 2 + i], sn = sinv[r * head_dim / 2 + i];
+                    tmp[h * head_dim + 2 * i] = a * c - bb * sn;
+                    tmp[h * head_dim + 2 * i + 1] = a * sn + bb * c;
+                }
+        }
+        for (size_t h = 0; h < heads; h++)
+            for (size_t j = 0; j < head_dim; j++) out[(h * rows + r) * head_dim + j] = tmp[h * head_dim + j];
+    }
+    free(tmp);
+}
+
 int orc_openmp_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -60,6 +60,13 @@ def lib():
                                  _f32p, _sz, ctypes.c_int]
         L.orc_gate_residual.argtypes = [_f32p, _f32p, _sz, _sz, _f32p, _sz]
         L.orc_openmp_threads.restype = ctypes.c_int
+        L.orc_attention.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _u8p, _f32p, ctypes.c_int]
+        L.orc_layer_norm.argtypes = [_f32p, _sz, _sz, ctypes.c_int, _f32p, _f32p, _f32p, _sz, _sz,
+                                     ctypes.c_float, _f32p]
+        L.orc_residual_norm.argtypes = [_f32p, _f32p, _sz, _sz, _f32p, ctypes.c_long, ctypes.c_int, _f32p,
+                                        _f32p, _sz, _sz, ctypes.c_float, _f32p]
+        L.orc_head_split.argtypes = [_f32p, _sz, _sz, _sz, _sz, _sz, _f32p, _f32p, _f32p, ctypes.c_float,
+                                     _f32p]
         _lib = L
     return _lib
 
@@ -211,3 +218,72 @@ def gate_residual(h: np.ndarray, a: np.ndarray, rows: int, dim: int, mods: np.nd
 
 def openmp_threads() -> int:
     return int(lib().orc_openmp_threads())
+
+
+# ---- attention / norms / head_split (cpu lib.rs:155-208, 328-459) -----------------------------
+def _f(a):
+    return np.ascontiguousarray(a, np.float32).reshape(-1)
+
+
+def attention(q, k, v, heads: int, sq: int, sk: int, d: int, mask=None, threads: int = 8) -> np.ndarray:
+    """attention_impl (cpu lib.rs:170-208): q [heads, sq, d], k / v [heads, sk, d], mask
+    [sq, sk] bool (True = allowed) or None -> out [sq, heads * d]."""
+    q, k, v = _f(q), _f(k), _f(v)
+    assert q.size == heads * sq * d and k.size == heads * sk * d and v.size == heads * sk * d
+    out = np.empty(sq * heads * d, np.float32)
+    mp = None
+    if mask is not None:
+        m = np.ascontiguousarray(np.asarray(mask, bool).reshape(sq, sk)).view(np.uint8)
+        mp = _p(m, _u8p)
+    lib().orc_attention(_p(q, _f32p), _p(k, _f32p), _p(v, _f32p), heads, sq, sk, d, mp, _p(out, _f32p), threads)
+    return out.reshape(sq, heads * d)
+
+
+def layer_norm(x, rows: int, dim: int, eps: float, w=None, b=None, mods=None, scale: int = 0,
+               shift: int = 0) -> np.ndarray:
+    """CpuBackend::layer_norm (cpu lib.rs:328-362): Affine when w/b are given, else Mod
+    (mods [slots, dim], rows `scale` and `shift`)."""
+    x = _f(x)
+    out = np.empty(rows * dim, np.float32)
+    kind = 0 if w is not None else 1
+    w = _f(w) if w is not None else np.zeros(1, np.float32)
+    b = _f(b) if b is not None else np.zeros(1, np.float32)
+    mods = _f(mods) if mods is not None else np.zeros(1, np.float32)
+    lib().orc_layer_norm(_p(x, _f32p), rows, dim, kind, _p(w, _f32p), _p(b, _f32p), _p(mods, _f32p), scale,
+                         shift, eps, _p(out, _f32p))
+    return out.reshape(rows, dim)
+
+
+def residual_norm(h, a, rows: int, dim: int, mods, gate, eps: float, w=None, b=None, scale: int = 0,
+                  shift: int = 0):
+    """CpuBackend::residual_norm (cpu lib.rs:364-392) -> (updated h, normed)."""
+    h = np.array(_f(h), copy=True)
+    a = _f(a)
+    mods = _f(mods)
+    out = np.empty(rows * dim, np.float32)
+    kind = 0 if w is not None else 1
+    w = _f(w) if w is not None else np.zeros(1, np.float32)
+    b = _f(b) if b is not None else np.zeros(1, np.float32)
+    lib().orc_residual_norm(_p(h, _f32p), _p(a, _f32p), rows, dim, _p(mods, _f32p), -1 if gate is None else gate,
+                            kind, _p(w, _f32p), _p(b, _f32p), scale, shift, eps, _p(out, _f32p))
+    return h.reshape(rows, dim), out.reshape(rows, dim)
+
+
+def head_split(src, rows: int, src_stride: int, col_off: int, heads: int, head_dim: int, rms_w=None,
+               rope=None, eps: float = 1e-6) -> np.ndarray:
+    """CpuBackend::head_split (cpu lib.rs:406-459) -> [heads, rows, head_dim]."""
+    src = _f(src)
+    out = np.empty(heads * rows * head_dim, np.float32)
+    wp = _p(_f(rms_w), _f32p) if rms_w is not None else None
+    keep = []
+    cp = sp = None
+    if rope is not None:
+        c, s_ = _f(rope[0]), _f(rope[1])
+        keep += [c, s_]
+        cp, sp = _p(c, _f32p), _p(s_, _f32p)
+    if rms_w is not None:
+        keep.append(_f(rms_w))
+        wp = _p(keep[-1], _f32p)
+    lib().orc_head_split(_p(src, _f32p), rows, src_stride, col_off, heads, head_dim, wp, cp, sp, eps,
+                         _p(out, _f32p))
+    return out.reshape(heads, rows, head_dim)
