@@ -1167,10 +1167,12 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     } else if (m.mode == ATT_MASK_TEMPORAL) {
         void *stage = nullptr;
         if ((s = att_host_staging(ctx, mask_bytes, &stage))) return s;
+        // [tq ranges int2 x n_qt][tk ranges int2 x n_kb][tq x sq][tk x sk]: the
+        // int2 arrays first, so that they start on 8-byte boundaries
         int32_t *host = (int32_t *)stage;
-        memcpy(host, m.tq, sq * 4);
-        memcpy(host + sq, m.tk, sk * 4);
-        int32_t *tqr = host + sq + sk, *tkr = tqr + 2 * n_qt;
+        int32_t *tqr = host, *tkr = tqr + 2 * n_qt;
+        memcpy(tkr + 2 * n_kb, m.tq, sq * 4);
+        memcpy(tkr + 2 * n_kb + sq, m.tk, sk * 4);
         for (size_t t = 0; t < n_qt; ++t) {
             int32_t lo = INT32_MAX, hi = INT32_MIN;
             for (size_t i = t * 128; i < sq && i < (t + 1) * 128; ++i) {
@@ -1191,10 +1193,10 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         }
         CUDA_TRY(ctx, cudaMemcpyAsync(mws, host, mask_bytes, cudaMemcpyHostToDevice, ctx->stream));
         CUDA_TRY(ctx, cudaEventRecord(ctx->att_host_ev, ctx->stream));
-        tq_dev = (const int *)mws;
-        tk_dev = tq_dev + sq;
-        tqr_dev = (const int2 *)(tk_dev + sk);
+        tqr_dev = (const int2 *)mws;
         tkr_dev = tqr_dev + n_qt;
+        tq_dev = (const int *)(tkr_dev + n_kb);
+        tk_dev = tq_dev + sq;
     }
     if (tc) {
         __nv_bfloat16 *vt = (__nv_bfloat16 *)ws;
