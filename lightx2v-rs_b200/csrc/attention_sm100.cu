@@ -242,33 +242,52 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
             if (!okw) { ok = false; break; }
             tc_fence_after();
             const uint32_t scol = 128u + (uint32_t)((it & 1) * 128);
+            // the row's 128 raw scores: four loads in flight, one wait
             uint32_t sv[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t t[32];
-                tmem_ld_32x32b_x32(lane_base + scol + (uint32_t)(c * 32), t);
-                tmem_wait_ld_regs(t);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
-            }
-            float mx = NEG_INF;
-            const int k0 = j * AT_BK;
-#pragma unroll
-            for (int i = 0; i < 128; ++i) {
-                float s = __uint_as_float(sv[i]) * p.scale_log2;
-                if (!full) {
-                    const int key = k0 + i;
-                    bool vis = key < p.sk;
-                    if (vis && q_ok) {
-                        if (p.mask_mode == ATT_MASK_TEMPORAL) vis = __ldg(p.tk + key) <= tq_row;
-                        else if (p.mask_mode == ATT_MASK_BITS)
-                            vis = (__ldg(p.mask_bits + (int64_t)q * p.mask_words + (key >> 5)) >> (key & 31)) & 1u;
+            tmem_ld_32x32b_x32(lane_base + scol, *reinterpret_cast<uint32_t(*)[32]>(sv));
+            tmem_ld_32x32b_x32(lane_base + scol + 32u, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+            tmem_ld_32x32b_x32(lane_base + scol + 64u, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
+            tmem_ld_32x32b_x32(lane_base + scol + 96u, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
+            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv));
+            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 64));
+            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 96));
+            if (!full) {
+                // a block some query does not see in full: visibility bits of
+                // the row's 128 keys (a small rolled loop), then -inf where hidden
+                const int k0 = j * AT_BK;
+                uint32_t vm[4];
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w = 0;
+                    const int kc = k0 + c * 32;
+                    if (p.mask_mode == ATT_MASK_BITS && q_ok && kc < p.sk) {
+                        w = __ldg(p.mask_bits + (int64_t)q * p.mask_words + (kc >> 5));
+                    } else if (p.mask_mode == ATT_MASK_TEMPORAL && q_ok) {
+#pragma unroll 1
+                        for (int b = 0; b < 32; ++b)
+                            if (kc + b < p.sk && __ldg(p.tk + kc + b) <= tq_row) w |= 1u << b;
+                    } else {
+                        w = 0xFFFFFFFFu;
                     }
-                    s = vis ? s : NEG_INF;
+                    const int valid = p.sk - kc;  // keys past sk are never visible
+                    if (valid < 32) w &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+                    vm[c] = w;
                 }
-                sv[i] = __float_as_uint(s);
-                mx = fmaxf(mx, s);
+#pragma unroll
+                for (int i = 0; i < 128; ++i)
+                    if (!((vm[i >> 5] >> (i & 31)) & 1u)) sv[i] = 0xFF800000u;  // -inf
             }
+            // row max of the raw scores (scale > 0 commutes with max)
+            float mx0 = NEG_INF, mx1 = NEG_INF, mx2 = NEG_INF, mx3 = NEG_INF;
+#pragma unroll
+            for (int i = 0; i < 128; i += 4) {
+                mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
+                mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
+                mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
+                mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
+            }
+            const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
             const float m_new = fmaxf(m_run, mx);
             const bool need = m_run != NEG_INF && m_new > m_run + AT_RESCALE_LOG2;
             if (__any_sync(0xFFFFFFFFu, need)) {
@@ -279,18 +298,15 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
                 if (!okw) { ok = false; break; }
                 tc_fence_after();
                 const float corr = need ? ex2(m_run - m_new) : 1.0f;
-#pragma unroll
+#pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     uint32_t t[32];
                     tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), t);
                     tmem_wait_ld_regs(t);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-                    uint32_t lo[16], hi[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) { lo[i] = t[i]; hi[i] = t[16 + i]; }
-                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32), lo);
-                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32 + 16), hi);
+                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[16]>(t));
+                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(t + 16));
                 }
                 tmem_wait_st();
                 if (need) {
@@ -299,16 +315,19 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
                 }
             }
             if (m_run == NEG_INF) m_run = m_new;  // nothing visible so far: O holds zeros
-            const float m_use = m_run == NEG_INF ? 0.0f : m_run;
+            const float nm = m_run == NEG_INF ? 0.0f : -m_run;
+            const float sc = p.scale_log2;
             uint32_t pk[64];
-            float lsum = 0.0f;
+            float ls0 = 0.0f, ls1 = 0.0f;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                const float a = ex2(__uint_as_float(sv[2 * i]) - m_use);
-                const float b = ex2(__uint_as_float(sv[2 * i + 1]) - m_use);
-                lsum += a + b;
+                const float a = ex2(fmaf(__uint_as_float(sv[2 * i]), sc, nm));
+                const float b = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), sc, nm));
+                ls0 += a;
+                ls1 += b;
                 pk[i] = pack_bf16x2(a, b);
             }
+            const float lsum = ls0 + ls1;
             l += lsum;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
