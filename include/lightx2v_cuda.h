@@ -190,6 +190,51 @@ LX2V_API lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_bu
                                                     size_t head_dim, const int32_t *tq, const int32_t *tk,
                                                     lx2v_buf *out);
 
+/* ---- KV cache / MemRoPE (backend.rs:334-390) ---------------------------- */
+/* The per-layer KV cache (Backend::KvCache; CPU reference
+ * crates/lightx2v-cpu/src/lib.rs:607-806). K and V rows live on the device
+ * as [heads][capacity][head_dim] bf16; each row carries a temporal index and
+ * a slot kind (sink, long EMA, short EMA, recent, new) kept on the host. */
+typedef struct lx2v_kv_cache lx2v_kv_cache;
+/* Backend::kv_cache_new: an empty cache with room for capacity_tokens rows
+ * (it grows when a MemRoPE update needs more). */
+LX2V_API lx2v_status lx2v_kv_cache_new(lx2v_ctx *ctx, size_t heads, size_t head_dim, size_t capacity_tokens,
+                                       lx2v_kv_cache **out);
+LX2V_API void lx2v_kv_cache_free(lx2v_ctx *ctx, lx2v_kv_cache *cache);
+/* Backend::kv_cache_append: k and v are [heads, rows, head_dim] buffers,
+ * temporal host [rows]; the rows are appended as New slots. */
+LX2V_API lx2v_status lx2v_kv_cache_append(lx2v_ctx *ctx, lx2v_kv_cache *cache, const lx2v_buf *k,
+                                          const lx2v_buf *v, size_t rows, const size_t *temporal);
+/* Backend::kv_cache_put: overwrite the rows already cached under the same
+ * temporal indices (the same chunk on the next denoising step), else
+ * append. */
+LX2V_API lx2v_status lx2v_kv_cache_put(lx2v_ctx *ctx, lx2v_kv_cache *cache, const lx2v_buf *k, const lx2v_buf *v,
+                                       size_t rows, const size_t *temporal);
+/* Backend::kv_cache_len. */
+LX2V_API lx2v_status lx2v_kv_cache_len(lx2v_ctx *ctx, const lx2v_kv_cache *cache, size_t *rows);
+/* Backend::kv_cache_temporal: the rows' temporal indices in cache order into
+ * out[0..rows) (cap >= rows). */
+LX2V_API lx2v_status lx2v_kv_cache_temporal(lx2v_ctx *ctx, const lx2v_kv_cache *cache, size_t *out, size_t cap);
+/* Backend::kv_cache_kv: the cached K and V as [heads, rows, head_dim] into
+ * k_out / v_out (bf16 or f32 buffers of at least heads * rows * head_dim). */
+LX2V_API lx2v_status lx2v_kv_cache_kv(lx2v_ctx *ctx, const lx2v_kv_cache *cache, lx2v_buf *k_out,
+                                      lx2v_buf *v_out);
+/* Backend::kv_cache_memrope_update with the MemRopeConfig fields it reads
+ * (crates/lightx2v-core/src/config.rs:265-300; new_frames is
+ * MemRopeConfig::new_frames()): seed the EMA slots, graduate New frames to
+ * Recent, and while more than cache_frames frames are cached fold the
+ * oldest Recent (else New) frame into the EMA slots and evict it. */
+LX2V_API lx2v_status lx2v_kv_cache_memrope_update(lx2v_ctx *ctx, lx2v_kv_cache *cache, size_t cache_frames,
+                                                  size_t sink_frames, size_t new_frames, float ema_alpha_long,
+                                                  float ema_alpha_short, size_t frame_tokens);
+/* No counterpart in the reference (there: kv_cache_kv, then causal_attention
+ * with the boolean mask, crates/lightx2v-model/src/dit.rs:643-667): the
+ * causal attention of q ([heads, sq, head_dim]) against the cache, reading
+ * K and V in place, key visible to query i when its temporal index <= tq[i]
+ * (host int32 [sq]). out is [sq, heads * head_dim]. */
+LX2V_API lx2v_status lx2v_kv_cache_attention(lx2v_ctx *ctx, const lx2v_buf *q, size_t sq, const int32_t *tq,
+                                             const lx2v_kv_cache *cache, lx2v_buf *out);
+
 /* ---- profiling (backend.rs:192-196) -------------------------------------- */
 /* Backend::profile_report: per-op device time since the last reset, as JSON
  * {"op": {"calls": n, "ms": t}, ...}. Profiling is on when the context was

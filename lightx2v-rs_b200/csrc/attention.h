@@ -27,6 +27,7 @@ struct alignas(64) AttnParams {
     const int *tk;        // [sk] temporal index of each key
     const int2 *tk_range; // [ceil(sk / 128)] (min, max) tk of each key block
     const int2 *tq_range; // [ceil(sq / 128)] (min, max) tq of each query tile
+    const int *tile_order;  // [ceil(sq / 128)] query tiles, most key blocks first (or null: in order)
     int *err;
     uint64_t wait_limit_ns;
 };

@@ -102,8 +102,11 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_qt = (p.sq + AT_BQ - 1) / AT_BQ;
-    const int h = (int)blockIdx.x / n_qt, qt = (int)blockIdx.x % n_qt;
+    // CTAs take the query tiles with the most visible key blocks first (all
+    // heads of a tile together), so that the light tiles fill the last wave
+    const int h = (int)blockIdx.x % p.heads;
+    const int rank_t = (int)blockIdx.x / p.heads;
+    const int qt = p.tile_order ? p.tile_order[rank_t] : rank_t;
     const int nblk = (p.sk + AT_BK - 1) / AT_BK;
     const int2 tqr = p.mask_mode == ATT_MASK_TEMPORAL ? p.tq_range[qt] : make_int2(0, 0);
     int *err = p.err;

@@ -26,6 +26,7 @@
 #include "dequant.cuh"
 #include "gemm.h"
 #include "attention.h"
+#include "kvcache.h"
 
 using namespace lx2v;
 
@@ -64,6 +65,8 @@ struct lx2v_ctx {
     size_t gemv_tiles = 0;
     void *att_ws = nullptr;      // attention: V^T copy, mask bits / temporal indices
     size_t att_ws_bytes = 0;
+    void *kv_tmp = nullptr;      // KV cache: staging of row moves (splice / evict)
+    size_t kv_tmp_bytes = 0;
     void *att_host = nullptr;    // page-locked staging of the mask data (reused once its copy is done)
     size_t att_host_bytes = 0;
     cudaEvent_t att_host_ev = nullptr;
@@ -358,6 +361,7 @@ extern "C" void lx2v_free_ctx(lx2v_ctx *ctx) {
     if (ctx->gemv_ws) cudaFree(ctx->gemv_ws);
     if (ctx->att_ws) cudaFree(ctx->att_ws);
     if (ctx->att_host) cudaFreeHost(ctx->att_host);
+    if (ctx->kv_tmp) cudaFree(ctx->kv_tmp);
     if (ctx->att_host_ev) cudaEventDestroy(ctx->att_host_ev);
     for (void *b : ctx->dq_ws)
         if (b) cudaFree(b);
@@ -1145,7 +1149,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     const size_t words = (sk + 31) / 32;
     size_t mask_bytes = 0;
     if (m.mode == ATT_MASK_BITS) mask_bytes = sq * words * 4;
-    else if (m.mode == ATT_MASK_TEMPORAL) mask_bytes = (sq + sk) * 4 + (n_qt + n_kb) * 8;
+    else if (m.mode == ATT_MASK_TEMPORAL) mask_bytes = (sq + sk) * 4 + (n_qt + n_kb) * 8 + n_qt * 4;
     lx2v_status s = ensure_att_workspace(ctx, vt_bytes + align_up(mask_bytes, 256) + 256);
     if (s) return s;
     char *ws = (char *)ctx->att_ws;
@@ -1153,6 +1157,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     const uint32_t *bits_dev = nullptr;
     const int *tq_dev = nullptr, *tk_dev = nullptr;
     const int2 *tqr_dev = nullptr, *tkr_dev = nullptr;
+    const int *order_dev = nullptr;
     if (m.mode == ATT_MASK_BITS) {
         void *stage = nullptr;
         if ((s = att_host_staging(ctx, mask_bytes, &stage))) return s;
@@ -1173,6 +1178,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         int32_t *tqr = host, *tkr = tqr + 2 * n_qt;
         memcpy(tkr + 2 * n_kb, m.tq, sq * 4);
         memcpy(tkr + 2 * n_kb + sq, m.tk, sk * 4);
+        int32_t *order = tkr + 2 * n_kb + sq + sk;
         for (size_t t = 0; t < n_qt; ++t) {
             int32_t lo = INT32_MAX, hi = INT32_MIN;
             for (size_t i = t * 128; i < sq && i < (t + 1) * 128; ++i) {
@@ -1191,12 +1197,22 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
             tkr[2 * b] = lo;
             tkr[2 * b + 1] = hi;
         }
+        // query tiles by the number of key blocks they attend to, most first
+        std::vector<std::pair<int, int>> work(n_qt);
+        for (size_t t = 0; t < n_qt; ++t) {
+            int live = 0;
+            for (size_t b = 0; b < n_kb; ++b) live += tkr[2 * b] <= tqr[2 * t + 1];
+            work[t] = {-live, (int)t};
+        }
+        std::stable_sort(work.begin(), work.end());
+        for (size_t t = 0; t < n_qt; ++t) order[t] = work[t].second;
         CUDA_TRY(ctx, cudaMemcpyAsync(mws, host, mask_bytes, cudaMemcpyHostToDevice, ctx->stream));
         CUDA_TRY(ctx, cudaEventRecord(ctx->att_host_ev, ctx->stream));
         tqr_dev = (const int2 *)mws;
         tkr_dev = tqr_dev + n_qt;
         tq_dev = (const int *)(tkr_dev + n_kb);
         tk_dev = tq_dev + sq;
+        order_dev = tk_dev + sk;
     }
     if (tc) {
         __nv_bfloat16 *vt = (__nv_bfloat16 *)ws;
@@ -1221,6 +1237,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         p.mask_mode = m.mode;
         p.mask_bits = bits_dev; p.mask_words = (int)words;
         p.tq = tq_dev; p.tk = tk_dev; p.tq_range = tqr_dev; p.tk_range = tkr_dev;
+        p.tile_order = order_dev;
         p.err = ctx->err_dev;
         p.wait_limit_ns = ctx->wait_limit_ns;
         CUDA_TRY(ctx, attention_tc_launch(p, ctx->stream));
@@ -1295,6 +1312,306 @@ extern "C" lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_
     m.tq = tq;
     m.tk = tk;
     return attention_buffers(ctx, "causal_attention", q, k, v, heads, sq, sk, head_dim, m, out);
+}
+
+// ---- KV cache / MemRoPE (backend.rs:334-390) ------------------------------------------------
+// The CPU reference (crates/lightx2v-cpu/src/lib.rs:607-806) keeps K and V as
+// [rows][heads][head_dim] f32 vectors and splices them. Here the rows live on
+// the device as [heads][capacity][head_dim] bf16 (the CUDA backend's
+// activation precision), so each head's keys are one matrix the attention
+// kernel reads directly; the slot bookkeeping (temporal index and kind per
+// row) stays on the host and follows the reference step for step.
+enum : uint8_t { SLOT_SINK = 0, SLOT_LONG_EMA = 1, SLOT_SHORT_EMA = 2, SLOT_RECENT = 3, SLOT_NEW = 4 };
+
+struct lx2v_kv_cache {
+    size_t heads = 0, head_dim = 0;
+    size_t cap = 0;   // rows per head the device arrays hold
+    size_t rows = 0;  // rows in use
+    __nv_bfloat16 *k = nullptr, *v = nullptr;
+    std::vector<size_t> temporal;
+    std::vector<uint8_t> kinds;
+};
+
+static lx2v_status kv_reserve(lx2v_ctx *ctx, lx2v_kv_cache *c, size_t need) {
+    if (need <= c->cap) return LX2V_OK;
+    size_t cap = c->cap + c->cap / 2;
+    if (cap < need) cap = need;
+    cap = align_up(cap, 128);
+    const size_t bytes = c->heads * cap * c->head_dim * 2;
+    __nv_bfloat16 *nk = nullptr, *nv = nullptr;
+    cudaError_t e = cudaMalloc(&nk, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&nv, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(nk, 0, bytes, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(nv, 0, bytes, ctx->stream);
+    if (e == cudaSuccess && c->rows) {
+        e = kv_copy_rows_launch(c->k, 0, (int64_t)c->cap, 0, nk, 0, (int64_t)cap, 0, (int64_t)c->rows,
+                                (int)c->head_dim, (int)c->heads, ctx->stream);
+        if (e == cudaSuccess)
+            e = kv_copy_rows_launch(c->v, 0, (int64_t)c->cap, 0, nv, 0, (int64_t)cap, 0, (int64_t)c->rows,
+                                    (int)c->head_dim, (int)c->heads, ctx->stream);
+        ctx->launches += 2;
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        if (nk) cudaFree(nk);
+        if (nv) cudaFree(nv);
+        return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA, "KV cache growth: %s",
+                    cudaGetErrorString(e));
+    }
+    if (c->k) cudaFree(c->k);
+    if (c->v) cudaFree(c->v);
+    c->k = nk;
+    c->v = nv;
+    c->cap = cap;
+    return LX2V_OK;
+}
+
+// rows [src, src + n) -> [dst, dst + n) of K and V, overlapping ranges
+// allowed (through a staging buffer).
+static lx2v_status kv_move(lx2v_ctx *ctx, lx2v_kv_cache *c, size_t src, size_t dst, size_t n) {
+    if (n == 0 || src == dst) return LX2V_OK;
+    const size_t bytes = c->heads * n * c->head_dim * 2;
+    if (ctx->kv_tmp_bytes < bytes) {
+        if (ctx->kv_tmp) {
+            CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+            cudaFree(ctx->kv_tmp);
+            ctx->kv_tmp = nullptr;
+            ctx->kv_tmp_bytes = 0;
+        }
+        CUDA_TRY(ctx, cudaMalloc(&ctx->kv_tmp, bytes));
+        ctx->kv_tmp_bytes = bytes;
+    }
+    for (__nv_bfloat16 *a : {c->k, c->v}) {
+        CUDA_TRY(ctx, kv_copy_rows_launch(a, 0, (int64_t)c->cap, (int64_t)src, ctx->kv_tmp, 0, (int64_t)n, 0,
+                                          (int64_t)n, (int)c->head_dim, (int)c->heads, ctx->stream));
+        CUDA_TRY(ctx, kv_copy_rows_launch(ctx->kv_tmp, 0, (int64_t)n, 0, a, 0, (int64_t)c->cap, (int64_t)dst,
+                                          (int64_t)n, (int)c->head_dim, (int)c->heads, ctx->stream));
+        ctx->launches += 2;
+    }
+    return LX2V_OK;
+}
+
+static lx2v_status kv_write_rows(lx2v_ctx *ctx, lx2v_kv_cache *c, const lx2v_buf *k, const lx2v_buf *v,
+                                 size_t rows, size_t at) {
+    CUDA_TRY(ctx, kv_copy_rows_launch(k->ptr, k->dtype == LX2V_F32, (int64_t)rows, 0, c->k, 0, (int64_t)c->cap,
+                                      (int64_t)at, (int64_t)rows, (int)c->head_dim, (int)c->heads, ctx->stream));
+    CUDA_TRY(ctx, kv_copy_rows_launch(v->ptr, v->dtype == LX2V_F32, (int64_t)rows, 0, c->v, 0, (int64_t)c->cap,
+                                      (int64_t)at, (int64_t)rows, (int)c->head_dim, (int)c->heads, ctx->stream));
+    ctx->launches += 2;
+    CUDA_TRY(ctx, note_uses(ctx, {k, v}));
+    return LX2V_OK;
+}
+
+static lx2v_status kv_check_rows(lx2v_ctx *ctx, lx2v_kv_cache *c, const lx2v_buf *k, const lx2v_buf *v, size_t rows,
+                                 const size_t *temporal) {
+    if (!c || !k || !v || (rows && !temporal)) return fail(ctx, LX2V_ERR_INVALID, "null cache, k, v or temporal");
+    if (c->heads * rows * c->head_dim > k->len || c->heads * rows * c->head_dim > v->len)
+        return fail(ctx, LX2V_ERR_INVALID, "k/v hold fewer than heads x rows x head_dim elements");
+    return LX2V_OK;
+}
+
+static lx2v_status kv_append(lx2v_ctx *ctx, lx2v_kv_cache *c, const lx2v_buf *k, const lx2v_buf *v, size_t rows,
+                             const size_t *temporal) {
+    lx2v_status s = kv_reserve(ctx, c, c->rows + rows);
+    if (s) return s;
+    if ((s = kv_write_rows(ctx, c, k, v, rows, c->rows))) return s;
+    for (size_t r = 0; r < rows; ++r) {
+        c->temporal.push_back(temporal[r]);
+        c->kinds.push_back(SLOT_NEW);  // graduated by memrope_update
+    }
+    c->rows += rows;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_kv_cache_new(lx2v_ctx *ctx, size_t heads, size_t head_dim, size_t capacity_tokens,
+                                         lx2v_kv_cache **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || heads == 0 || head_dim == 0) return fail(ctx, LX2V_ERR_INVALID, "bad KV cache shape");
+    auto *c = new lx2v_kv_cache();
+    c->heads = heads;
+    c->head_dim = head_dim;
+    if ((s = kv_reserve(ctx, c, capacity_tokens ? capacity_tokens : 128))) {
+        delete c;
+        return s;
+    }
+    *out = c;
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_kv_cache_free(lx2v_ctx *ctx, lx2v_kv_cache *c) {
+    if (!c) return;
+    if (ctx) {
+        cudaSetDevice(ctx->dev);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    if (c->k) cudaFree(c->k);
+    if (c->v) cudaFree(c->v);
+    delete c;
+}
+
+extern "C" lx2v_status lx2v_kv_cache_append(lx2v_ctx *ctx, lx2v_kv_cache *c, const lx2v_buf *k, const lx2v_buf *v,
+                                            size_t rows, const size_t *temporal) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if ((s = kv_check_rows(ctx, c, k, v, rows, temporal))) return s;
+    OpScope ps(ctx, "kv_cache_append");
+    return kv_append(ctx, c, k, v, rows, temporal);
+}
+
+extern "C" lx2v_status lx2v_kv_cache_put(lx2v_ctx *ctx, lx2v_kv_cache *c, const lx2v_buf *k, const lx2v_buf *v,
+                                         size_t rows, const size_t *temporal) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if ((s = kv_check_rows(ctx, c, k, v, rows, temporal))) return s;
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "kv_cache_put");
+    // the same temporal run already cached (not in an EMA slot, which shares
+    // the first non-sink frame's index): overwrite those rows in place
+    for (size_t pos = 0; pos < c->rows; ++pos) {
+        if (c->temporal[pos] != temporal[0] || c->kinds[pos] == SLOT_LONG_EMA || c->kinds[pos] == SLOT_SHORT_EMA)
+            continue;
+        bool match = pos + rows <= c->rows;
+        for (size_t i = 0; match && i < rows; ++i) match = c->temporal[pos + i] == temporal[i];
+        if (match) return kv_write_rows(ctx, c, k, v, rows, pos);
+        break;  // the first candidate decides, as the reference's position() does
+    }
+    return kv_append(ctx, c, k, v, rows, temporal);
+}
+
+extern "C" lx2v_status lx2v_kv_cache_len(lx2v_ctx *ctx, const lx2v_kv_cache *c, size_t *rows) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!c || !rows) return fail(ctx, LX2V_ERR_INVALID, "null cache or output");
+    *rows = c->rows;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_kv_cache_temporal(lx2v_ctx *ctx, const lx2v_kv_cache *c, size_t *out, size_t cap) {
+    if (!ctx) return fail(nullptr, LX2V_ERR_INVALID, "null context");
+    if (!c || (c->rows && !out)) return fail(ctx, LX2V_ERR_INVALID, "null cache or output");
+    if (cap < c->rows) return fail(ctx, LX2V_ERR_INVALID, "output holds %zu of %zu rows", cap, c->rows);
+    if (c->rows) memcpy(out, c->temporal.data(), c->rows * sizeof(size_t));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_kv_cache_kv(lx2v_ctx *ctx, const lx2v_kv_cache *c, lx2v_buf *k_out, lx2v_buf *v_out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!c || !k_out || !v_out) return fail(ctx, LX2V_ERR_INVALID, "null cache or output");
+    const size_t n = c->heads * c->rows * c->head_dim;
+    if (k_out->len < n || v_out->len < n) return fail(ctx, LX2V_ERR_INVALID, "outputs hold fewer than %zu elements", n);
+    OpScope ps(ctx, "kv_cache_kv");
+    CUDA_TRY(ctx, kv_copy_rows_launch(c->k, 0, (int64_t)c->cap, 0, k_out->ptr, k_out->dtype == LX2V_F32,
+                                      (int64_t)c->rows, 0, (int64_t)c->rows, (int)c->head_dim, (int)c->heads,
+                                      ctx->stream));
+    CUDA_TRY(ctx, kv_copy_rows_launch(c->v, 0, (int64_t)c->cap, 0, v_out->ptr, v_out->dtype == LX2V_F32,
+                                      (int64_t)c->rows, 0, (int64_t)c->rows, (int)c->head_dim, (int)c->heads,
+                                      ctx->stream));
+    ctx->launches += 2;
+    CUDA_TRY(ctx, note_uses(ctx, {k_out, v_out}));
+    return LX2V_OK;
+}
+
+// crates/lightx2v-cpu/src/lib.rs:688-806, step for step.
+extern "C" lx2v_status lx2v_kv_cache_memrope_update(lx2v_ctx *ctx, lx2v_kv_cache *c, size_t cache_frames,
+                                                    size_t sink_frames, size_t new_frames, float ema_alpha_long,
+                                                    float ema_alpha_short, size_t frame_tokens) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!c || frame_tokens == 0) return fail(ctx, LX2V_ERR_INVALID, "null cache or zero frame_tokens");
+    OpScope ps(ctx, "kv_cache_memrope_update");
+    const size_t ft = frame_tokens;
+    auto n_frames = [&] { return c->rows / ft; };
+    auto frame_kinds = [&] {
+        std::vector<uint8_t> fk(n_frames());
+        for (size_t f = 0; f < fk.size(); ++f) fk[f] = c->kinds[f * ft];
+        return fk;
+    };
+    if (n_frames() == 0) return LX2V_OK;
+    std::vector<uint8_t> fk = frame_kinds();
+    const bool has_long = std::find(fk.begin(), fk.end(), SLOT_LONG_EMA) != fk.end();
+    if (!has_long && fk.size() > sink_frames) {
+        // seed the EMA slots with zero frames after the sinks: Short, then Long
+        // inserted at the same row, so the order becomes [sink, long, short]
+        const size_t at = sink_frames * ft;
+        const size_t t = c->temporal[std::min(at, c->rows - 1)];
+        for (uint8_t kind : {SLOT_SHORT_EMA, SLOT_LONG_EMA}) {
+            if ((s = kv_reserve(ctx, c, c->rows + ft))) return s;
+            if (at < c->rows && (s = kv_move(ctx, c, at, at + ft, c->rows - at))) return s;
+            for (__nv_bfloat16 *a : {c->k, c->v})
+                CUDA_TRY(ctx, cudaMemset2DAsync(a + at * c->head_dim, c->cap * c->head_dim * 2, 0,
+                                                ft * c->head_dim * 2, c->heads, ctx->stream));
+            c->temporal.insert(c->temporal.begin() + at, ft, t);
+            c->kinds.insert(c->kinds.begin() + at, ft, kind);
+            c->rows += ft;
+            fk = frame_kinds();
+        }
+    }
+    // graduate New frames beyond the newest `new_frames` to Recent
+    std::vector<size_t> news;
+    for (size_t f = 0; f < fk.size(); ++f)
+        if (fk[f] == SLOT_NEW) news.push_back(f);
+    if (news.size() > new_frames) {
+        const size_t excess = news.size() - new_frames;
+        for (size_t i = 0; i < excess; ++i)
+            std::fill(c->kinds.begin() + news[i] * ft, c->kinds.begin() + (news[i] + 1) * ft, SLOT_RECENT);
+    }
+    // evict while over capacity: fold the oldest Recent (else New) frame into
+    // the EMA slots, then drop it
+    while (n_frames() > cache_frames) {
+        const std::vector<uint8_t> kn = frame_kinds();
+        auto first = [&](uint8_t kind) -> long {
+            for (size_t f = 0; f < kn.size(); ++f)
+                if (kn[f] == kind) return (long)f;
+            return -1;
+        };
+        long f = first(SLOT_RECENT);
+        if (f < 0) f = first(SLOT_NEW);
+        if (f < 0) break;
+        const std::pair<uint8_t, float> slots[2] = {{SLOT_LONG_EMA, ema_alpha_long}, {SLOT_SHORT_EMA, ema_alpha_short}};
+        for (const auto &sl : slots) {
+            const long sf = first(sl.first);
+            if (sf < 0) continue;
+            for (__nv_bfloat16 *a : {c->k, c->v})
+                CUDA_TRY(ctx, kv_ema_launch(a, (int64_t)c->cap, (int64_t)sf * (int64_t)ft, (int64_t)f * (int64_t)ft,
+                                            (int64_t)ft, (int)c->head_dim, (int)c->heads, sl.second, ctx->stream));
+            ctx->launches += 2;
+        }
+        const size_t base = (size_t)f * ft;
+        if ((s = kv_move(ctx, c, base + ft, base, c->rows - base - ft))) return s;
+        c->temporal.erase(c->temporal.begin() + base, c->temporal.begin() + base + ft);
+        c->kinds.erase(c->kinds.begin() + base, c->kinds.begin() + base + ft);
+        c->rows -= ft;
+    }
+    // the first sink_frames frames are sinks (they were appended as New)
+    for (size_t f = 0; f < std::min(sink_frames, n_frames()); ++f)
+        std::fill(c->kinds.begin() + f * ft, c->kinds.begin() + (f + 1) * ft, SLOT_SINK);
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_kv_cache_attention(lx2v_ctx *ctx, const lx2v_buf *q, size_t sq, const int32_t *tq,
+                                               const lx2v_kv_cache *c, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!q || !c || !out || (sq && !tq)) return fail(ctx, LX2V_ERR_INVALID, "null q, cache, output or tq");
+    const size_t heads = c->heads, d = c->head_dim;
+    if (heads * sq * d > q->len) return fail(ctx, LX2V_ERR_INVALID, "q holds fewer than heads x sq x head_dim");
+    if (sq * heads * d > out->len) return fail(ctx, LX2V_ERR_INVALID, "output holds fewer than sq x heads x head_dim");
+    if (out == q) return fail(ctx, LX2V_ERR_INVALID, "output aliases q");
+    std::vector<int32_t> tk(c->rows);
+    for (size_t i = 0; i < c->rows; ++i) {
+        if (c->temporal[i] > (size_t)INT32_MAX) return fail(ctx, LX2V_ERR_UNSUPPORTED, "temporal index beyond int32");
+        tk[i] = (int32_t)c->temporal[i];
+    }
+    AttnMaskArgs m;
+    m.mode = ATT_MASK_TEMPORAL;
+    m.tq = tq;
+    m.tk = tk.data();
+    s = attention_queue(ctx, "kv_cache_attention", q->ptr, q->dtype == LX2V_F32, sq, c->k, c->v, 0, c->cap, heads,
+                        sq, c->rows, d, m, out);
+    if (s) return s;
+    CUDA_TRY(ctx, note_uses(ctx, {q, out}));
+    return LX2V_OK;
 }
 
 // ---- profiling / knobs ---------------------------------------------------------------------

@@ -67,6 +67,15 @@ SIGNATURES = {
     "lx2v_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]),
     "lx2v_causal_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     "lx2v_causal_attention_temporal": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
+    "lx2v_kv_cache_new": (_st, [_vp, _sz, _sz, _sz, _pp]),
+    "lx2v_kv_cache_free": (None, [_vp, _vp]),
+    "lx2v_kv_cache_append": (_st, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "lx2v_kv_cache_put": (_st, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "lx2v_kv_cache_len": (_st, [_vp, _vp, ctypes.POINTER(_sz)]),
+    "lx2v_kv_cache_temporal": (_st, [_vp, _vp, _vp, _sz]),
+    "lx2v_kv_cache_kv": (_st, [_vp, _vp, _vp, _vp]),
+    "lx2v_kv_cache_memrope_update": (_st, [_vp, _vp, _sz, _sz, _sz, ctypes.c_float, ctypes.c_float, _sz]),
+    "lx2v_kv_cache_attention": (_st, [_vp, _vp, _sz, _vp, _vp, _vp]),
     "lx2v_profile_json": (_st, [_vp, ctypes.c_char_p, _sz, ctypes.POINTER(_sz)]),
     "lx2v_profile_reset": (_st, [_vp]),
     "lx2v_set_linear_path": (_st, [_vp, ctypes.c_int]),

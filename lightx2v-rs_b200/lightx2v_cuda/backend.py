@@ -73,6 +73,18 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
 
 
+class KvCache:
+    """A device KV cache handle (Backend::KvCache); freed with the object."""
+
+    def __init__(self, be: "CudaBackend", handle: int, heads: int, head_dim: int):
+        self.be, self.handle, self.heads, self.head_dim = be, handle, heads, head_dim
+
+    def __del__(self):
+        if getattr(self, "handle", None) and getattr(self.be, "_ctx", None):
+            self.be._lib.lx2v_kv_cache_free(self.be._ctx, self.handle)
+            self.handle = None
+
+
 class CudaBackend:
     """The CUDA backend for one device. Buffers default to bf16, the CUDA
     backend's activation precision (backend.rs:9-11)."""
@@ -288,6 +300,54 @@ class CudaBackend:
         self._check(self._lib.lx2v_causal_attention_temporal(self._ctx, q.handle, k.handle, v.handle, heads,
                                                              sq, sk, head_dim, tq.ctypes.data,
                                                              tk.ctypes.data, out.handle))
+
+    # ---- KV cache / MemRoPE, backend.rs:334-390 ------------------------------------
+    def kv_cache_new(self, heads: int, head_dim: int, capacity_tokens: int) -> "KvCache":
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_kv_cache_new(self._ctx, heads, head_dim, capacity_tokens, ctypes.byref(h)))
+        return KvCache(self, h.value, heads, head_dim)
+
+    def kv_cache_append(self, cache: "KvCache", k: Buf, v: Buf, rows: int, temporal):
+        t = np.ascontiguousarray(temporal, np.uint64)
+        assert t.size == rows
+        self._check(self._lib.lx2v_kv_cache_append(self._ctx, cache.handle, k.handle, v.handle, rows,
+                                                   t.ctypes.data))
+
+    def kv_cache_put(self, cache: "KvCache", k: Buf, v: Buf, rows: int, temporal):
+        t = np.ascontiguousarray(temporal, np.uint64)
+        assert t.size == rows
+        self._check(self._lib.lx2v_kv_cache_put(self._ctx, cache.handle, k.handle, v.handle, rows, t.ctypes.data))
+
+    def kv_cache_len(self, cache: "KvCache") -> int:
+        n = ctypes.c_size_t()
+        self._check(self._lib.lx2v_kv_cache_len(self._ctx, cache.handle, ctypes.byref(n)))
+        return n.value
+
+    def kv_cache_temporal(self, cache: "KvCache") -> np.ndarray:
+        n = self.kv_cache_len(cache)
+        out = np.zeros(max(n, 1), np.uint64)
+        self._check(self._lib.lx2v_kv_cache_temporal(self._ctx, cache.handle, out.ctypes.data, out.size))
+        return out[:n].astype(np.int64)
+
+    def kv_cache_kv(self, cache: "KvCache", dtype: int = L.BF16):
+        n = cache.heads * self.kv_cache_len(cache) * cache.head_dim
+        k, v = self.alloc(n, dtype), self.alloc(n, dtype)
+        self._check(self._lib.lx2v_kv_cache_kv(self._ctx, cache.handle, k.handle, v.handle))
+        return k, v
+
+    def kv_cache_memrope_update(self, cache: "KvCache", cfg, frame_tokens: int):
+        """cfg: any object with cache_frames, sink_frames, ema_alpha_long, ema_alpha_short
+        (MemRopeConfig, config.rs:265-300); new_frames() is 3 unless cfg says otherwise."""
+        new_frames = cfg.new_frames() if hasattr(cfg, "new_frames") else 3
+        self._check(self._lib.lx2v_kv_cache_memrope_update(self._ctx, cache.handle, cfg.cache_frames,
+                                                           cfg.sink_frames, new_frames, cfg.ema_alpha_long,
+                                                           cfg.ema_alpha_short, frame_tokens))
+
+    def kv_cache_attention(self, q: Buf, sq: int, tq, cache: "KvCache", out: Buf):
+        tq = np.ascontiguousarray(tq, np.int32)
+        assert tq.size == sq
+        self._check(self._lib.lx2v_kv_cache_attention(self._ctx, q.handle, sq, tq.ctypes.data, cache.handle,
+                                                      out.handle))
 
     def gate_residual(self, h: Buf, a: Buf, rows: int, dim: int, mods: Buf, gate: int):
         """In place on h: h += a * mods[gate] (backend.rs:244-253)."""

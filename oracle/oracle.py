@@ -287,3 +287,101 @@ def head_split(src, rows: int, src_stride: int, col_off: int, heads: int, head_d
     lib().orc_head_split(_p(src, _f32p), rows, src_stride, col_off, heads, head_dim, wp, cp, sp, eps,
                          _p(out, _f32p))
     return out.reshape(heads, rows, head_dim)
+
+
+# ---- KV cache / MemRoPE (cpu lib.rs:607-806; memrope.rs ema_update) ----------------------------
+SINK, LONG_EMA, SHORT_EMA, RECENT, NEW = range(5)
+
+
+class KvCacheRef:
+    """CpuBackend's KvCache restated in numpy: k / v rows [rows, heads * head_dim]
+    f32 (a token row holds all its heads, as the reference's flat Vec does),
+    one temporal index and slot kind per row."""
+
+    def __init__(self, heads: int, head_dim: int):
+        self.heads, self.head_dim = heads, head_dim
+        self.k = np.zeros((0, heads * head_dim), np.float32)
+        self.v = np.zeros((0, heads * head_dim), np.float32)
+        self.temporal: list[int] = []
+        self.kinds: list[int] = []
+
+    def rows(self) -> int:
+        return len(self.temporal)
+
+    @staticmethod
+    def _rows_of(x, heads, rows, hd):
+        # [heads, rows, head_dim] -> [rows, heads * head_dim]
+        return np.asarray(x, np.float32).reshape(heads, rows, hd).transpose(1, 0, 2).reshape(rows, heads * hd)
+
+    def append(self, k, v, rows: int, temporal):
+        """kv_cache_append, lib.rs:620-648."""
+        self.k = np.concatenate([self.k, self._rows_of(k, self.heads, rows, self.head_dim)])
+        self.v = np.concatenate([self.v, self._rows_of(v, self.heads, rows, self.head_dim)])
+        self.temporal += [int(t) for t in temporal]
+        self.kinds += [NEW] * rows
+
+    def put(self, k, v, rows: int, temporal):
+        """kv_cache_put, lib.rs:650-678."""
+        temporal = [int(t) for t in temporal]
+        pos = next((i for i, (t, kd) in enumerate(zip(self.temporal, self.kinds))
+                    if t == temporal[0] and kd not in (LONG_EMA, SHORT_EMA)), None)
+        if pos is not None and all(pos + i < self.rows() and self.temporal[pos + i] == temporal[i]
+                                   for i in range(rows)):
+            self.k[pos:pos + rows] = self._rows_of(k, self.heads, rows, self.head_dim)
+            self.v[pos:pos + rows] = self._rows_of(v, self.heads, rows, self.head_dim)
+            return
+        self.append(k, v, rows, temporal)
+
+    def kv(self):
+        """kv_cache_kv, lib.rs:690-706: [heads, rows, head_dim] each."""
+        r = self.rows()
+        f = lambda a: a.reshape(r, self.heads, self.head_dim).transpose(1, 0, 2).copy()
+        return f(self.k), f(self.v)
+
+    def memrope_update(self, cache_frames: int, sink_frames: int, new_frames: int, alpha_long: float,
+                       alpha_short: float, ft: int):
+        """kv_cache_memrope_update, lib.rs:708-806."""
+        def n_frames():
+            return self.rows() // ft
+
+        def frame_kinds():
+            return [self.kinds[f * ft] for f in range(n_frames())]
+
+        if n_frames() == 0:
+            return
+        fk = frame_kinds()
+        if LONG_EMA not in fk and n_frames() > sink_frames:
+            at = sink_frames * ft
+            t = self.temporal[min(at, max(self.rows() - 1, 0))]
+            zero = np.zeros((ft, self.k.shape[1]), np.float32)
+            for kind in (SHORT_EMA, LONG_EMA):
+                self.k = np.concatenate([self.k[:at], zero, self.k[at:]])
+                self.v = np.concatenate([self.v[:at], zero, self.v[at:]])
+                self.temporal[at:at] = [t] * ft
+                self.kinds[at:at] = [kind] * ft
+                fk = frame_kinds()
+        news = [i for i, kd in enumerate(fk) if kd == NEW]
+        if len(news) > new_frames:
+            for f in news[:len(news) - new_frames]:
+                self.kinds[f * ft:(f + 1) * ft] = [RECENT] * ft
+        while n_frames() > cache_frames:
+            kn = frame_kinds()
+            f = kn.index(RECENT) if RECENT in kn else (kn.index(NEW) if NEW in kn else None)
+            if f is None:
+                break
+            ev_k = self.k[f * ft:(f + 1) * ft].copy()
+            ev_v = self.v[f * ft:(f + 1) * ft].copy()
+            for kind, alpha in ((LONG_EMA, alpha_long), (SHORT_EMA, alpha_short)):
+                if kind in kn:
+                    sf = kn.index(kind)
+                    a = np.float32(alpha)
+                    one_m = np.float32(1.0) - a
+                    for arr, ev in ((self.k, ev_k), (self.v, ev_v)):
+                        e = arr[sf * ft:(sf + 1) * ft]
+                        arr[sf * ft:(sf + 1) * ft] = (one_m * e).astype(np.float32) + (a * ev).astype(np.float32)
+            self.k = np.concatenate([self.k[:f * ft], self.k[(f + 1) * ft:]])
+            self.v = np.concatenate([self.v[:f * ft], self.v[(f + 1) * ft:]])
+            del self.temporal[f * ft:(f + 1) * ft]
+            del self.kinds[f * ft:(f + 1) * ft]
+        for f in range(min(sink_frames, n_frames())):
+            self.kinds[f * ft:(f + 1) * ft] = [SINK] * ft
