@@ -190,6 +190,41 @@ LX2V_API lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_bu
                                                     size_t head_dim, const int32_t *tq, const int32_t *tk,
                                                     lx2v_buf *out);
 
+/* ---- norms, head_split, patchify, dmd_step (backend.rs:214-273, 392-428) -- */
+/* NormKind (backend.rs:47-53): kind 0 = Affine { w, b } (out = LN(x) * w + b,
+ * w and b of dim elements), 1 = Mod { scale, shift } (out = LN(x) *
+ * (1 + mods[scale]) + mods[shift], rows of the [slots, dim] mods table). */
+enum { LX2V_NORM_AFFINE = 0, LX2V_NORM_MOD = 1 };
+/* Backend::layer_norm: rows of width dim (at most 4096). Unused arguments of
+ * the other kind may be NULL / 0. */
+LX2V_API lx2v_status lx2v_layer_norm(lx2v_ctx *ctx, const lx2v_buf *x, size_t rows, size_t dim, int kind,
+                                     const lx2v_buf *w, const lx2v_buf *b, size_t scale, size_t shift,
+                                     const lx2v_buf *mods, float eps, lx2v_buf *out);
+/* Backend::residual_norm: in place h += a * mods[gate] (gate < 0: h += a),
+ * then normed = norm(h) of the unrounded f32 sum. */
+LX2V_API lx2v_status lx2v_residual_norm(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_buf *a, size_t rows, size_t dim,
+                                        const lx2v_buf *mods, long gate, int kind, const lx2v_buf *w,
+                                        const lx2v_buf *b, size_t scale, size_t shift, float eps,
+                                        lx2v_buf *normed);
+/* Backend::head_split: columns [col_off, col_off + heads * head_dim) of src
+ * (rows of src_stride) -> out [heads, rows, head_dim], RMS-normalised across
+ * all heads times rms_w when rms_w is given, rotated by RoPE on interleaved
+ * pairs when cos and sin ([rows, head_dim / 2]) are given. */
+LX2V_API lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                     size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                     const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out);
+/* Backend::patchify: latent [c, t, h, w] -> tokens [t*(h/p)*(w/p), c*p*p],
+ * feature c*p^2 + kh*p + kw. */
+LX2V_API lx2v_status lx2v_patchify(lx2v_ctx *ctx, const lx2v_buf *latent, size_t c, size_t t, size_t h, size_t w,
+                                   size_t p, lx2v_buf *out);
+/* Backend::unpatchify: the inverse of lx2v_patchify. */
+LX2V_API lx2v_status lx2v_unpatchify(lx2v_ctx *ctx, const lx2v_buf *x, size_t c, size_t t, size_t h, size_t w,
+                                     size_t p, lx2v_buf *out);
+/* Backend::dmd_step: in place on x[0..n): x0 = x - sigma_t * v, then
+ * x = (1 - sigma_next) * x0 + sigma_next * noise when noise is given. */
+LX2V_API lx2v_status lx2v_dmd_step(lx2v_ctx *ctx, lx2v_buf *x, const lx2v_buf *v, const lx2v_buf *noise,
+                                   float sigma_t, float sigma_next, size_t n);
+
 /* ---- KV cache / MemRoPE (backend.rs:334-390) ---------------------------- */
 /* The per-layer KV cache (Backend::KvCache; CPU reference
  * crates/lightx2v-cpu/src/lib.rs:607-806). K and V rows live on the device

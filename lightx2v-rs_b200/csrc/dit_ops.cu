@@ -1,0 +1,226 @@
+// dit_ops.cu — the DiT block's row-wise and elementwise ops around the
+// linears and the attention: layer_norm / residual_norm (AdaLN or affine),
+// head_split (RMS across all heads, per-channel weight, interleaved RoPE,
+// [rows, heads*d] -> [heads, rows, d]), patchify / unpatchify and dmd_step.
+// CPU reference: crates/lightx2v-cpu/src/lib.rs:328-459 and 806-874; trait
+// crates/lightx2v-core/src/backend.rs:214-273, 392-428.
+//
+// All of them are HBM-bound: one CTA per row, the row held in registers
+// between its two passes (statistics, then the normalised output), so each
+// row is read once and written once.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "dit_ops.h"
+
+namespace lx2v {
+
+namespace {
+
+constexpr int ROW_THREADS = 128;
+constexpr int ROW_PER_THREAD = 32;  // rows up to 4096 values
+
+__device__ __forceinline__ float ld_v(const void *p, int f32, int64_t i) {
+    return f32 ? reinterpret_cast<const float *>(p)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+}
+__device__ __forceinline__ void st_v(void *p, int f32, int64_t i, float v) {
+    if (f32) reinterpret_cast<float *>(p)[i] = v;
+    else reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// Sum over the CTA (ROW_THREADS threads); every thread gets the total.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    __syncthreads();  // red is free (an earlier call has read it)
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < ROW_THREADS / 32; ++w) t += red[w];
+    return t;
+}
+
+// One row: mean and variance of vals[0..n) (thread's share), then the
+// normalised values written to out (row r). Norm kind 0 = affine (w, b),
+// 1 = modulated (1 + mods[scale]) and + mods[shift].
+__device__ __forceinline__ void norm_row(const float (&vals)[ROW_PER_THREAD], const NormArgs &a, int64_t r,
+                                         float *red) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < ROW_PER_THREAD; ++i)
+        if (threadIdx.x + i * ROW_THREADS < a.dim) s += vals[i];
+    const float mean = block_sum(s, red) / (float)a.dim;
+    float vs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < ROW_PER_THREAD; ++i)
+        if (threadIdx.x + i * ROW_THREADS < a.dim) {
+            const float c = vals[i] - mean;
+            vs += c * c;
+        }
+    const float var = block_sum(vs, red) / (float)a.dim;
+    const float inv = 1.0f / sqrtf(var + a.eps);
+#pragma unroll
+    for (int i = 0; i < ROW_PER_THREAD; ++i) {
+        const int j = threadIdx.x + i * ROW_THREADS;
+        if (j >= a.dim) break;
+        const float n = (vals[i] - mean) * inv;
+        float o;
+        if (a.kind == 0) o = n * ld_v(a.w, a.w_f32, j) + ld_v(a.b, a.b_f32, j);
+        else o = n * (1.0f + ld_v(a.mods, a.mods_f32, (int64_t)a.scale * a.dim + j)) +
+                 ld_v(a.mods, a.mods_f32, (int64_t)a.shift * a.dim + j);
+        st_v(a.out, a.out_f32, r * a.dim + j, o);
+    }
+}
+
+__global__ void __launch_bounds__(ROW_THREADS) layer_norm_kernel(NormArgs a) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int64_t r = blockIdx.x;
+    float vals[ROW_PER_THREAD];
+#pragma unroll
+    for (int i = 0; i < ROW_PER_THREAD; ++i) {
+        const int j = threadIdx.x + i * ROW_THREADS;
+        vals[i] = j < a.dim ? ld_v(a.x, a.x_f32, r * a.dim + j) : 0.0f;
+    }
+    norm_row(vals, a, r, red);
+}
+
+// h += a * mods[gate] (or + a), stored back, then the norm of the f32 sum.
+__global__ void __launch_bounds__(ROW_THREADS) residual_norm_kernel(NormArgs a, void *h, int h_f32, const void *res,
+                                                                    int res_f32, int gate) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int64_t r = blockIdx.x;
+    float vals[ROW_PER_THREAD];
+#pragma unroll
+    for (int k = 0; k < ROW_PER_THREAD; ++k) {
+        const int j = threadIdx.x + k * ROW_THREADS;
+        vals[k] = 0.0f;
+        if (j < a.dim) {
+            const int64_t i = r * a.dim + j;
+            const float g = gate >= 0 ? ld_v(a.mods, a.mods_f32, (int64_t)gate * a.dim + j) : 1.0f;
+            const float v = ld_v(h, h_f32, i) + ld_v(res, res_f32, i) * g;
+            st_v(h, h_f32, i, v);
+            vals[k] = v;
+        }
+    }
+    norm_row(vals, a, r, red);
+}
+
+// One row of src: columns [col_off, col_off + heads * hd), optional RMS over
+// all of them times w[j], optional RoPE on interleaved pairs of each head,
+// written to out[h][r][:]. Thread t takes the pairs t, t + 128, ...
+__global__ void __launch_bounds__(ROW_THREADS) head_split_kernel(HeadSplitArgs a) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int64_t r = blockIdx.x;
+    const int d = a.heads * a.head_dim;
+    const int pairs = d / 2;
+    constexpr int NP = ROW_PER_THREAD / 2;
+    float x0[NP], x1[NP];
+    const int64_t base = r * a.src_stride + a.col_off;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+        const int pi = threadIdx.x + i * ROW_THREADS;
+        x0[i] = pi < pairs ? ld_v(a.src, a.src_f32, base + 2 * pi) : 0.0f;
+        x1[i] = pi < pairs ? ld_v(a.src, a.src_f32, base + 2 * pi + 1) : 0.0f;
+    }
+    if (a.rms_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];  // zeros past the row add nothing
+        const float ms = block_sum(ss, red) / (float)d;
+        const float inv = 1.0f / sqrtf(ms + a.eps);
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+            const int j = 2 * (threadIdx.x + i * ROW_THREADS);
+            if (j >= d) break;
+            x0[i] = x0[i] * inv * ld_v(a.rms_w, a.w_f32, j);
+            x1[i] = x1[i] * inv * ld_v(a.rms_w, a.w_f32, j + 1);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+        const int j = 2 * (threadIdx.x + i * ROW_THREADS);
+        if (j >= d) break;
+        const int h = j / a.head_dim, e = j % a.head_dim;
+        float o0 = x0[i], o1 = x1[i];
+        if (a.cos) {
+            const int64_t ci = r * (a.head_dim / 2) + e / 2;
+            const float c = ld_v(a.cos, a.cs_f32, ci), sn = ld_v(a.sin, a.cs_f32, ci);
+            o0 = x0[i] * c - x1[i] * sn;
+            o1 = x0[i] * sn + x1[i] * c;
+        }
+        const int64_t oi = ((int64_t)h * a.rows + r) * a.head_dim + e;
+        st_v(a.out, a.out_f32, oi, o0);
+        st_v(a.out, a.out_f32, oi + 1, o1);
+    }
+}
+
+// latent [c, t, h, w] <-> tokens [t * (h/p) * (w/p), c * p * p]; `to_tokens`
+// picks the direction. Thread = one element of the token matrix.
+__global__ void patchify_kernel(const void *src, int src_f32, void *dst, int dst_f32, int c, int t, int h, int w, int p,
+                                int to_tokens) {
+    const int hp = h / p, wp = w / p, feat = c * p * p;
+    const int64_t total = (int64_t)t * hp * wp * feat;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t tok = i / feat;
+        const int f = (int)(i % feat);
+        const int cc = f / (p * p), kh = (f / p) % p, kw = f % p;
+        const int ww = (int)(tok % wp), hh = (int)((tok / wp) % hp), tt = (int)(tok / ((int64_t)wp * hp));
+        const int64_t li = (((int64_t)cc * t + tt) * h + hh * p + kh) * w + ww * p + kw;
+        if (to_tokens) st_v(dst, dst_f32, i, ld_v(src, src_f32, li));
+        else st_v(dst, dst_f32, li, ld_v(src, src_f32, i));
+    }
+}
+
+// x = x - sigma_t * v, then (1 - sigma_next) * x0 + sigma_next * noise.
+__global__ void dmd_step_kernel(void *x, int x_f32, const void *v, int v_f32, const void *noise, int n_f32,
+                                float sigma_t, float sigma_next, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float x0 = ld_v(x, x_f32, i) - sigma_t * ld_v(v, v_f32, i);
+        st_v(x, x_f32, i, noise ? (1.0f - sigma_next) * x0 + sigma_next * ld_v(noise, n_f32, i) : x0);
+    }
+}
+
+int grid_elems(int64_t n) {
+    int64_t b = (n + 255) / 256;
+    return (int)(b < 1 ? 1 : (b > 148 * 32 ? 148 * 32 : b));
+}
+
+}  // namespace
+
+bool row_op_supported(int dim) { return dim > 0 && dim <= ROW_THREADS * ROW_PER_THREAD; }
+
+cudaError_t layer_norm_launch(const NormArgs &a, cudaStream_t st) {
+    if (a.rows == 0) return cudaSuccess;
+    layer_norm_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t residual_norm_launch(const NormArgs &a, void *h, int h_f32, const void *res, int res_f32, int gate,
+                                 cudaStream_t st) {
+    if (a.rows == 0) return cudaSuccess;
+    residual_norm_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a, h, h_f32, res, res_f32, gate);
+    return cudaGetLastError();
+}
+
+cudaError_t head_split_launch(const HeadSplitArgs &a, cudaStream_t st) {
+    if (a.rows == 0) return cudaSuccess;
+    head_split_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t patchify_launch(const void *src, int src_f32, void *dst, int dst_f32, int c, int t, int h, int w, int p,
+                            int to_tokens, cudaStream_t st) {
+    const int64_t total = (int64_t)t * (h / p) * (w / p) * c * p * p;
+    if (total == 0) return cudaSuccess;
+    patchify_kernel<<<grid_elems(total), 256, 0, st>>>(src, src_f32, dst, dst_f32, c, t, h, w, p, to_tokens);
+    return cudaGetLastError();
+}
+
+cudaError_t dmd_step_launch(void *x, int x_f32, const void *v, int v_f32, const void *noise, int n_f32, float sigma_t,
+                            float sigma_next, int64_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    dmd_step_kernel<<<grid_elems(n), 256, 0, st>>>(x, x_f32, v, v_f32, noise, n_f32, sigma_t, sigma_next, n);
+    return cudaGetLastError();
+}
+
+}  // namespace lx2v

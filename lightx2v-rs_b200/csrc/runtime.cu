@@ -27,6 +27,7 @@
 #include "gemm.h"
 #include "attention.h"
 #include "kvcache.h"
+#include "dit_ops.h"
 
 using namespace lx2v;
 
@@ -1611,6 +1612,148 @@ extern "C" lx2v_status lx2v_kv_cache_attention(lx2v_ctx *ctx, const lx2v_buf *q,
                         sq, c->rows, d, m, out);
     if (s) return s;
     CUDA_TRY(ctx, note_uses(ctx, {q, out}));
+    return LX2V_OK;
+}
+
+// ---- norms, head_split, patchify, dmd_step (backend.rs:214-273, 392-428) --------------------
+static int is_f32(const lx2v_buf *b) { return b && b->dtype == LX2V_F32 ? 1 : 0; }
+
+// NormKind: kind 0 = Affine { w, b } (length dim each), 1 = Mod { scale, shift }
+// (rows of the mods table).
+static lx2v_status norm_args(lx2v_ctx *ctx, NormArgs &a, size_t rows, size_t dim, int kind, const lx2v_buf *w,
+                             const lx2v_buf *b, size_t scale, size_t shift, const lx2v_buf *mods, float eps,
+                             lx2v_buf *out) {
+    if (!out || (kind != 0 && kind != 1)) return fail(ctx, LX2V_ERR_INVALID, "null output or bad norm kind %d", kind);
+    if (!row_op_supported((int)dim)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "norm rows of %zu values (max 4096)", dim);
+    if (rows * dim > out->len) return fail(ctx, LX2V_ERR_INVALID, "norm output holds fewer than rows x dim");
+    if (kind == 0 && (!w || !b || w->len < dim || b->len < dim))
+        return fail(ctx, LX2V_ERR_INVALID, "affine norm needs w and b of dim elements");
+    if (kind == 1 && (!mods || mods->len < (std::max(scale, shift) + 1) * dim))
+        return fail(ctx, LX2V_ERR_INVALID, "modulated norm: mods has too few rows");
+    memset(&a, 0, sizeof a);
+    a.out = out->ptr; a.out_f32 = is_f32(out);
+    a.rows = (int64_t)rows; a.dim = (int)dim; a.kind = kind;
+    a.w = w ? w->ptr : nullptr; a.w_f32 = is_f32(w);
+    a.b = b ? b->ptr : nullptr; a.b_f32 = is_f32(b);
+    a.mods = mods ? mods->ptr : nullptr; a.mods_f32 = is_f32(mods);
+    a.scale = (int)scale; a.shift = (int)shift; a.eps = eps;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_layer_norm(lx2v_ctx *ctx, const lx2v_buf *x, size_t rows, size_t dim, int kind,
+                                       const lx2v_buf *w, const lx2v_buf *b, size_t scale, size_t shift,
+                                       const lx2v_buf *mods, float eps, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!x || rows * dim > x->len) return fail(ctx, LX2V_ERR_INVALID, "x holds fewer than rows x dim");
+    if (x == out) return fail(ctx, LX2V_ERR_INVALID, "output aliases x");
+    NormArgs a;
+    if ((s = norm_args(ctx, a, rows, dim, kind, w, b, scale, shift, mods, eps, out))) return s;
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "layer_norm");
+    a.x = x->ptr; a.x_f32 = is_f32(x);
+    CUDA_TRY(ctx, layer_norm_launch(a, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {x, w, b, mods, out}));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_residual_norm(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_buf *a_buf, size_t rows, size_t dim,
+                                          const lx2v_buf *mods, long gate, int kind, const lx2v_buf *w,
+                                          const lx2v_buf *b, size_t scale, size_t shift, float eps,
+                                          lx2v_buf *normed) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!h || !a_buf || rows * dim > h->len || rows * dim > a_buf->len)
+        return fail(ctx, LX2V_ERR_INVALID, "h / a hold fewer than rows x dim");
+    if (normed == h || normed == a_buf) return fail(ctx, LX2V_ERR_INVALID, "normed aliases h or a");
+    if (gate >= 0 && (!mods || mods->len < ((size_t)gate + 1) * dim))
+        return fail(ctx, LX2V_ERR_INVALID, "gate row beyond mods");
+    NormArgs a;
+    if ((s = norm_args(ctx, a, rows, dim, kind, w, b, scale, shift, mods, eps, normed))) return s;
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "residual_norm");
+    a.x = h->ptr; a.x_f32 = is_f32(h);
+    CUDA_TRY(ctx, residual_norm_launch(a, h->ptr, is_f32(h), a_buf->ptr, is_f32(a_buf), gate >= 0 ? (int)gate : -1,
+                                       ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {h, a_buf, w, b, mods, normed}));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                       size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                       const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    const size_t d = heads * head_dim;
+    if (!src || !out || head_dim == 0 || head_dim % 2) return fail(ctx, LX2V_ERR_INVALID, "null src/out or odd head_dim");
+    if (col_off + d > src_stride || (rows && (rows - 1) * src_stride + col_off + d > src->len))
+        return fail(ctx, LX2V_ERR_INVALID, "head_split columns beyond src");
+    if (rows * d > out->len) return fail(ctx, LX2V_ERR_INVALID, "head_split output holds fewer than rows x heads x head_dim");
+    if (rms_w && rms_w->len < d) return fail(ctx, LX2V_ERR_INVALID, "rms weight holds fewer than heads x head_dim");
+    if ((cos == nullptr) != (sin == nullptr)) return fail(ctx, LX2V_ERR_INVALID, "RoPE needs both cos and sin");
+    if (cos && (cos->len < rows * head_dim / 2 || sin->len < rows * head_dim / 2 || cos->dtype != sin->dtype))
+        return fail(ctx, LX2V_ERR_INVALID, "cos / sin hold fewer than rows x head_dim / 2 (or differ in type)");
+    if (out == src) return fail(ctx, LX2V_ERR_INVALID, "output aliases src");
+    if (!row_op_supported((int)d)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "head_split rows of %zu values (max 4096)", d);
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "head_split");
+    HeadSplitArgs a;
+    memset(&a, 0, sizeof a);
+    a.src = src->ptr; a.src_f32 = is_f32(src);
+    a.rows = (int64_t)rows; a.src_stride = (int64_t)src_stride; a.col_off = (int64_t)col_off;
+    a.heads = (int)heads; a.head_dim = (int)head_dim;
+    a.rms_w = rms_w ? rms_w->ptr : nullptr; a.w_f32 = is_f32(rms_w);
+    a.cos = cos ? cos->ptr : nullptr; a.sin = sin ? sin->ptr : nullptr; a.cs_f32 = is_f32(cos);
+    a.eps = eps;
+    a.out = out->ptr; a.out_f32 = is_f32(out);
+    CUDA_TRY(ctx, head_split_launch(a, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {src, rms_w, cos, sin, out}));
+    return LX2V_OK;
+}
+
+static lx2v_status patchify_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t c, size_t t, size_t h, size_t w, size_t p,
+                                 lx2v_buf *dst, int to_tokens) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!src || !dst || p == 0 || h % p || w % p) return fail(ctx, LX2V_ERR_INVALID, "null buffer or h, w not multiples of p");
+    const size_t n = c * t * h * w;
+    if (src->len < n || dst->len < n) return fail(ctx, LX2V_ERR_INVALID, "buffers hold fewer than c x t x h x w");
+    if (src == dst) return fail(ctx, LX2V_ERR_INVALID, "output aliases input");
+    if (n > (1ull << 31)) return fail(ctx, LX2V_ERR_UNSUPPORTED, "latent too large");
+    if (n == 0) return LX2V_OK;
+    OpScope ps(ctx, to_tokens ? "patchify" : "unpatchify");
+    CUDA_TRY(ctx, patchify_launch(src->ptr, is_f32(src), dst->ptr, is_f32(dst), (int)c, (int)t, (int)h, (int)w, (int)p,
+                                  to_tokens, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {src, dst}));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_patchify(lx2v_ctx *ctx, const lx2v_buf *latent, size_t c, size_t t, size_t h, size_t w,
+                                     size_t p, lx2v_buf *out) {
+    return patchify_impl(ctx, latent, c, t, h, w, p, out, 1);
+}
+
+extern "C" lx2v_status lx2v_unpatchify(lx2v_ctx *ctx, const lx2v_buf *x, size_t c, size_t t, size_t h, size_t w,
+                                       size_t p, lx2v_buf *out) {
+    return patchify_impl(ctx, x, c, t, h, w, p, out, 0);
+}
+
+extern "C" lx2v_status lx2v_dmd_step(lx2v_ctx *ctx, lx2v_buf *x, const lx2v_buf *v, const lx2v_buf *noise,
+                                     float sigma_t, float sigma_next, size_t n) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!x || !v || n > x->len || n > v->len || (noise && n > noise->len))
+        return fail(ctx, LX2V_ERR_INVALID, "dmd_step buffers hold fewer than n elements");
+    if (n == 0) return LX2V_OK;
+    OpScope ps(ctx, "dmd_step");
+    CUDA_TRY(ctx, dmd_step_launch(x->ptr, is_f32(x), v->ptr, is_f32(v), noise ? noise->ptr : nullptr, is_f32(noise),
+                                  sigma_t, sigma_next, (int64_t)n, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {x, v, noise}));
     return LX2V_OK;
 }
 

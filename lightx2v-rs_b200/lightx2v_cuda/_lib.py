@@ -67,6 +67,13 @@ SIGNATURES = {
     "lx2v_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]),
     "lx2v_causal_attention": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     "lx2v_causal_attention_temporal": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
+    "lx2v_layer_norm": (_st, [_vp, _vp, _sz, _sz, ctypes.c_int, _vp, _vp, _sz, _sz, _vp, ctypes.c_float, _vp]),
+    "lx2v_residual_norm": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_long, ctypes.c_int, _vp, _vp, _sz, _sz,
+                                 ctypes.c_float, _vp]),
+    "lx2v_head_split": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp, _vp, ctypes.c_float, _vp]),
+    "lx2v_patchify": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp]),
+    "lx2v_unpatchify": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp]),
+    "lx2v_dmd_step": (_st, [_vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _sz]),
     "lx2v_kv_cache_new": (_st, [_vp, _sz, _sz, _sz, _pp]),
     "lx2v_kv_cache_free": (None, [_vp, _vp]),
     "lx2v_kv_cache_append": (_st, [_vp, _vp, _vp, _vp, _sz, _vp]),

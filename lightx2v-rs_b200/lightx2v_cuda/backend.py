@@ -301,6 +301,44 @@ class CudaBackend:
                                                              sq, sk, head_dim, tq.ctypes.data,
                                                              tk.ctypes.data, out.handle))
 
+    # ---- norms / head_split / patchify / dmd_step, backend.rs:214-273, 392-428 -----
+    @staticmethod
+    def _norm(norm):
+        """NormKind as ("affine", w, b) or ("mod", scale, shift) -> C arguments."""
+        if norm[0] == "affine":
+            return 0, norm[1].handle, norm[2].handle, 0, 0
+        assert norm[0] == "mod"
+        return 1, None, None, norm[1], norm[2]
+
+    def layer_norm(self, x: Buf, rows: int, dim: int, norm, mods: Buf | None, eps: float, out: Buf):
+        kind, w, b, scale, shift = self._norm(norm)
+        self._check(self._lib.lx2v_layer_norm(self._ctx, x.handle, rows, dim, kind, w, b, scale, shift,
+                                              mods.handle if mods is not None else None, eps, out.handle))
+
+    def residual_norm(self, h: Buf, a: Buf, rows: int, dim: int, mods: Buf, gate: int | None, norm, eps: float,
+                      normed: Buf):
+        kind, w, b, scale, shift = self._norm(norm)
+        self._check(self._lib.lx2v_residual_norm(self._ctx, h.handle, a.handle, rows, dim, mods.handle,
+                                                 -1 if gate is None else gate, kind, w, b, scale, shift, eps,
+                                                 normed.handle))
+
+    def head_split(self, src: Buf, rows: int, src_stride: int, col_off: int, heads: int, head_dim: int,
+                   rms_w: Buf | None, rope, eps: float, out: Buf):
+        cos, sin = (rope[0].handle, rope[1].handle) if rope is not None else (None, None)
+        self._check(self._lib.lx2v_head_split(self._ctx, src.handle, rows, src_stride, col_off, heads, head_dim,
+                                              rms_w.handle if rms_w is not None else None, cos, sin, eps,
+                                              out.handle))
+
+    def patchify(self, latent: Buf, c: int, t: int, h: int, w: int, p: int, out: Buf):
+        self._check(self._lib.lx2v_patchify(self._ctx, latent.handle, c, t, h, w, p, out.handle))
+
+    def unpatchify(self, x: Buf, c: int, t: int, h: int, w: int, p: int, out: Buf):
+        self._check(self._lib.lx2v_unpatchify(self._ctx, x.handle, c, t, h, w, p, out.handle))
+
+    def dmd_step(self, x: Buf, v: Buf, noise: Buf | None, sigma_t: float, sigma_next: float, n: int):
+        self._check(self._lib.lx2v_dmd_step(self._ctx, x.handle, v.handle,
+                                            noise.handle if noise is not None else None, sigma_t, sigma_next, n))
+
     # ---- KV cache / MemRoPE, backend.rs:334-390 ------------------------------------
     def kv_cache_new(self, heads: int, head_dim: int, capacity_tokens: int) -> "KvCache":
         h = ctypes.c_void_p()

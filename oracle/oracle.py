@@ -274,16 +274,11 @@ def head_split(src, rows: int, src_stride: int, col_off: int, heads: int, head_d
     """CpuBackend::head_split (cpu lib.rs:406-459) -> [heads, rows, head_dim]."""
     src = _f(src)
     out = np.empty(heads * rows * head_dim, np.float32)
-    wp = _p(_f(rms_w), _f32p) if rms_w is not None else None
-    keep = []
-    cp = sp = None
-    if rope is not None:
-        c, s_ = _f(rope[0]), _f(rope[1])
-        keep += [c, s_]
-        cp, sp = _p(c, _f32p), _p(s_, _f32p)
-    if rms_w is not None:
-        keep.append(_f(rms_w))
-        wp = _p(keep[-1], _f32p)
+    w = _f(rms_w) if rms_w is not None else None
+    c, s_ = (_f(rope[0]), _f(rope[1])) if rope is not None else (None, None)
+    wp = _p(w, _f32p) if w is not None else None
+    cp = _p(c, _f32p) if c is not None else None
+    sp = _p(s_, _f32p) if s_ is not None else None
     lib().orc_head_split(_p(src, _f32p), rows, src_stride, col_off, heads, head_dim, wp, cp, sp, eps,
                          _p(out, _f32p))
     return out.reshape(heads, rows, head_dim)
