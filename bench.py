@@ -729,6 +729,81 @@ def attention_arm(args, local_rank: int):
           flush=True)
 
 
+def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
+    """one denoising step of a Wan2.1-1.3B chunk (3 latent
+    frames of 30 x 52 patches = 4680 tokens, dim 1536, 12 heads x 128, FFN
+    8960) through all 30 blocks and the output head, at start frame 12 with
+    each layer's MemRoPE cache holding 12 frames (18720 keys) after its
+    update. Weights: one synthetic block N(0, 0.02) quantized with the
+    reference's quantizer, uploaded as 30 separate device copies; prompt
+    K/V from a random 512 x 4096 text embedding. The caches are filled by
+    running the chunks at start frames 0, 3, 6 and 9 first; every timed step
+    re-runs the chunk at frame 12 (the next DMD step of the same chunk
+    overwrites its own cache rows). ms per step from CUDA events on the
+    library's stream, L2 flushed before each."""
+    from lightx2v_cuda import F32, quant, rng
+    from lightx2v_cuda.dit import LightDitCuda, WanConfig, synthetic_block
+    cfg = WanConfig(layers=layers)
+    d = cfg.dim
+    qz = {"fp8": lambda w, r, c: quant.Fp8E4M3.quantize(w, r, c),
+          "q8": lambda w, r, c: quant.Q8.quantize(w, r, c)}[fmt]
+    t0 = time.perf_counter()
+    block = synthetic_block(cfg, 3, qz)
+    mat = lambda seed, r, c: (rng.normal(seed, r * c, 0.02), rng.normal(seed + 1, r, 0.01))
+    model = LightDitCuda(be, cfg, [block] * layers, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim),
+                         mat(905, d, d), mat(907, cfg.patch_out, d))
+    prompt = model.prepare_prompt(rng.normal(911, cfg.text_len * cfg.text_dim))
+    ft, frames = 30 * 52, 3
+    s = ft * frames
+    ang = rng.normal(931, s * cfg.head_dim // 2, 1.0)
+    ws = model.workspace(frames, ft, np.cos(ang), np.sin(ang))
+    mods = [be.upload(rng.normal(920 + l % 7, 6 * d, 0.1), F32) for l in range(layers)]
+    head = be.upload(rng.normal(930, 2 * d, 0.1), F32)
+    out = be.alloc(s * cfg.patch_out, F32)
+    latent = be.upload(rng.normal(950, cfg.in_channels * frames * 60 * 104), F32)
+    setup_s = time.perf_counter() - t0
+
+    def step(start):
+        model.patch_embed(ws, latent, cfg.in_channels, frames, 60, 104)
+        model.forward_chunk(ws, mods, head, prompt, start, out)
+
+    for start in (0, 3, 6, 9):
+        step(start)
+    for _ in range(max(args.warmup, 3)):
+        step(12)
+    be.sync()
+    n = max(3, min(args.steps, 10))
+    ms = float(np.median(timed_steps(be, ext, flush, lambda: step(12), n)))
+    sk = be.kv_cache_len(ws.caches[0])
+    # FLOPs: linears 2 M N K; self-attention 4 d per visible (query, key) pair and head
+    # (queries of frame 12 + i see the 9 + 1 + i cached frames up to their own);
+    # cross-attention 4 d x 512 keys per query and head
+    lin = 2.0 * s * d * (3 * d + d + d + d + 2 * cfg.ffn_dim) + 2.0 * s * cfg.patch_in * d + 2.0 * s * d * cfg.patch_out
+    tk = np.array(be.kv_cache_temporal(ws.caches[0]))
+    tq = 12 + np.arange(s) // ft
+    visible = int(sum(int(np.sum(tk <= t)) for t in (12, 13, 14)) * ft)
+    att = 4.0 * cfg.head_dim * cfg.heads * (visible + s * cfg.text_len)
+    flops = layers * (lin + att) - (layers - 1) * (2.0 * s * cfg.patch_in * d + 2.0 * s * d * cfg.patch_out)
+    return {"workload": f"Wan2.1-1.3B chunk step: {layers} blocks + patch embed + head, 4680 tokens, start frame 12, "
+                        f"{fmt} block weights, 12-frame MemRoPE cache", "ms_per_step": ms,
+            "tflops": flops / (ms * 1e-3) / 1e12, "flop_per_step": flops, "cache_keys": sk,
+            "visible_pairs_per_head": visible, "steps": n, "setup_s": setup_s,
+            "note": "one step = patch_embed + forward_chunk (self-attention over the cache, cross-attention, FFN, "
+                    "head) through the C ABI from Python; the caches were filled by four earlier chunks"}
+
+
+def c4_arm(args, local_rank: int):
+    import torch
+    from lightx2v_cuda import CudaBackend
+    torch.cuda.set_device(local_rank)
+    be = CudaBackend(local_rank)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    r = c4_measure(args, be, ext, flush, args.c4_format)
+    print(json.dumps({"config": "c4", "metric": "chunk_step_ms", "value": r["ms_per_step"], "unit": "ms",
+                      "higher_is_better": False, "data": "synthetic", **r}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -739,7 +814,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--m", type=int, nargs="*", default=None,
                     help="with --config c3: only these token counts of the sweep")
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn"],
+    ap.add_argument("--c4-format", default="fp8", choices=["fp8", "q8"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn", "c4"],
                     help="c2 (default): the headline FP8 linear set, with C1 / C3 and the tensor-parallel FFN as "
                          "extra keys; c1 / c3: those configs alone, one line per shape (c3: the whole M sweep)")
     args = ap.parse_args()
@@ -751,6 +827,9 @@ def main():
     elif args.config == "attn":
         if rank == 0:
             attention_arm(args, local_rank)
+    elif args.config == "c4":
+        if rank == 0:
+            c4_arm(args, local_rank)
     elif args.config != "c2":
         if rank == 0:
             config_arm(args, local_rank)
