@@ -774,6 +774,14 @@ def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
     be.sync()
     n = max(3, min(args.steps, 10))
     ms = float(np.median(timed_steps(be, ext, flush, lambda: step(12), n)))
+    prof = None
+    if getattr(args, "profile", False):
+        # per-op device time of one more step (the context records events
+        # around every op when LIGHTX2V_PROFILE is set)
+        be.profile_reset()
+        step(12)
+        be.sync()
+        prof = {k: round(v["ms"], 3) for k, v in sorted(be.profile().items(), key=lambda kv: -kv[1]["ms"])}
     sk = be.kv_cache_len(ws.caches[0])
     # FLOPs: linears 2 M N K; self-attention 4 d per visible (query, key) pair and head
     # (queries of frame 12 + i see the 9 + 1 + i cached frames up to their own);
@@ -787,19 +795,23 @@ def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
     return {"workload": f"Wan2.1-1.3B chunk step: {layers} blocks + patch embed + head, 4680 tokens, start frame 12, "
                         f"{fmt} block weights, 12-frame MemRoPE cache", "ms_per_step": ms,
             "tflops": flops / (ms * 1e-3) / 1e12, "flop_per_step": flops, "cache_keys": sk,
-            "visible_pairs_per_head": visible, "steps": n, "setup_s": setup_s,
+            "visible_pairs_per_head": visible, "steps": n, "setup_s": setup_s, "_profile": prof,
             "note": "one step = patch_embed + forward_chunk (self-attention over the cache, cross-attention, FFN, "
                     "head) through the C ABI from Python; the caches were filled by four earlier chunks"}
 
 
 def c4_arm(args, local_rank: int):
     import torch
+    if args.profile:
+        os.environ["LIGHTX2V_PROFILE"] = "1"
     from lightx2v_cuda import CudaBackend
     torch.cuda.set_device(local_rank)
     be = CudaBackend(local_rank)
     ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
     r = c4_measure(args, be, ext, flush, args.c4_format)
+    if args.profile:
+        r["profile_ms_per_step"] = r.pop("_profile", None)
     print(json.dumps({"config": "c4", "metric": "chunk_step_ms", "value": r["ms_per_step"], "unit": "ms",
                       "higher_is_better": False, "data": "synthetic", **r}), flush=True)
 
@@ -815,6 +827,7 @@ def main():
     ap.add_argument("--m", type=int, nargs="*", default=None,
                     help="with --config c3: only these token counts of the sweep")
     ap.add_argument("--c4-format", default="fp8", choices=["fp8", "q8"])
+    ap.add_argument("--profile", action="store_true", help="with --config c4: add the per-op device times of one step")
     ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn", "c4"],
                     help="c2 (default): the headline FP8 linear set, with C1 / C3 and the tensor-parallel FFN as "
                          "extra keys; c1 / c3: those configs alone, one line per shape (c3: the whole M sweep)")
