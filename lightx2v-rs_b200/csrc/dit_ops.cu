@@ -180,6 +180,137 @@ __global__ void dmd_step_kernel(void *x, int x_f32, const void *v, int v_f32, co
     }
 }
 
+// ---- vectorized row kernels: thread t owns values [8t, 8t + 8) of the row ----
+// (dim a multiple of 256, at most 4096: blockDim = dim / 8 is whole warps)
+__device__ __forceinline__ void ld8(const void *p, int f32, int64_t i, float (&v)[8]) {
+    if (f32) {
+        const float4 a = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + i);
+        const float4 b = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + i + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p) + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            v[2 * k] = __uint_as_float(w[k] << 16);
+            v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+    }
+}
+__device__ __forceinline__ void st8(void *p, int f32, int64_t i, const float (&v)[8]) {
+    if (f32) {
+        float4 *d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p) + i);
+        d[0] = make_float4(v[0], v[1], v[2], v[3]);
+        d[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+            w[k] = *reinterpret_cast<const uint32_t *>(&b);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ float block_sum_any(float v, float *red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+    const int nw = (int)(blockDim.x >> 5);
+    for (int w = 0; w < nw; ++w) t += red[w];
+    return t;
+}
+
+template <bool RESID>
+__global__ void __launch_bounds__(512) norm_vec_kernel(NormArgs a, void *h, int h_f32, const void *res, int res_f32,
+                                                       int gate) {
+    __shared__ float red[16];
+    const int64_t r = blockIdx.x;
+    const int j0 = threadIdx.x * 8;
+    const int64_t i0 = r * a.dim + j0;
+    float v[8];
+    if (RESID) {
+        float hv[8], av[8], g[8];
+        ld8(h, h_f32, i0, hv);
+        ld8(res, res_f32, i0, av);
+        if (gate >= 0) ld8(a.mods, a.mods_f32, (int64_t)gate * a.dim + j0, g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = hv[k] + av[k] * (gate >= 0 ? g[k] : 1.0f);
+        st8(h, h_f32, i0, v);
+    } else {
+        ld8(a.x, a.x_f32, i0, v);
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += v[k];
+    const float mean = block_sum_any(s, red) / (float)a.dim;
+    float vs = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float c = v[k] - mean;
+        vs += c * c;
+    }
+    const float var = block_sum_any(vs, red) / (float)a.dim;
+    const float inv = 1.0f / sqrtf(var + a.eps);
+    float p[8], q[8], o[8];
+    if (a.kind == 0) {
+        ld8(a.w, a.w_f32, j0, p);
+        ld8(a.b, a.b_f32, j0, q);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = (v[k] - mean) * inv * p[k] + q[k];
+    } else {
+        ld8(a.mods, a.mods_f32, (int64_t)a.scale * a.dim + j0, p);
+        ld8(a.mods, a.mods_f32, (int64_t)a.shift * a.dim + j0, q);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = (v[k] - mean) * inv * (1.0f + p[k]) + q[k];
+    }
+    st8(a.out, a.out_f32, i0, o);
+}
+
+// head_split with 8 values (4 RoPE pairs of one head) per thread.
+__global__ void __launch_bounds__(512) head_split_vec_kernel(HeadSplitArgs a) {
+    __shared__ float red[16];
+    const int64_t r = blockIdx.x;
+    const int d = a.heads * a.head_dim;
+    const int j0 = threadIdx.x * 8;
+    float x[8];
+    ld8(a.src, a.src_f32, r * a.src_stride + a.col_off + j0, x);
+    if (a.rms_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
+        const float ms = block_sum_any(ss, red) / (float)d;
+        const float inv = 1.0f / sqrtf(ms + a.eps);
+        float w[8];
+        ld8(a.rms_w, a.w_f32, j0, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = x[k] * inv * w[k];
+    }
+    const int h = j0 / a.head_dim, e = j0 % a.head_dim;
+    float o[8];
+    if (a.cos) {
+        const int64_t ci = r * (a.head_dim / 2) + e / 2;
+        float c[4], sn[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            c[k] = ld_v(a.cos, a.cs_f32, ci + k);
+            sn[k] = ld_v(a.sin, a.cs_f32, ci + k);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            o[2 * k] = x[2 * k] * c[k] - x[2 * k + 1] * sn[k];
+            o[2 * k + 1] = x[2 * k] * sn[k] + x[2 * k + 1] * c[k];
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = x[k];
+    }
+    st8(a.out, a.out_f32, ((int64_t)h * a.rows + r) * a.head_dim + e, o);
+}
+
 int grid_elems(int64_t n) {
     int64_t b = (n + 255) / 256;
     return (int)(b < 1 ? 1 : (b > 148 * 32 ? 148 * 32 : b));
@@ -189,8 +320,17 @@ int grid_elems(int64_t n) {
 
 bool row_op_supported(int dim) { return dim > 0 && dim <= ROW_THREADS * ROW_PER_THREAD; }
 
+// The vectorized kernels need whole warps of 8-value threads and 16-byte
+// aligned rows (every buffer and row offset here is a multiple of 16 bytes
+// when dim % 256 == 0).
+static bool vec_ok(int dim) { return dim % 256 == 0 && dim <= 4096; }
+
 cudaError_t layer_norm_launch(const NormArgs &a, cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    if (vec_ok(a.dim)) {
+        norm_vec_kernel<false><<<(unsigned)a.rows, a.dim / 8, 0, st>>>(a, nullptr, 0, nullptr, 0, -1);
+        return cudaGetLastError();
+    }
     layer_norm_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a);
     return cudaGetLastError();
 }
@@ -198,12 +338,23 @@ cudaError_t layer_norm_launch(const NormArgs &a, cudaStream_t st) {
 cudaError_t residual_norm_launch(const NormArgs &a, void *h, int h_f32, const void *res, int res_f32, int gate,
                                  cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    if (vec_ok(a.dim)) {
+        norm_vec_kernel<true><<<(unsigned)a.rows, a.dim / 8, 0, st>>>(a, h, h_f32, res, res_f32, gate);
+        return cudaGetLastError();
+    }
     residual_norm_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a, h, h_f32, res, res_f32, gate);
     return cudaGetLastError();
 }
 
 cudaError_t head_split_launch(const HeadSplitArgs &a, cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    const int d = a.heads * a.head_dim;
+    // 8 values a thread never straddle a head; src rows, the column offset and
+    // the RoPE rows stay 16-byte aligned
+    if (vec_ok(d) && a.head_dim % 8 == 0 && a.src_stride % 8 == 0 && a.col_off % 8 == 0) {
+        head_split_vec_kernel<<<(unsigned)a.rows, d / 8, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     head_split_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a);
     return cudaGetLastError();
 }

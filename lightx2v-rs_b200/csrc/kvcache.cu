@@ -61,6 +61,13 @@ cudaError_t kv_copy_rows_launch(const void *src, int src_f32, int64_t src_hs, in
                                 int dst_f32, int64_t dst_hs, int64_t dst_row0, int64_t rows, int d, int heads,
                                 cudaStream_t st) {
     if (rows <= 0 || heads <= 0) return cudaSuccess;
+    if (src_f32 == dst_f32) {
+        // same element type: one strided copy, a row block per head
+        const size_t es = src_f32 ? 4 : 2;
+        return cudaMemcpy2DAsync((char *)dst + (size_t)dst_row0 * d * es, (size_t)dst_hs * d * es,
+                                 (const char *)src + (size_t)src_row0 * d * es, (size_t)src_hs * d * es,
+                                 (size_t)rows * d * es, (size_t)heads, cudaMemcpyDeviceToDevice, st);
+    }
     kv_copy_rows_kernel<<<grid_for(rows * d * heads), 256, 0, st>>>(src, src_f32, src_hs, src_row0, dst, dst_f32,
                                                                     dst_hs, dst_row0, rows, d, heads);
     return cudaGetLastError();
