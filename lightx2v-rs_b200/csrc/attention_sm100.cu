@@ -29,10 +29,13 @@
 // A query that sees no key gets NaN, as the reference's softmax of an
 // all -inf row does.
 //
-// Warp roles (256 threads, one CTA per SM: TMEM 512 columns):
-//   warp 0     TMA producer: Q once, then K_j / V_j^T into a 2-stage ring
-//   warp 1     TMEM allocator and MMA issuer (one thread)
-//   warps 4-7  softmax, then the epilogue (O / l -> out)
+// Warp roles (384 threads, one CTA per SM: TMEM 512 columns):
+//   warp 0      TMA producer: Q once, then K_j / V_j^T into a 2-stage ring
+//   warp 1      TMEM allocator and MMA issuer (one thread)
+//   warps 4-11  softmax, then the epilogue (O / l -> out): two warpgroups,
+//               each taking half of every S block's key columns (and half of
+//               O's columns) for all 128 query rows, so that every scheduler
+//               runs two softmax warps
 // Every mbarrier wait is bounded; on expiry the kernel records an error
 // word, drains its own copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -60,7 +63,7 @@ constexpr int AT_OFF_V = AT_OFF_K + AT_NS * AT_TILE;
 constexpr int AT_OFF_BAR = AT_OFF_V + AT_NS * AT_TILE;
 // q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2], p_full[2], pv_done, o_full, drain
 constexpr int AT_NUM_BARS = 1 + 4 * AT_NS + 2 + 2 + 3;
-constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16;
+constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16 + (512 + 256 + 4) * 4;
 constexpr int AT_TMEM_COLS = 512;  // O: 0-127, S/P buffers: 128-255, 256-383
 constexpr float AT_RESCALE_LOG2 = 8.0f;
 
@@ -85,7 +88,7 @@ __device__ __forceinline__ bool block_full(const AttnParams &p, int j, int2 tqr)
     return false;
 }
 
-__global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_constant__ AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AT_OFF_BAR);
@@ -123,11 +126,12 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&p_full[b], 4);
+            mbar_init(&p_full[b], 8);
         }
         mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
+        *reinterpret_cast<volatile int *>(reinterpret_cast<float *>(tmem_slot + 4) + 768) = 0;  // softmax abort flag
         fence_mbar_init();
         tma_prefetch_desc(&p.tmap_q);
         tma_prefetch_desc(&p.tmap_k);
@@ -226,42 +230,54 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ---------------- softmax + epilogue: thread = query row ----------------
-        const int r = (warp - 4) * 32 + lane;
+        // ---------------- softmax + epilogue ----------------
+        // Two warpgroups share each query row: warpgroup wg takes the key
+        // columns [64 wg, 64 wg + 64) of every S block (and the same half of
+        // O's columns). Thread = query row (TMEM lane). The halves' row maxima
+        // meet in shared memory, so both warpgroups use the same running max.
+        const int wg = (warp - 4) >> 2;
+        const int r = (warp & 3) * 32 + lane;
         const int q = qt * AT_BQ + r;
         const bool q_ok = q < p.sq;
-        const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const int tq_row = (p.mask_mode == ATT_MASK_TEMPORAL && q_ok) ? p.tq[q] : 0;
+        float *xmax = reinterpret_cast<float *>(tmem_slot + 4);  // [2 blocks][2 warpgroups][128 rows]
+        volatile int *abort_flag = reinterpret_cast<volatile int *>(xmax + 768);
         const float NEG_INF = -INFINITY;
         float m_run = NEG_INF, l = 0.0f;
         int it = 0;
         bool ok = true;
+        // Both warpgroups meet at a named barrier every block, so neither may
+        // leave the loop alone: a failed wait only sets abort_flag, and both
+        // leave together right after the next barrier.
         for (int j = 0; j < nblk; ++j) {
             if (!block_live(p, j, tqr)) continue;
             const bool full = block_full(p, j, tqr);
             int okw = 1;
             if (lane == 0) okw = mbar_wait_bounded(&s_full[it & 1], (uint32_t)((it >> 1) & 1), err, lim) ? 1 : 0;
             okw = __shfl_sync(0xFFFFFFFFu, okw, 0);
-            if (!okw) { ok = false; break; }
+            if (!okw && lane == 0) *abort_flag = 1;
             tc_fence_after();
             const uint32_t scol = 128u + (uint32_t)((it & 1) * 128);
-            // the row's 128 raw scores: four loads in flight, one wait
-            uint32_t sv[128];
-            tmem_ld_32x32b_x32(lane_base + scol, *reinterpret_cast<uint32_t(*)[32]>(sv));
-            tmem_ld_32x32b_x32(lane_base + scol + 32u, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-            tmem_ld_32x32b_x32(lane_base + scol + 64u, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
-            tmem_ld_32x32b_x32(lane_base + scol + 96u, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
-            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv));
-            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 64));
-            tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 96));
+            // this half's 64 raw scores: two loads in flight, one wait
+            uint32_t sv[64];
+            if (okw) {
+                tmem_ld_32x32b_x32(lane_base + scol + (uint32_t)(wg * 64), *reinterpret_cast<uint32_t(*)[32]>(sv));
+                tmem_ld_32x32b_x32(lane_base + scol + (uint32_t)(wg * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+                tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv));
+                tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) sv[i] = 0xFF800000u;
+            }
             if (!full) {
-                // a block some query does not see in full: visibility bits of
-                // the row's 128 keys (a small rolled loop), then -inf where hidden
-                const int k0 = j * AT_BK;
-                uint32_t vm[4];
+                // some query of the tile does not see all of this block: the
+                // visibility bits of the row's 64 keys (a rolled loop), then
+                // -inf where hidden
+                const int k0 = j * AT_BK + wg * 64;
+                uint32_t vm[2];
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t w = 0;
                     const int kc = k0 + c * 32;
                     if (p.mask_mode == ATT_MASK_BITS && q_ok && kc < p.sk) {
@@ -278,38 +294,49 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
                     vm[c] = w;
                 }
 #pragma unroll
-                for (int i = 0; i < 128; ++i)
+                for (int i = 0; i < 64; ++i)
                     if (!((vm[i >> 5] >> (i & 31)) & 1u)) sv[i] = 0xFF800000u;  // -inf
             }
-            // row max of the raw scores (scale > 0 commutes with max)
+            // row max of the raw scores (scale > 0 commutes with max), both halves
             float mx0 = NEG_INF, mx1 = NEG_INF, mx2 = NEG_INF, mx3 = NEG_INF;
 #pragma unroll
-            for (int i = 0; i < 128; i += 4) {
+            for (int i = 0; i < 64; i += 4) {
                 mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
                 mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
                 mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
                 mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
             }
-            const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
+            float *xm = xmax + (it & 1) * 256;
+            xm[wg * 128 + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            // also orders both halves' S loads before either half's P stores
+            // (P overwrites S's first 64 columns, half of which the other
+            // warpgroup reads)
+            tc_fence_before();
+            named_bar_sync(1, 256);
+            tc_fence_after();
+            if (*abort_flag) { ok = false; break; }
+            const float mx = fmaxf(xm[r], xm[128 + r]) * p.scale_log2;
             const float m_new = fmaxf(m_run, mx);
             const bool need = m_run != NEG_INF && m_new > m_run + AT_RESCALE_LOG2;
             if (__any_sync(0xFFFFFFFFu, need)) {
                 // O holds P_0..P_{it-1} V scaled by 2^-m_run: wait for the last
-                // of those products, then rescale this warp's rows in TMEM
+                // of those products, then rescale this warp's rows (this
+                // warpgroup's half of the columns) in TMEM
                 if (lane == 0) okw = mbar_wait_bounded(pv_done, (uint32_t)((it - 1) & 1), err, lim) ? 1 : 0;
                 okw = __shfl_sync(0xFFFFFFFFu, okw, 0);
-                if (!okw) { ok = false; break; }
+                if (!okw && lane == 0) *abort_flag = 1;  // both warpgroups leave at the next barrier
                 tc_fence_after();
                 const float corr = need ? ex2(m_run - m_new) : 1.0f;
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2 && okw; ++c) {
+                    const uint32_t oc = (uint32_t)(wg * 64 + c * 32);
                     uint32_t t[32];
-                    tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), t);
+                    tmem_ld_32x32b_x32(lane_base + oc, t);
                     tmem_wait_ld_regs(t);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[16]>(t));
-                    tmem_st_32x32b_x16(lane_base + (uint32_t)(c * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(t + 16));
+                    tmem_st_32x32b_x16(lane_base + oc, *reinterpret_cast<uint32_t(*)[16]>(t));
+                    tmem_st_32x32b_x16(lane_base + oc + 16u, *reinterpret_cast<uint32_t(*)[16]>(t + 16));
                 }
                 tmem_wait_st();
                 if (need) {
@@ -320,25 +347,20 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
             if (m_run == NEG_INF) m_run = m_new;  // nothing visible so far: O holds zeros
             const float nm = m_run == NEG_INF ? 0.0f : -m_run;
             const float sc = p.scale_log2;
-            uint32_t pk[64];
+            uint32_t pk[32];
             float ls0 = 0.0f, ls1 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
                 const float a = ex2(fmaf(__uint_as_float(sv[2 * i]), sc, nm));
                 const float b = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), sc, nm));
                 ls0 += a;
                 ls1 += b;
                 pk[i] = pack_bf16x2(a, b);
             }
-            const float lsum = ls0 + ls1;
-            l += lsum;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t t[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) t[i] = pk[c * 16 + i];
-                tmem_st_32x32b_x16(lane_base + scol + (uint32_t)(c * 16), t);
-            }
+            l += ls0 + ls1;
+            // keys [64 wg, 64 wg + 64) -> P columns [32 wg, 32 wg + 32)
+            tmem_st_32x32b_x16(lane_base + scol + (uint32_t)(wg * 32), *reinterpret_cast<uint32_t(*)[16]>(pk));
+            tmem_st_32x32b_x16(lane_base + scol + (uint32_t)(wg * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -346,6 +368,11 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
             ++it;
         }
         // ---------------- epilogue: out[q, h*D + c] = O / l ----------------
+        // every softmax thread arrives here (also after an error) for the row-sum exchange
+        float *xl = xmax + 512;
+        xl[wg * 128 + r] = l;
+        named_bar_sync(1, 256);
+        const float lt = xl[r] + xl[128 + r];
         if (ok && it > 0) {
             int okw = 1;
             if (lane == 0) okw = mbar_wait_bounded(o_full, 0, err, lim) ? 1 : 0;
@@ -354,13 +381,13 @@ __global__ void __launch_bounds__(256, 1) attention_tc_kernel(const __grid_const
         }
         if (ok) {
             tc_fence_after();
-            const float inv = 1.0f / l;  // l == 0 (no visible key): NaN, as the reference
-            const int64_t obase = (int64_t)q * p.heads * AT_D + (int64_t)h * AT_D;
+            const float inv = 1.0f / lt;  // lt == 0 (no visible key): NaN, as the reference
+            const int64_t obase = (int64_t)q * p.heads * AT_D + (int64_t)h * AT_D + wg * 64;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t t[32];
                 if (it > 0) {
-                    tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), t);
+                    tmem_ld_32x32b_x32(lane_base + (uint32_t)(wg * 64 + c * 32), t);
                     tmem_wait_ld_regs(t);
                 } else {
 #pragma unroll
@@ -481,7 +508,7 @@ cudaError_t attention_tc_launch(const AttnParams &p, cudaStream_t st) {
         if (slot) slot->store(1);
     }
     const int n_qt = (p.sq + AT_BQ - 1) / AT_BQ;
-    attention_tc_kernel<<<n_qt * p.heads, 256, AT_SMEM, st>>>(p);
+    attention_tc_kernel<<<n_qt * p.heads, 384, AT_SMEM, st>>>(p);
     return cudaGetLastError();
 }
 
