@@ -75,23 +75,6 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 2^x on the FMA pipe, for a share of the softmax exponentials so that the
-// MUFU unit (ex2) is not the bottleneck: x = n + f with n = floor(x) taken
-// from the low bits of x + 1.5 * 2^23 added rounding down, 2^f for f in
-// [0, 1) from a degree-3 polynomial (coefficients fitted here to 2^f on
-// [0, 1] in relative error: at most 7.5e-5, far below the bf16 rounding of
-// P), and 2^n added to the exponent field. x <= -126 (including the -inf of
-// hidden keys) gives exactly 0 and NaN stays NaN, as through ex2.
-__device__ __forceinline__ float ex2_fma(float x) {
-    const float y = __fadd_rd(x, 12582912.0f);  // 1.5 * 2^23: floor(x) in the low mantissa bits
-    const float n = y - 12582912.0f;
-    const float f = x - n;
-    const float p = fmaf(fmaf(fmaf(0.07802403f, f, 0.22606707f), f, 0.69583398f), f, 0.99992514f);
-    // (bits(y) - bits(1.5 * 2^23)) << 23 == bits(y) << 23 modulo 2^32
-    const float r = __int_as_float(__float_as_int(p) + (__float_as_int(y) << 23));
-    return (x > -126.0f || x != x) ? r : 0.0f;  // a NaN score stays NaN, as through ex2
-}
-
 // Whether key block j can hold a key that some query of the tile sees, and
 // whether every query of the tile sees every key of it (no per-element mask).
 __device__ __forceinline__ bool block_live(const AttnParams &p, int j, int2 tqr) {
@@ -366,13 +349,10 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
             const float sc = p.scale_log2;
             uint32_t pk[32];
             float ls0 = 0.0f, ls1 = 0.0f;
-            // one pair in three through the FMA-pipe exp2, the rest through ex2
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                const float xa = fmaf(__uint_as_float(sv[2 * i]), sc, nm);
-                const float xb = fmaf(__uint_as_float(sv[2 * i + 1]), sc, nm);
-                const float a = (i % 3 == 2) ? ex2_fma(xa) : ex2(xa);
-                const float b = (i % 3 == 2) ? ex2_fma(xb) : ex2(xb);
+                const float a = ex2(fmaf(__uint_as_float(sv[2 * i]), sc, nm));
+                const float b = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), sc, nm));
                 ls0 += a;
                 ls1 += b;
                 pk[i] = pack_bf16x2(a, b);
