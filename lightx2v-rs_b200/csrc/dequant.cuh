@@ -190,11 +190,14 @@ __device__ __forceinline__ void q4_products(const uint2 raw, float s, float z, f
     const float2 nz = make_float2(-z, -z), s2 = make_float2(s, s);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
+        // low and high nibbles of the four bytes, then one byte permute per
+        // value builds the float 2^23 + c (byte 3 = 0x4B, byte 0 = c)
+        const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float2 c;
-            c.x = __uint_as_float(((w[j] >> (8 * i)) & 0xFu) | 0x4B000000u);
-            c.y = __uint_as_float(((w[j] >> (8 * i + 4)) & 0xFu) | 0x4B000000u);
+            c.x = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | (uint32_t)i));
+            c.y = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | (uint32_t)i));
             p[4 * j + i] = __fmul2_rn(__fadd2_rn(__fadd2_rn(c, m23), nz), s2);
         }
     }

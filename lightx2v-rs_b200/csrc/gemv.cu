@@ -26,6 +26,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstring>
 #include "gemm_common.cuh"  // decoders, GELU
 
 namespace lx2v {
@@ -131,11 +132,21 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int spli
     const int n_warp = tile * GV_ROWS + warp * 8;  // first of this warp's 8 rows
     const int n = n_warp + g;                      // this thread's B row
 
+    // Launched as a programmatic dependent of the previous kernel: the next
+    // kernel may launch as soon as every CTA of this one has started, and
+    // this one's weight loads (immutable, nothing earlier in the stream
+    // writes them) are in flight before it waits for the previous kernel.
+    griddep_launch_dependents();
+
     // 1. issue every weight load of this thread's k-range
     GvChunk<FMT> ck[GV_MAXCH];
 #pragma unroll
     for (int j = 0; j < GV_MAXCH; ++j)
         if (j < nch) gv_load<FMT>(a, n, k_begin + j * F::KC + c * F::VT, ck[j]);
+
+    // everything below reads x or writes y / partials / arrival counters,
+    // which earlier kernels in the stream may still use
+    griddep_wait();
 
     // 2. meanwhile stage x rows (16, zero beyond M) of the k-range as bf16,
     //    row stride kext + 8, 8 values per thread and step
@@ -186,13 +197,17 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(LinearArgs a, int spli
         const int col = warp * 8 + 2 * c;
         __stcg(reinterpret_cast<float2 *>(mine + g * GV_ROWS + col), make_float2(d[0], d[1]));
         __stcg(reinterpret_cast<float2 *>(mine + (g + 8) * GV_ROWS + col), make_float2(d[2], d[3]));
-        __threadfence();
+        // the CTA's partial stores, then one GPU-scope fence (cumulative over
+        // the stores the barrier ordered before it) and the arrival
         __syncthreads();
         __shared__ int last;
-        if (threadIdx.x == 0) last = atomicAdd(arrivals + tile, 1) == splits - 1;
+        if (threadIdx.x == 0) {
+            __threadfence();
+            last = atomicAdd(arrivals + tile, 1) == splits - 1;
+            if (last) __threadfence();  // the other CTAs' partials are visible below
+        }
         __syncthreads();
         if (!last) return;
-        __threadfence();
         float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         for (int sp = 0; sp < splits; ++sp) {
             const float *p = partials + (int64_t)(tile * splits + sp) * (16 * GV_ROWS);
@@ -242,8 +257,18 @@ cudaError_t gemv_launch_t(const LinearArgs &a, int num_sms, float *partials, int
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<tiles * splits, GV_THREADS, smem, st>>>(a, splits, per, partials, arrivals);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(tiles * splits);
+    cfg.blockDim = dim3(GV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, splits, per, partials, arrivals);
 }
 
 }  // namespace

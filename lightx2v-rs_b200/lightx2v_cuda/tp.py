@@ -10,7 +10,9 @@ Split over P ranks:
   - the partials are summed with one all-reduce (NCCL over NVLink, on the
     backend's stream), b2 is added once (by rank 0, inside its partial), and
     the gated residual h += gate * sum is applied on every rank, which keeps
-    h replicated.
+    h replicated. The partials are bf16 by default (the activation precision
+    of the CUDA backend, half the bytes on NVLink; each partial is rounded
+    once, within the north star's 1e-2) or f32 on request.
 Hidden features are split on boundaries that are multiples of the FFN2
 weight's quantization group (and of 128), so every rank's W2 slice is a
 whole number of the reference's groups: the shard holds exactly the
@@ -75,8 +77,9 @@ class TensorParallelFFN:
     quantized weights (every rank holds the same host copy), `b1` [F] and
     `b2` [D] f32. The backend must have joined the group (`comm_init`)."""
 
-    def __init__(self, be, rank: int, world: int, w1, b1, w2, b2):
+    def __init__(self, be, rank: int, world: int, w1, b1, w2, b2, partial_dtype: int = L.BF16):
         self.be, self.rank, self.world = be, rank, world
+        self.partial_dtype = partial_dtype
         self.dim, self.ffn = w1.cols, w1.rows
         assert w2.rows == self.dim and w2.cols == self.ffn
         unit = int(np.lcm(w2.group, 128))
@@ -92,12 +95,14 @@ class TensorParallelFFN:
     def collective_desc(self) -> str:
         if self.world == 1:
             return "none (one rank)"
-        return (f"one NCCL all-reduce (sum) of the f32 [rows, {self.dim}] FFN2 partials per step, on the "
+        dt = "f32" if self.partial_dtype == L.F32 else "bf16"
+        return (f"one NCCL all-reduce (sum) of the {dt} [rows, {self.dim}] FFN2 partials per step, on the "
                 "backend's stream")
 
     def _scratch(self, rows: int):
         if rows not in self._bufs:
-            self._bufs[rows] = (self.be.alloc(rows * self.local, L.BF16), self.be.alloc(rows * self.dim, L.F32))
+            self._bufs[rows] = (self.be.alloc(rows * self.local, L.BF16),
+                                self.be.alloc(rows * self.dim, self.partial_dtype))
         return self._bufs[rows]
 
     def forward(self, x, rows: int, h, mods, gate: int):
