@@ -729,21 +729,31 @@ def attention_arm(args, local_rank: int):
           flush=True)
 
 
-def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
-    """one denoising step of a Wan2.1-1.3B chunk (3 latent
-    frames of 30 x 52 patches = 4680 tokens, dim 1536, 12 heads x 128, FFN
-    8960) through all 30 blocks and the output head, at start frame 12 with
-    each layer's MemRoPE cache holding 12 frames (18720 keys) after its
-    update. Weights: one synthetic block N(0, 0.02) quantized with the
-    reference's quantizer, uploaded as 30 separate device copies; prompt
-    K/V from a random 512 x 4096 text embedding. The caches are filled by
-    running the chunks at start frames 0, 3, 6 and 9 first; every timed step
-    re-runs the chunk at frame 12 (the next DMD step of the same chunk
-    overwrites its own cache rows). ms per step from CUDA events on the
-    library's stream, L2 flushed before each."""
+# The chunk-step configs of BASELINE.json: (WanConfig fields, latent frame h x w)
+CHUNK_PRESETS = {
+    # Wan2.1-T2V-1.3B, 832 x 480 -> latent 104 x 60 -> 52 x 30 patches = 1560 tokens / frame
+    "c4": ({"heads": 12, "head_dim": 128, "ffn_dim": 8960, "in_channels": 16, "out_channels": 16}, (60, 104)),
+    # Wan2.2-TI2V-5B shape, 1280 x 704 -> latent 80 x 44 (48 channels) -> 40 x 22 = 880 tokens / frame;
+    # WanConfig has no 5B preset, so the model is built from these fields directly
+    "c5": ({"heads": 24, "head_dim": 128, "ffn_dim": 14336, "in_channels": 48, "out_channels": 48}, (44, 80)),
+}
+
+
+def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8", layers: int = 30):
+    """BASELINE configs C4 / C5: one denoising step of a 3-latent-frame chunk
+    through all blocks and the output head, at start frame 12 with each
+    layer's MemRoPE cache holding 12 frames after its update. Weights: one
+    synthetic block N(0, 0.02) quantized with the reference's quantizer,
+    uploaded as `layers` separate device copies; prompt K/V from a random
+    512 x 4096 text embedding. The caches are filled by running the chunks
+    at start frames 0, 3, 6 and 9 first; every timed step re-runs the chunk
+    at frame 12 (the next DMD step of the same chunk overwrites its own
+    cache rows). ms per step from CUDA events on the library's stream, L2
+    flushed before each."""
     from lightx2v_cuda import F32, quant, rng
     from lightx2v_cuda.dit import LightDitCuda, WanConfig, synthetic_block
-    cfg = WanConfig(layers=layers)
+    fields, (lh, lw) = CHUNK_PRESETS[preset]
+    cfg = WanConfig(layers=layers, **fields)
     d = cfg.dim
     qz = {"fp8": lambda w, r, c: quant.Fp8E4M3.quantize(w, r, c),
           "q8": lambda w, r, c: quant.Q8.quantize(w, r, c)}[fmt]
@@ -753,18 +763,18 @@ def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
     model = LightDitCuda(be, cfg, [block] * layers, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim),
                          mat(905, d, d), mat(907, cfg.patch_out, d))
     prompt = model.prepare_prompt(rng.normal(911, cfg.text_len * cfg.text_dim))
-    ft, frames = 30 * 52, 3
+    ft, frames = (lh // cfg.patch) * (lw // cfg.patch), 3
     s = ft * frames
     ang = rng.normal(931, s * cfg.head_dim // 2, 1.0)
     ws = model.workspace(frames, ft, np.cos(ang), np.sin(ang))
     mods = [be.upload(rng.normal(920 + l % 7, 6 * d, 0.1), F32) for l in range(layers)]
     head = be.upload(rng.normal(930, 2 * d, 0.1), F32)
     out = be.alloc(s * cfg.patch_out, F32)
-    latent = be.upload(rng.normal(950, cfg.in_channels * frames * 60 * 104), F32)
+    latent = be.upload(rng.normal(950, cfg.in_channels * frames * lh * lw), F32)
     setup_s = time.perf_counter() - t0
 
     def step(start):
-        model.patch_embed(ws, latent, cfg.in_channels, frames, 60, 104)
+        model.patch_embed(ws, latent, cfg.in_channels, frames, lh, lw)
         model.forward_chunk(ws, mods, head, prompt, start, out)
 
     for start in (0, 3, 6, 9):
@@ -783,24 +793,26 @@ def c4_measure(args, be, ext, flush, fmt: str = "fp8", layers: int = 30):
         be.sync()
         prof = {k: round(v["ms"], 3) for k, v in sorted(be.profile().items(), key=lambda kv: -kv[1]["ms"])}
     sk = be.kv_cache_len(ws.caches[0])
-    # FLOPs: linears 2 M N K; self-attention 4 d per visible (query, key) pair and head
-    # (queries of frame 12 + i see the 9 + 1 + i cached frames up to their own);
-    # cross-attention 4 d x 512 keys per query and head
-    lin = 2.0 * s * d * (3 * d + d + d + d + 2 * cfg.ffn_dim) + 2.0 * s * cfg.patch_in * d + 2.0 * s * d * cfg.patch_out
+    # FLOPs: block linears 2 M N K each layer, patch embed and head once;
+    # self-attention 4 d per visible (query, key) pair and head (queries of
+    # frame 12 + i see the cached frames up to their own); cross-attention
+    # 4 d x 512 keys per query and head
+    blk = 2.0 * s * d * (3 * d + d + d + d + 2 * cfg.ffn_dim)
+    ends = 2.0 * s * cfg.patch_in * d + 2.0 * s * d * cfg.patch_out
     tk = np.array(be.kv_cache_temporal(ws.caches[0]))
-    tq = 12 + np.arange(s) // ft
     visible = int(sum(int(np.sum(tk <= t)) for t in (12, 13, 14)) * ft)
     att = 4.0 * cfg.head_dim * cfg.heads * (visible + s * cfg.text_len)
-    flops = layers * (lin + att) - (layers - 1) * (2.0 * s * cfg.patch_in * d + 2.0 * s * d * cfg.patch_out)
-    return {"workload": f"Wan2.1-1.3B chunk step: {layers} blocks + patch embed + head, 4680 tokens, start frame 12, "
-                        f"{fmt} block weights, 12-frame MemRoPE cache", "ms_per_step": ms,
+    flops = layers * (blk + att) + ends
+    return {"workload": f"{preset}: {layers} blocks (dim {d}, {cfg.heads} x {cfg.head_dim} heads, FFN {cfg.ffn_dim}) + "
+                        f"patch embed + head, {s} tokens ({frames} frames x {ft}), start frame 12, {fmt} block "
+                        f"weights, 12-frame MemRoPE cache", "ms_per_step": ms,
             "tflops": flops / (ms * 1e-3) / 1e12, "flop_per_step": flops, "cache_keys": sk,
             "visible_pairs_per_head": visible, "steps": n, "setup_s": setup_s, "_profile": prof,
             "note": "one step = patch_embed + forward_chunk (self-attention over the cache, cross-attention, FFN, "
                     "head) through the C ABI from Python; the caches were filled by four earlier chunks"}
 
 
-def c4_arm(args, local_rank: int):
+def chunk_arm(args, local_rank: int):
     import torch
     if args.profile:
         os.environ["LIGHTX2V_PROFILE"] = "1"
@@ -809,10 +821,11 @@ def c4_arm(args, local_rank: int):
     be = CudaBackend(local_rank)
     ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local_rank))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
-    r = c4_measure(args, be, ext, flush, args.c4_format)
+    r = chunk_step_measure(args, be, ext, flush, args.config, args.chunk_format)
+    prof = r.pop("_profile", None)
     if args.profile:
-        r["profile_ms_per_step"] = r.pop("_profile", None)
-    print(json.dumps({"config": "c4", "metric": "chunk_step_ms", "value": r["ms_per_step"], "unit": "ms",
+        r["profile_ms_per_step"] = prof
+    print(json.dumps({"config": args.config, "metric": "chunk_step_ms", "value": r["ms_per_step"], "unit": "ms",
                       "higher_is_better": False, "data": "synthetic", **r}), flush=True)
 
 
@@ -826,9 +839,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--m", type=int, nargs="*", default=None,
                     help="with --config c3: only these token counts of the sweep")
-    ap.add_argument("--c4-format", default="fp8", choices=["fp8", "q8"])
-    ap.add_argument("--profile", action="store_true", help="with --config c4: add the per-op device times of one step")
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn", "c4"],
+    ap.add_argument("--chunk-format", default="fp8", choices=["fp8", "q8"],
+                    help="with --config c4 / c5: the block weights' format")
+    ap.add_argument("--profile", action="store_true",
+                    help="with --config c4 / c5: add the per-op device times of one step")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "attn", "c4", "c5"],
                     help="c2 (default): the headline FP8 linear set, with C1 / C3 and the tensor-parallel FFN as "
                          "extra keys; c1 / c3: those configs alone, one line per shape (c3: the whole M sweep)")
     args = ap.parse_args()
@@ -840,9 +855,9 @@ def main():
     elif args.config == "attn":
         if rank == 0:
             attention_arm(args, local_rank)
-    elif args.config == "c4":
+    elif args.config in ("c4", "c5"):
         if rank == 0:
-            c4_arm(args, local_rank)
+            chunk_arm(args, local_rank)
     elif args.config != "c2":
         if rank == 0:
             config_arm(args, local_rank)

@@ -287,7 +287,17 @@ class Fp8E4M3:
         g = w.reshape(-1, group)
         amax = _amax(g)
         s = np.where(amax > 0, amax / FP8_E4M3_MAX, _F32(1.0)).astype(_F32)
-        q = f32_to_e4m3((g / s[:, None]).astype(_F32))
+        scaled = (g / s[:, None]).astype(_F32)
+        # element-wise: blocks of groups on a thread pool (numpy releases the
+        # GIL), the same codes whatever the split
+        blocks = max(1, min(os.cpu_count() or 1, 16, g.shape[0] // 8192))
+        if blocks == 1:
+            q = f32_to_e4m3(scaled)
+        else:
+            from concurrent.futures import ThreadPoolExecutor
+            cuts = np.linspace(0, g.shape[0], blocks + 1).astype(int)
+            with ThreadPoolExecutor(blocks) as ex:
+                q = np.concatenate(list(ex.map(lambda i: f32_to_e4m3(scaled[cuts[i]:cuts[i + 1]]), range(blocks))))
         return Fp8E4M3(q.reshape(-1), s, rows, cols, group)
 
     def dequantize(self) -> np.ndarray:
