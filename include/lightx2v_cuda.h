@@ -1,6 +1,7 @@
 /*
- * lightx2v_cuda.h — C ABI of the B200 (sm_100a) backend for lightx2v-rs's
- * quantized linear path.
+ * lightx2v_cuda.h — C ABI of the B200 (sm_100a) backend for lightx2v-rs: the
+ * quantized linear path, and the other ops of the DiT chunk step around it
+ * (attention, KV cache / MemRoPE, norms, head_split, patchify, dmd_step).
  *
  * The entry points are what a `lightx2v-cuda` crate's `impl Backend for
  * CudaBackend` binds (crates/lightx2v-core/src/backend.rs:145-446). Each
@@ -213,6 +214,20 @@ LX2V_API lx2v_status lx2v_residual_norm(lx2v_ctx *ctx, lx2v_buf *h, const lx2v_b
 LX2V_API lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
                                      size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
                                      const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out);
+/* No counterpart in the reference (its head_split normalises across the
+ * heads it is given, all of them): for a tensor-parallel block that holds
+ * only some heads. lx2v_row_sumsq writes out[r] = sum of the squares of
+ * columns [col_off, col_off + width) of row r (f32 [rows]); the caller sums
+ * these over the ranks (lx2v_all_reduce_sum) and lx2v_head_split_rms then
+ * normalises by rsqrt(sumsq[r] / rms_dim + eps), rms_dim being the width of
+ * all heads together, so that every rank's heads are normalised exactly as
+ * head_split normalises the full row. */
+LX2V_API lx2v_status lx2v_row_sumsq(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                    size_t col_off, size_t width, lx2v_buf *out);
+LX2V_API lx2v_status lx2v_head_split_rms(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                         size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                         const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos,
+                                         const lx2v_buf *sin, float eps, lx2v_buf *out);
 /* Backend::patchify: latent [c, t, h, w] -> tokens [t*(h/p)*(w/p), c*p*p],
  * feature c*p^2 + kh*p + kw. */
 LX2V_API lx2v_status lx2v_patchify(lx2v_ctx *ctx, const lx2v_buf *latent, size_t c, size_t t, size_t h, size_t w,

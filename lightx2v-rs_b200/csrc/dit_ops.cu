@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(ROW_THREADS) head_split_kernel(HeadSplitArgs a
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < NP; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];  // zeros past the row add nothing
-        const float ms = block_sum(ss, red) / (float)d;
+        const float ms = a.sumsq ? a.sumsq[r] / (float)a.rms_dim : block_sum(ss, red) / (float)d;
         const float inv = 1.0f / sqrtf(ms + a.eps);
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(512) head_split_vec_kernel(HeadSplitArgs a) {
         float ss = 0.0f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
-        const float ms = block_sum_any(ss, red) / (float)d;
+        const float ms = a.sumsq ? a.sumsq[r] / (float)a.rms_dim : block_sum_any(ss, red) / (float)d;
         const float inv = 1.0f / sqrtf(ms + a.eps);
         float w[8];
         ld8(a.rms_w, a.w_f32, j0, w);
@@ -309,6 +309,20 @@ __global__ void __launch_bounds__(512) head_split_vec_kernel(HeadSplitArgs a) {
         for (int k = 0; k < 8; ++k) o[k] = x[k];
     }
     st8(a.out, a.out_f32, ((int64_t)h * a.rows + r) * a.head_dim + e, o);
+}
+
+// One row per CTA: the sum of squares of `width` values, f32.
+__global__ void __launch_bounds__(ROW_THREADS) row_sumsq_kernel(const void *src, int src_f32, int64_t stride,
+                                                                int64_t col_off, int width, float *out) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int64_t r = blockIdx.x;
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < width; j += ROW_THREADS) {
+        const float v = ld_v(src, src_f32, r * stride + col_off + j);
+        ss += v * v;
+    }
+    const float t = block_sum(ss, red);
+    if (threadIdx.x == 0) out[r] = t;
 }
 
 int grid_elems(int64_t n) {
@@ -356,6 +370,13 @@ cudaError_t head_split_launch(const HeadSplitArgs &a, cudaStream_t st) {
         return cudaGetLastError();
     }
     head_split_kernel<<<(unsigned)a.rows, ROW_THREADS, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t row_sumsq_launch(const void *src, int src_f32, int64_t rows, int64_t stride, int64_t col_off, int width,
+                             float *out, cudaStream_t st) {
+    if (rows == 0) return cudaSuccess;
+    row_sumsq_kernel<<<(unsigned)rows, ROW_THREADS, 0, st>>>(src, src_f32, stride, col_off, width, out);
     return cudaGetLastError();
 }
 

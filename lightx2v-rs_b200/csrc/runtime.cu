@@ -1681,11 +1681,53 @@ extern "C" lx2v_status lx2v_residual_norm(lx2v_ctx *ctx, lx2v_buf *h, const lx2v
     return LX2V_OK;
 }
 
+static lx2v_status head_split_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                   size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                   const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos, const lx2v_buf *sin,
+                                   float eps, lx2v_buf *out);
+
 extern "C" lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
                                        size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
                                        const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out) {
+    return head_split_impl(ctx, src, rows, src_stride, col_off, heads, head_dim, rms_w, nullptr, 0, cos, sin, eps,
+                           out);
+}
+
+extern "C" lx2v_status lx2v_head_split_rms(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                           size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                           const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos,
+                                           const lx2v_buf *sin, float eps, lx2v_buf *out) {
+    if (!rms_w || !sumsq || rms_dim == 0)
+        return fail(ctx, LX2V_ERR_INVALID, "head_split_rms needs the RMS weight, the row sums and their width");
+    return head_split_impl(ctx, src, rows, src_stride, col_off, heads, head_dim, rms_w, sumsq, rms_dim, cos, sin, eps,
+                           out);
+}
+
+extern "C" lx2v_status lx2v_row_sumsq(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                      size_t col_off, size_t width, lx2v_buf *out) {
     lx2v_status s = enter(ctx);
     if (s) return s;
+    if (!src || !out || out->dtype != LX2V_F32) return fail(ctx, LX2V_ERR_INVALID, "null src or non-f32 output");
+    if (col_off + width > src_stride || (rows && (rows - 1) * src_stride + col_off + width > src->len))
+        return fail(ctx, LX2V_ERR_INVALID, "row_sumsq columns beyond src");
+    if (rows > out->len) return fail(ctx, LX2V_ERR_INVALID, "row_sumsq output holds fewer than rows");
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "row_sumsq");
+    CUDA_TRY(ctx, row_sumsq_launch(src->ptr, is_f32(src), (int64_t)rows, (int64_t)src_stride, (int64_t)col_off,
+                                   (int)width, (float *)out->ptr, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {src, out}));
+    return LX2V_OK;
+}
+
+static lx2v_status head_split_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                   size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                   const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos, const lx2v_buf *sin,
+                                   float eps, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (sumsq && (sumsq->dtype != LX2V_F32 || sumsq->len < rows))
+        return fail(ctx, LX2V_ERR_INVALID, "row sums of squares must be f32, one per row");
     const size_t d = heads * head_dim;
     if (!src || !out || head_dim == 0 || head_dim % 2) return fail(ctx, LX2V_ERR_INVALID, "null src/out or odd head_dim");
     if (col_off + d > src_stride || (rows && (rows - 1) * src_stride + col_off + d > src->len))
@@ -1705,12 +1747,13 @@ extern "C" lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_
     a.rows = (int64_t)rows; a.src_stride = (int64_t)src_stride; a.col_off = (int64_t)col_off;
     a.heads = (int)heads; a.head_dim = (int)head_dim;
     a.rms_w = rms_w ? rms_w->ptr : nullptr; a.w_f32 = is_f32(rms_w);
+    a.sumsq = sumsq ? (const float *)sumsq->ptr : nullptr; a.rms_dim = (int)rms_dim;
     a.cos = cos ? cos->ptr : nullptr; a.sin = sin ? sin->ptr : nullptr; a.cs_f32 = is_f32(cos);
     a.eps = eps;
     a.out = out->ptr; a.out_f32 = is_f32(out);
     CUDA_TRY(ctx, head_split_launch(a, ctx->stream));
     ctx->launches++;
-    CUDA_TRY(ctx, note_uses(ctx, {src, rms_w, cos, sin, out}));
+    CUDA_TRY(ctx, note_uses(ctx, {src, rms_w, sumsq, cos, sin, out}));
     return LX2V_OK;
 }
 

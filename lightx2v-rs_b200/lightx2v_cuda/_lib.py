@@ -71,6 +71,9 @@ SIGNATURES = {
     "lx2v_residual_norm": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_long, ctypes.c_int, _vp, _vp, _sz, _sz,
                                  ctypes.c_float, _vp]),
     "lx2v_head_split": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp, _vp, ctypes.c_float, _vp]),
+    "lx2v_row_sumsq": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _vp]),
+    "lx2v_head_split_rms": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp, _sz, _vp, _vp, ctypes.c_float,
+                                  _vp]),
     "lx2v_patchify": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp]),
     "lx2v_unpatchify": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp]),
     "lx2v_dmd_step": (_st, [_vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _sz]),

@@ -329,6 +329,18 @@ class CudaBackend:
                                               rms_w.handle if rms_w is not None else None, cos, sin, eps,
                                               out.handle))
 
+    def row_sumsq(self, src: Buf, rows: int, src_stride: int, col_off: int, width: int, out: Buf):
+        """out[r] = sum of squares of columns [col_off, col_off + width) of row r (f32)."""
+        self._check(self._lib.lx2v_row_sumsq(self._ctx, src.handle, rows, src_stride, col_off, width, out.handle))
+
+    def head_split_rms(self, src: Buf, rows: int, src_stride: int, col_off: int, heads: int, head_dim: int,
+                       rms_w: Buf, sumsq: Buf, rms_dim: int, rope, eps: float, out: Buf):
+        """head_split with the RMS statistic given (rows' sums of squares over
+        rms_dim values, summed across tensor-parallel ranks)."""
+        cos, sin = (rope[0].handle, rope[1].handle) if rope is not None else (None, None)
+        self._check(self._lib.lx2v_head_split_rms(self._ctx, src.handle, rows, src_stride, col_off, heads, head_dim,
+                                                  rms_w.handle, sumsq.handle, rms_dim, cos, sin, eps, out.handle))
+
     def patchify(self, latent: Buf, c: int, t: int, h: int, w: int, p: int, out: Buf):
         self._check(self._lib.lx2v_patchify(self._ctx, latent.handle, c, t, h, w, p, out.handle))
 
