@@ -114,3 +114,193 @@ class TensorParallelFFN:
         if self.world > 1:
             self.be.all_reduce_sum(part, rows * self.dim)
         self.be.gate_residual(h, part, rows, self.dim, mods, gate)
+
+
+# ---- the DiT block tensor-parallel over heads and FFN features ----------------------------------
+def _rows(w, r0: int, r1: int, cols: int):
+    """Rows [r0, r1) of a quantized struct or of a flat f32 [rows * cols] array."""
+    if isinstance(w, (Q8, Q4, Fp8E4M3)):
+        return slice_rows(w, r0, r1)
+    return np.ascontiguousarray(np.asarray(w, np.float32).reshape(-1, cols)[r0:r1]).reshape(-1)
+
+
+def _cols(w, k0: int, k1: int, cols: int):
+    """Columns [k0, k1) of a quantized struct (group boundaries) or of an f32 array."""
+    if isinstance(w, (Q8, Q4, Fp8E4M3)):
+        return slice_cols(w, k0, k1)
+    return np.ascontiguousarray(np.asarray(w, np.float32).reshape(-1, cols)[:, k0:k1]).reshape(-1)
+
+
+def _stack(parts):
+    """Rows of several matrices stacked (the fused QKV / KV layout, dit.rs:106-149)."""
+    a = parts[0]
+    if isinstance(a, (Q8, Q4, Fp8E4M3)):
+        return type(a).concat(parts)
+    return np.concatenate([np.asarray(p, np.float32).reshape(-1) for p in parts])
+
+
+def head_split_points(heads: int, world: int) -> list[int]:
+    """Heads per rank, earlier ranks taking the extra ones (12 heads on 8 GPUs:
+    2, 2, 2, 2, 1, 1, 1, 1)."""
+    return split_points(heads, world, 1)
+
+
+def shard_block(block: dict, dim: int, head_dim: int, h0: int, h1: int):
+    """This rank's attention weights of one block (host side): the fused QKV
+    and the cross-attention KV keep only the rows of heads [h0, h1) of each
+    of their parts, q2 likewise; out1 / out2 keep the matching input columns
+    (their partial products are summed over the ranks); the q/k RMS weights
+    keep those heads' channels. FFN and norm2 are handled elsewhere."""
+    c0, c1 = h0 * head_dim, h1 * head_dim
+    wq, bq = block["qkv"]
+    wkv, bkv = block["kv2"]
+    bq, bkv = np.asarray(bq, np.float32), np.asarray(bkv, np.float32)
+    sel = lambda v: np.asarray(v, np.float32)[c0:c1]
+    return {
+        "qkv": (_stack([_rows(wq, p * dim + c0, p * dim + c1, dim) for p in range(3)]),
+                np.concatenate([bq[p * dim + c0:p * dim + c1] for p in range(3)])),
+        "norm_q1": sel(block["norm_q1"]), "norm_k1": sel(block["norm_k1"]),
+        "out1": (_cols(block["out1"][0], c0, c1, dim), np.asarray(block["out1"][1], np.float32)),
+        "q2": (_rows(block["q2"][0], c0, c1, dim), sel(block["q2"][1])),
+        "kv2": (_stack([_rows(wkv, p * dim + c0, p * dim + c1, dim) for p in range(2)]),
+                np.concatenate([bkv[p * dim + c0:p * dim + c1] for p in range(2)])),
+        "norm_q2": sel(block["norm_q2"]), "norm_k2": sel(block["norm_k2"]),
+        "out2": (_cols(block["out2"][0], c0, c1, dim), np.asarray(block["out2"][1], np.float32)),
+    }
+
+
+class TensorParallelDit:
+    """LightDit's chunk step (crates/lightx2v-model/src/dit.rs:440-782) with each
+    block tensor-parallel over the group, one process per GPU:
+
+      attention  rank r owns heads [h_r, h_{r+1}): the fused QKV keeps those
+                 heads' rows, so q, k, v, the KV cache and the attention are
+                 local; the q/k RMS norm spans all heads (cpu lib.rs:433-438),
+                 so each rank's per-row sum of squares over its heads is
+                 all-reduced (f32, one value per row) before head_split
+                 normalises; out1 is split by its input columns and its
+                 partial products are all-reduced (bias added once);
+      cross-attn q2 and the prompt's K/V the same way (the prompt K RMS too);
+                 out2 split and all-reduced like out1;
+      FFN        TensorParallelFFN (features split, FFN2 partials all-reduced);
+      the rest   patch embed, the norms, the residual stream h and the output
+                 head are replicated, so every rank ends a step with the same h.
+
+    `blocks` etc. are the host weights of lightx2v_cuda.dit.LightDitCuda; every
+    rank holds the same host copy and uploads only its shard."""
+
+    def __init__(self, be, rank: int, world: int, cfg, blocks, patch, text1, text2, proj_out, memrope=None,
+                 partial_dtype: int = L.BF16):
+        from .dit import Block, Linear, MemRopeConfig, upload_weight as up
+        self.be, self.rank, self.world, self.cfg = be, rank, world, cfg
+        self.memrope = memrope or MemRopeConfig()
+        self.partial_dtype = partial_dtype
+        d, hd = cfg.dim, cfg.head_dim
+        pts = head_split_points(cfg.heads, world)
+        self.h0, self.h1 = pts[rank], pts[rank + 1]
+        self.nl = self.h1 - self.h0
+        self.dl = self.nl * hd
+        dl = self.dl
+
+        def lin(p, rows, cols, bias=True):
+            b = be.upload(np.asarray(p[1], np.float32), L.F32) if bias else None
+            return Linear(up(be, p[0], rows, cols), b)
+
+        def vec(a):
+            return be.upload(np.asarray(a, np.float32), L.F32)
+
+        self.patch = lin(patch, d, cfg.patch_in)
+        self.text1 = lin(text1, d, cfg.text_dim)
+        self.text2 = lin(text2, d, d)
+        self.proj_out = lin(proj_out, cfg.patch_out, d)
+        self.blocks, self.ffns = [], []
+        for b in blocks:
+            sh = shard_block(b, d, hd, self.h0, self.h1)
+            self.blocks.append(Block(
+                qkv=lin(sh["qkv"], 3 * dl, d), norm_q1=vec(sh["norm_q1"]), norm_k1=vec(sh["norm_k1"]),
+                out1=lin(sh["out1"], d, dl, bias=rank == 0), q2=lin(sh["q2"], dl, d), kv2=lin(sh["kv2"], 2 * dl, d),
+                norm_q2=vec(sh["norm_q2"]), norm_k2=vec(sh["norm_k2"]), out2=lin(sh["out2"], d, dl, bias=rank == 0),
+                norm2_w=vec(b["norm2_w"]), norm2_b=vec(b["norm2_b"]), ffn1=None, ffn2=None))
+            self.ffns.append(TensorParallelFFN(be, rank, world, b["ffn1"][0], b["ffn1"][1], b["ffn2"][0],
+                                               b["ffn2"][1], partial_dtype=partial_dtype))
+
+    def _reduce(self, buf, n):
+        if self.world > 1:
+            self.be.all_reduce_sum(buf, n)
+
+    def prepare_prompt(self, embeds):
+        be, c = self.be, self.cfg
+        n, d, dl = c.text_len, c.dim, self.dl
+        x = be.upload(np.asarray(embeds, np.float32))
+        mid, ctx = be.alloc(n * d), be.alloc(n * d)
+        be.linear(x, 0, n, self.text1.w, self.text1.b, L.ACT_GELU_TANH, mid, 0)
+        be.linear(mid, 0, n, self.text2.w, self.text2.b, L.ACT_NONE, ctx, 0)
+        kv, ss = be.alloc(n * 2 * dl), be.alloc(n, L.F32)
+        out = []
+        for b in self.blocks:
+            be.linear(ctx, 0, n, b.kv2.w, b.kv2.b, L.ACT_NONE, kv, 0)
+            k, v = be.alloc(n * dl), be.alloc(n * dl)
+            be.row_sumsq(kv, n, 2 * dl, 0, dl, ss)
+            self._reduce(ss, n)
+            be.head_split_rms(kv, n, 2 * dl, 0, self.nl, c.head_dim, b.norm_k2, ss, d, None, c.eps, k)
+            be.head_split(kv, n, 2 * dl, dl, self.nl, c.head_dim, None, None, c.eps, v)
+            out.append((k, v))
+        return out
+
+    def workspace(self, chunk_frames: int, frame_tokens: int, rope_cos, rope_sin):
+        from types import SimpleNamespace
+        be, c = self.be, self.cfg
+        s, d, dl = chunk_frames * frame_tokens, c.dim, self.dl
+        cap = self.memrope.cache_frames * frame_tokens
+        return SimpleNamespace(
+            tokens=s, frame_tokens=frame_tokens,
+            caches=[be.kv_cache_new(self.nl, c.head_dim, cap) for _ in self.blocks],
+            h=be.alloc(s * d, L.F32), normed=be.alloc(s * d), qkv=be.alloc(s * 3 * dl), q=be.alloc(s * dl),
+            k=be.alloc(s * dl), v=be.alloc(s * dl), attn=be.alloc(s * dl), q2=be.alloc(s * dl),
+            part=be.alloc(s * d, self.partial_dtype), ss_q=be.alloc(s, L.F32), ss_k=be.alloc(s, L.F32),
+            patches=be.alloc(s * max(c.patch_in, c.patch_out)),
+            rope_cos=be.upload(np.asarray(rope_cos, np.float32), L.F32),
+            rope_sin=be.upload(np.asarray(rope_sin, np.float32), L.F32))
+
+    def patch_embed(self, ws, latent, c: int, t: int, h: int, w: int):
+        be = self.be
+        be.patchify(latent, c, t, h, w, self.cfg.patch, ws.patches)
+        be.linear(ws.patches, 0, ws.tokens, self.patch.w, self.patch.b, L.ACT_NONE, ws.h, 0)
+
+    def forward_chunk(self, ws, mods, head_mods, prompt, start_frame: int, out):
+        """dit.rs:569-782 on this rank's shard; h and out end replicated."""
+        from .dit import GATE_FFN, GATE_MSA, SCALE_FFN, SCALE_MSA, SHIFT_FFN, SHIFT_MSA
+        be, c = self.be, self.cfg
+        s, d, hd, nl, dl, eps = ws.tokens, c.dim, c.head_dim, self.nl, self.dl, c.eps
+        rope = (ws.rope_cos, ws.rope_sin)
+        token_temporal = start_frame + np.arange(s) // ws.frame_tokens
+        tq = token_temporal.astype(np.int32)
+        for li, (bl, m) in enumerate(zip(self.blocks, mods)):
+            be.layer_norm(ws.h, s, d, ("mod", SCALE_MSA, SHIFT_MSA), m, eps, ws.normed)
+            be.linear(ws.normed, 0, s, bl.qkv.w, bl.qkv.b, L.ACT_NONE, ws.qkv, 0)
+            be.row_sumsq(ws.qkv, s, 3 * dl, 0, dl, ws.ss_q)
+            be.row_sumsq(ws.qkv, s, 3 * dl, dl, dl, ws.ss_k)
+            self._reduce(ws.ss_q, s)
+            self._reduce(ws.ss_k, s)
+            be.head_split_rms(ws.qkv, s, 3 * dl, 0, nl, hd, bl.norm_q1, ws.ss_q, d, rope, eps, ws.q)
+            be.head_split_rms(ws.qkv, s, 3 * dl, dl, nl, hd, bl.norm_k1, ws.ss_k, d, rope, eps, ws.k)
+            be.head_split(ws.qkv, s, 3 * dl, 2 * dl, nl, hd, None, None, eps, ws.v)
+            cache = ws.caches[li]
+            be.kv_cache_put(cache, ws.k, ws.v, s, token_temporal)
+            be.kv_cache_memrope_update(cache, self.memrope, ws.frame_tokens)
+            be.kv_cache_attention(ws.q, s, tq, cache, ws.attn)
+            be.linear(ws.attn, 0, s, bl.out1.w, bl.out1.b, L.ACT_NONE, ws.part, 0)
+            self._reduce(ws.part, s * d)
+            be.residual_norm(ws.h, ws.part, s, d, m, GATE_MSA, ("affine", bl.norm2_w, bl.norm2_b), eps, ws.normed)
+            k2, v2 = prompt[li]
+            be.linear(ws.normed, 0, s, bl.q2.w, bl.q2.b, L.ACT_NONE, ws.q2, 0)
+            be.row_sumsq(ws.q2, s, dl, 0, dl, ws.ss_q)
+            self._reduce(ws.ss_q, s)
+            be.head_split_rms(ws.q2, s, dl, 0, nl, hd, bl.norm_q2, ws.ss_q, d, None, eps, ws.q)
+            be.attention(ws.q, k2, v2, nl, s, c.text_len, hd, ws.attn)
+            be.linear(ws.attn, 0, s, bl.out2.w, bl.out2.b, L.ACT_NONE, ws.part, 0)
+            self._reduce(ws.part, s * d)
+            be.residual_norm(ws.h, ws.part, s, d, m, None, ("mod", SCALE_FFN, SHIFT_FFN), eps, ws.normed)
+            self.ffns[li].forward(ws.normed, s, ws.h, m, GATE_FFN)
+        be.layer_norm(ws.h, s, d, ("mod", 1, 0), head_mods, eps, ws.normed)
+        be.linear(ws.normed, 0, s, self.proj_out.w, self.proj_out.b, L.ACT_NONE, out, 0)

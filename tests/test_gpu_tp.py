@@ -106,3 +106,83 @@ def test_tensor_parallel_ffn_on_two_gpus_matches_one_gpu():
         assert np.array_equal(np.isnan(got0[dt]), ~fin)
         upd, want = (got0[dt] - h)[fin], (ref - h)[fin]
         assert np.linalg.norm(upd - want) / np.linalg.norm(want) <= tol, dt
+
+
+# ---- the whole DiT chunk step tensor-parallel over two GPUs ----------------------------------
+def _dit_rank_main(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "lightx2v-rs_b200"))
+    import torch.distributed as dist
+    from lightx2v_cuda import F32, CudaBackend, quant, rng
+    from lightx2v_cuda.dit import LightDitCuda, WanConfig, synthetic_block
+    from lightx2v_cuda.tp import TensorParallelDit
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)  # id exchange only
+    try:
+        be = CudaBackend(rank)
+        uid = [be.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.comm_init(uid[0], rank, world)
+        cfg = WanConfig(layers=2)
+        d = cfg.dim
+        q8 = lambda w, r, c: quant.Q8.quantize(w, r, c)
+        blocks = [synthetic_block(cfg, 10 + l, q8) for l in range(cfg.layers)]
+        mat = lambda seed, r, c: (rng.normal(seed, r * c, 0.02), rng.normal(seed + 1, r, 0.01))
+        args = (cfg, blocks, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim), mat(905, d, d),
+                mat(907, cfg.patch_out, d))
+        ft, frames = 64, 3
+        s = ft * frames
+        ang = rng.normal(931, s * cfg.head_dim // 2, 1.0)
+        cos, sin = np.cos(ang), np.sin(ang)
+        embeds = rng.normal(911, cfg.text_len * cfg.text_dim)
+        mods = [be.upload(rng.normal(920 + l, 6 * d, 0.1), F32) for l in range(cfg.layers)]
+        head = be.upload(rng.normal(930, 2 * d, 0.1), F32)
+        models = [TensorParallelDit(be, rank, world, *args)]
+        if rank == 0:
+            models.append(LightDitCuda(be, *args))  # the unsplit model on one GPU
+        results = []
+        for mdl in models:
+            prompt = mdl.prepare_prompt(embeds)
+            ws = mdl.workspace(frames, ft, cos, sin)
+            out = be.alloc(s * cfg.patch_out, F32)
+            outs = []
+            for chunk in range(4):
+                be.write(ws.h, rng.normal(940 + chunk, s * d))
+                mdl.forward_chunk(ws, mods, head, prompt, 3 * chunk, out)
+                outs.append((be.download(out), be.download(ws.h)))
+            results.append(outs)
+        q.put((rank, results))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_tensor_parallel_dit_chunk_steps_match_one_gpu():
+    # heads split 6 + 6, the q/k RMS sums of squares and the out1 / out2 /
+    # FFN2 partials all-reduced (bf16 partials); four chunks through the
+    # MemRoPE caches; rank 0's output and residual stream against the unsplit
+    # model on one GPU, and h identical on both ranks
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dit_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, results = q.get(timeout=600)
+        res[r] = results
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    tp0, one = res[0][0], res[0][1]
+    tp1 = res[1][0]
+    for chunk in range(4):
+        assert np.array_equal(tp0[chunk][1], tp1[chunk][1])  # h replicated
+        for got, want in zip(tp0[chunk], one[chunk]):
+            assert np.isfinite(got).all()
+            assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-2, chunk

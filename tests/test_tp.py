@@ -116,3 +116,54 @@ def test_split_ffn_over_two_gloo_ranks_equals_the_full_ffn(oracle):
     assert np.array_equal(outs[0], outs[1])  # h stays replicated
     upd, ref = outs[0] - h, want - h
     assert np.linalg.norm(upd - ref) / np.linalg.norm(ref) <= 1e-5
+
+
+# ---- the DiT block tensor-parallel over heads ------------------------------------------------
+def test_heads_split_unevenly_earlier_ranks_first():
+    assert np.diff(tp.head_split_points(12, 8)).tolist() == [2, 2, 2, 2, 1, 1, 1, 1]
+    assert tp.head_split_points(24, 8) == list(range(0, 25, 3))
+    assert tp.head_split_points(12, 1) == [0, 12]
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("kind", ["native", "q8"])
+def test_attention_shards_reassemble_the_block(oracle, kind, world):
+    # per rank: the fused QKV / KV keep their heads' rows of every part, out1
+    # / out2 their heads' input columns; across the ranks the shards hold
+    # every row and column once, and the ranks' partial out1 products sum to
+    # the full one
+    heads, hd = 12, 128  # out1 / out2 column shards stay on Q8's 128-wide groups
+    d = heads * hd
+    def mat(seed, r, c):
+        w = oracle.normal(seed, r * c, 0.02)
+        return (quant.Q8.quantize(w, r, c) if kind == "q8" else w), oracle.normal(seed + 1, r, 0.01)
+    deq = lambda w: w.dequantize() if kind == "q8" else np.asarray(w, np.float32)
+    block = {"qkv": mat(1, 3 * d, d), "kv2": mat(3, 2 * d, d), "q2": mat(5, d, d), "out1": mat(7, d, d),
+             "out2": mat(9, d, d), "norm_q1": oracle.normal(11, d), "norm_k1": oracle.normal(12, d),
+             "norm_q2": oracle.normal(13, d), "norm_k2": oracle.normal(14, d)}
+    pts = tp.head_split_points(heads, world)
+    shards = [tp.shard_block(block, d, hd, pts[r], pts[r + 1]) for r in range(world)]
+    full_qkv = deq(block["qkv"][0]).reshape(3, heads, hd, d)
+    got_qkv = np.concatenate([deq(sh["qkv"][0]).reshape(3, -1, hd, d) for sh in shards], axis=1)
+    assert np.array_equal(got_qkv, full_qkv)
+    full_b = np.asarray(block["qkv"][1]).reshape(3, heads, hd)
+    assert np.array_equal(np.concatenate([sh["qkv"][1].reshape(3, -1, hd) for sh in shards], axis=1), full_b)
+    assert np.array_equal(np.concatenate([deq(sh["kv2"][0]).reshape(2, -1, hd, d) for sh in shards], axis=1),
+                          deq(block["kv2"][0]).reshape(2, heads, hd, d))
+    assert np.array_equal(np.concatenate([sh["norm_k1"] for sh in shards]), block["norm_k1"])
+    w1 = deq(block["out1"][0]).reshape(d, d)
+    assert np.array_equal(np.concatenate([deq(sh["out1"][0]).reshape(d, -1) for sh in shards], axis=1), w1)
+    a = oracle.normal(20, 5 * d).reshape(5, d).astype(np.float64)
+    parts = sum(a[:, pts[r] * hd:pts[r + 1] * hd] @ deq(shards[r]["out1"][0]).reshape(d, -1).T.astype(np.float64)
+                for r in range(world))
+    assert np.allclose(parts, a @ w1.T.astype(np.float64), rtol=1e-10, atol=1e-12)
+
+
+def test_row_sumsq_over_head_shards_is_the_row_sumsq(oracle):
+    # the cross-head RMS under head sharding: per-rank sums of squares over
+    # their heads' columns, summed, equal the full row's (cpu lib.rs:433-438)
+    heads, hd, world = 12, 128, 8
+    pts = tp.head_split_points(heads, world)
+    x = oracle.normal(30, 7 * heads * hd).reshape(7, -1).astype(np.float64)
+    parts = sum((x[:, pts[r] * hd:pts[r + 1] * hd] ** 2).sum(1) for r in range(world))
+    assert np.allclose(parts, (x ** 2).sum(1), rtol=1e-12)
