@@ -445,7 +445,20 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     total_ms, weak_ms, e2e_ms, gemm_ms = max_over_ranks([total_ms, weak_ms, e2e_ms, gemm_ms])
 
     # --- the chunk's FFN tensor-parallel over the ranks ----------------------------------
+    if world > 1:
+        uid = [be.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.comm_init(uid[0], rank, world)
     tp = tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barrier)
+
+    # --- the whole 1.3B chunk step (C4), tensor-parallel on several GPUs -------------------
+    chunk = None
+    if not args.no_chunk:
+        barrier()
+        chunk = chunk_step_measure(args, be, ext, flush, "c4", "fp8", 30, rank, world,
+                                   max_over_ranks if world > 1 else None)
+        chunk.pop("_profile", None)
+        barrier()
 
     flops_step = step_flops(M)
     value = flops_step * args.steps / (total_ms * 1e-3) / 1e12
@@ -495,6 +508,7 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
                                    "time, on a whole 4680-token chunk",
                          "per_linear": per_kernel},
             "tp_ffn": tp,
+            "chunk_step": chunk,
             "configs": configs,
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
@@ -518,10 +532,6 @@ def tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barr
     h update against it."""
     from lightx2v_cuda import BF16, F32, Act, quant, rng
     from lightx2v_cuda.tp import TensorParallelFFN
-    if world > 1:
-        uid = [be.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        be.comm_init(uid[0], rank, world)
     m = M_TOKENS
     # Q8: the kernels' work per element is the FP8 set's apart from the decode
     # pass, and the reference's FP8 quantizer's NaN codes would make every
@@ -739,7 +749,8 @@ CHUNK_PRESETS = {
 }
 
 
-def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8", layers: int = 30):
+def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8", layers: int = 30,
+                       rank: int = 0, world: int = 1, max_over_ranks=None):
     """BASELINE configs C4 / C5: one denoising step of a 3-latent-frame chunk
     through all blocks and the output head, at start frame 12 with each
     layer's MemRoPE cache holding 12 frames after its update. Weights: one
@@ -749,9 +760,12 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     at start frames 0, 3, 6 and 9 first; every timed step re-runs the chunk
     at frame 12 (the next DMD step of the same chunk overwrites its own
     cache rows). ms per step from CUDA events on the library's stream, L2
-    flushed before each."""
+    flushed before each. With world > 1 every block runs tensor-parallel
+    over the ranks (lightx2v_cuda/tp.py TensorParallelDit; the backend has
+    joined the group) and the time is the max over ranks."""
     from lightx2v_cuda import F32, quant, rng
     from lightx2v_cuda.dit import LightDitCuda, WanConfig, synthetic_block
+    from lightx2v_cuda.tp import TensorParallelDit
     fields, (lh, lw) = CHUNK_PRESETS[preset]
     cfg = WanConfig(layers=layers, **fields)
     d = cfg.dim
@@ -760,8 +774,9 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     t0 = time.perf_counter()
     block = synthetic_block(cfg, 3, qz)
     mat = lambda seed, r, c: (rng.normal(seed, r * c, 0.02), rng.normal(seed + 1, r, 0.01))
-    model = LightDitCuda(be, cfg, [block] * layers, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim),
-                         mat(905, d, d), mat(907, cfg.patch_out, d))
+    wargs = (cfg, [block] * layers, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim), mat(905, d, d),
+             mat(907, cfg.patch_out, d))
+    model = LightDitCuda(be, *wargs) if world == 1 else TensorParallelDit(be, rank, world, *wargs)
     prompt = model.prepare_prompt(rng.normal(911, cfg.text_len * cfg.text_dim))
     ft, frames = (lh // cfg.patch) * (lw // cfg.patch), 3
     s = ft * frames
@@ -784,6 +799,8 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     be.sync()
     n = max(3, min(args.steps, 10))
     ms = float(np.median(timed_steps(be, ext, flush, lambda: step(12), n)))
+    if max_over_ranks is not None:
+        (ms,) = max_over_ranks([ms])
     prof = None
     if getattr(args, "profile", False):
         # per-op device time of one more step (the context records events
@@ -803,7 +820,9 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     visible = int(sum(int(np.sum(tk <= t)) for t in (12, 13, 14)) * ft)
     att = 4.0 * cfg.head_dim * cfg.heads * (visible + s * cfg.text_len)
     flops = layers * (blk + att) + ends
-    return {"workload": f"{preset}: {layers} blocks (dim {d}, {cfg.heads} x {cfg.head_dim} heads, FFN {cfg.ffn_dim}) + "
+    return {"n_gpus": world, "parallelism": ("one GPU" if world == 1 else
+                                             f"tp{world}: heads and FFN features split, all-reduces over NVLink"),
+            "workload": f"{preset}: {layers} blocks (dim {d}, {cfg.heads} x {cfg.head_dim} heads, FFN {cfg.ffn_dim}) + "
                         f"patch embed + head, {s} tokens ({frames} frames x {ft}), start frame 12, {fmt} block "
                         f"weights, 12-frame MemRoPE cache", "ms_per_step": ms,
             "tflops": flops / (ms * 1e-3) / 1e12, "flop_per_step": flops, "cache_keys": sk,
@@ -837,6 +856,7 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-chunk", action="store_true", help="skip the C4 chunk step in the default line")
     ap.add_argument("--m", type=int, nargs="*", default=None,
                     help="with --config c3: only these token counts of the sweep")
     ap.add_argument("--chunk-format", default="fp8", choices=["fp8", "q8"],
