@@ -84,7 +84,7 @@ def test_tensor_parallel_ffn_on_two_gpus_matches_one_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -169,12 +169,12 @@ def test_tensor_parallel_dit_chunk_steps_match_one_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_dit_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_dit_rank_main, args=(r, 2, port, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
     for _ in range(2):
-        r, results = q.get(timeout=600)
+        r, results = q.get(timeout=400)
         res[r] = results
     for p in procs:
         p.join(timeout=120)
