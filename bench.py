@@ -309,14 +309,18 @@ class LinearSet:
             self.linear(name)
 
 
-def timed_steps(be, ext, flush, fn, steps):
+def timed_steps(be, ext, flush, fn, steps, cushion=1):
     """CUDA-event time (ms) of each of `steps` calls of fn on the library's
-    stream, L2 flushed (256 MB write) before each, outside the event pair."""
+    stream, L2 flushed (256 MB write) before each, outside the event pair.
+    `cushion` > 1 repeats the flush so that the GPU is still busy with it when
+    the host has queued the call: for calls of a few microseconds the event
+    pair then brackets the kernel, not the host's submission time."""
     import torch
     pairs = []
     for _ in range(steps):
         with torch.cuda.stream(ext):
-            flush.zero_()
+            for _ in range(cushion):
+                flush.zero_()
         a, b = ev(), ev()
         a.record(ext)
         fn()
@@ -620,7 +624,8 @@ def measure_configs(be, ext, flush, args, peak, hbm, src, which=("c1", "c3")):
             be.linear(xb, 0, m, dw, bb, 0, yb, 0)
         be.sync()
         steps = args.steps if m < 4680 else max(3, args.steps // 2)
-        ms = float(np.median(timed_steps(be, ext, flush, lambda: be.linear(xb, 0, m, dw, bb, 0, yb, 0), steps)))
+        ms = float(np.median(timed_steps(be, ext, flush, lambda: be.linear(xb, 0, m, dw, bb, 0, yb, 0), steps,
+                                         cushion=4 if m <= 16 else 1)))
         flops = 2.0 * m * n * k
         nbytes = wbytes + m * k * 2 + m * n * (4 if y_f32 else 2) + n * 4
         tflops = flops / (ms * 1e-3) / 1e12
@@ -628,7 +633,8 @@ def measure_configs(be, ext, flush, args, peak, hbm, src, which=("c1", "c3")):
         small = m <= 16
         entry = {"workload": f"{fmt} linear M={m} K={k} N={n}", "weights": wdesc, "ms": ms, "tflops": tflops,
                  "gbs": gbs, "steps": steps,
-                 "path": "few-token kernel (gemv_kernel)" if small else
+                 "path": ("few-token Q4 kernel (gemv_q4_kernel: codes exact in mma.sync, group affine after)"
+                          if fmt == "q4" else "few-token kernel (gemv_kernel)") if small else
                  ("two-pass (dequant_bf16_kernel + gemm_ss_pair_kernel)" if m >= 1024 else "tensor-core"),
                  "roofline": {"bound": "hbm" if small else "tensor", "achieved": gbs if small else tflops,
                               "peak": hbm if small else peak, "unit": "GB/s" if small else "TFLOP/s",

@@ -82,6 +82,8 @@ struct LinearArgs {
     const void *bias; int bias_f32;
     const void *gate; int gate_f32;   // non-null: y += gate * act(...)
     int act;
+    int *err;                 // error word for bounded waits (gemv_q4.cu), may be null
+    uint64_t wait_limit_ns;
 };
 cudaError_t linear_simt_launch(const LinearArgs &a, cudaStream_t st);
 // Few-token (M <= 16) bandwidth-bound kernel (gemv.cu). Split-K partials go
@@ -92,6 +94,12 @@ bool gemv_supported(const LinearArgs &a);
 size_t gemv_workspace_floats(int N, int K, int num_sms);
 cudaError_t linear_gemv_launch(const LinearArgs &a, int num_sms, cudaStream_t st, float *partials, int *arrivals,
                                size_t ws_floats);
+// Few-token Q4 kernel with the group affine applied after the products
+// (gemv_q4.cu): K and the group multiples of 64; no workspace (partials meet
+// in the cluster's shared memory). linear_gemv_launch takes it for Q4 when
+// gemv_q4_supported.
+bool gemv_q4_supported(const LinearArgs &a, int num_sms);
+cudaError_t gemv_q4_launch(const LinearArgs &a, int num_sms, cudaStream_t st);
 
 // Elementwise helpers (kernels.cu).
 cudaError_t convert_launch(const void *src, int src_f32, void *dst, int dst_f32, size_t n,

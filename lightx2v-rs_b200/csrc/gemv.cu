@@ -276,7 +276,9 @@ cudaError_t gemv_launch_t(const LinearArgs &a, int num_sms, float *partials, int
 bool gemv_supported(const LinearArgs &a) {
     if (a.M < 1 || a.M > 16 || a.N < 1) return false;
     switch (a.fmt) {
-        case FMT_Q4: return a.K % GvFmt<FMT_Q4>::KC == 0 && a.group % 32 == 0;
+        case FMT_Q4:  // this kernel, or gemv_q4.cu's for groups of 64k
+            return (a.K % GvFmt<FMT_Q4>::KC == 0 && a.group % 32 == 0) ||
+                   (a.K % 64 == 0 && a.group % 64 == 0 && a.K % a.group == 0 && a.K <= 49152);
         case FMT_Q8:
         case FMT_FP8: return a.K % 64 == 0 && a.group % 16 == 0;
         default: return a.K % 64 == 0;
@@ -299,7 +301,9 @@ cudaError_t linear_gemv_launch(const LinearArgs &a, int num_sms, cudaStream_t st
                                size_t ws_floats) {
     switch (a.fmt) {
         case FMT_Q8: return gemv_launch_t<FMT_Q8>(a, num_sms, partials, arrivals, ws_floats, st);
-        case FMT_Q4: return gemv_launch_t<FMT_Q4>(a, num_sms, partials, arrivals, ws_floats, st);
+        case FMT_Q4:
+            if (gemv_q4_supported(a, num_sms)) return gemv_q4_launch(a, num_sms, st);
+            return gemv_launch_t<FMT_Q4>(a, num_sms, partials, arrivals, ws_floats, st);
         case FMT_FP8: return gemv_launch_t<FMT_FP8>(a, num_sms, partials, arrivals, ws_floats, st);
         default: return gemv_launch_t<FMT_BF16>(a, num_sms, partials, arrivals, ws_floats, st);
     }

@@ -887,6 +887,8 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
     a.bias = bias ? bias->ptr : nullptr; a.bias_f32 = bias && bias->dtype == LX2V_F32;
     a.gate = gate_ptr; a.gate_f32 = mods && mods->dtype == LX2V_F32;
     a.act = act;
+    a.err = ctx->err_dev;
+    a.wait_limit_ns = ctx->wait_limit_ns;
     const bool gemv_ok = gemv_supported(a);
     // Two-pass linear (decode once, then both GEMM operands from shared
     // memory): any group size the unit decode takes.
@@ -909,7 +911,7 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
     if (path == 2) {
         if (!gemv_ok)
             return fail(ctx, LX2V_ERR_UNSUPPORTED,
-                        "the few-token kernel takes 1..16 rows, K a multiple of 64 (Q4: 128) and Q4 groups of 32+");
+                        "the few-token kernel takes 1..16 rows, K a multiple of 64 (Q4: 128, or 64 with groups of 64k)");
         lx2v_status s = ensure_gemv_workspace(ctx, (int)N, (int)K);
         if (s) return s;
         CUDA_TRY(ctx, linear_gemv_launch(a, ctx->num_sms, ctx->stream, ctx->gemv_ws, ctx->gemv_arrivals,
