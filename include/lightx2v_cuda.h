@@ -345,9 +345,11 @@ LX2V_API lx2v_status lx2v_set_linear_path(lx2v_ctx *ctx, int path);
 /* Token tile of the tensor-core kernel: 0 = automatic, else 128, 192 or 256
  * tokens per tile (each tile is 128 output features wide). */
 LX2V_API lx2v_status lx2v_set_token_tile(lx2v_ctx *ctx, int tokens);
-/* Work split of the CTA-pair kernel: 0 = automatic, 1 = whole tiles per
- * pair, 2 = stream-K (equal k-block ranges per pair; a tile split between
- * pairs is summed through a context-owned workspace, allocated on first use).
+/* Work split of the CTA-pair kernel: 0 = automatic (whole tiles; for the
+ * two-pass kernel's gated residual into an f32 buffer, tiles may be cut into
+ * k-ranges that each reduce-add into it), 1 = whole tiles per pair, 2 =
+ * stream-K (equal k-block ranges per pair; a tile split between pairs is
+ * summed through a context-owned workspace, allocated on first use).
  * No reference counterpart: lightx2v-rs has no GPU GEMM to tune. */
 LX2V_API lx2v_status lx2v_set_split_mode(lx2v_ctx *ctx, int mode);
 /* Bounded-wait limit of the pipelined kernels, in nanoseconds (default 2e9).

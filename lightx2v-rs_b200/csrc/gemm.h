@@ -53,6 +53,11 @@ struct alignas(64) GemmParams {
     int epoch;
     int kgroup;               // pair kernel: k-blocks per MMA group (1, or 2 when K % 128 == 0)
     int tma_y;                // two-pass kernel: y written by TMA tensor stores (reduce-add for f32 residuals)
+    // Two-pass kernel, whole-tile mode with a reduce-add epilogue and no
+    // activation: every tile's k-blocks split into `ksplit` ranges, each a
+    // work item of its own that reduce-adds gate * partial into y (the bias
+    // with the first range only). 0 or 1: whole tiles.
+    int ksplit;
     float *partials;
     int *flags;
 };
@@ -67,6 +72,7 @@ cudaError_t gemm_pair_launch(int fmt, int bt, const GemmParams &p, int num_sms, 
 // [N][K] weight (box {64, 128}, 128-byte swizzle), tmap_x has box {64, bt/2}.
 cudaError_t gemm_ss_pair_launch(int bt, const GemmParams &p, int num_sms, cudaStream_t st);
 int gemm_ss_token_tile(int M, int N, int K, int pairs);
+int gemm_ss_ksplit(int M, int N, int K, int bt, int pairs);
 
 // Small-M path and the generic CUDA-core path (kernels.cu); they take plain
 // pointers instead of tensor maps.

@@ -148,6 +148,10 @@ __device__ __forceinline__ void decode_units(const GemmParams &p, const uint8_t 
 struct PairWork {
     long long lo = 0, hi = 0;  // stream-K k-block range
     int KB = 1, pair = 0, npairs = 1, my_tiles = 0;
+    // whole-tile mode: ks k-ranges per tile, items range-major (item u is
+    // range u / n_tiles of tile u % n_tiles), so the pairs running at the
+    // same time share k-ranges of x; my_tiles counts this pair's items
+    int ks = 1, n_tiles = 0;
     int dp = 0, my_dp = 0;     // whole tiles before the split range (all pairs / this pair)
     bool sk = false;
     __host__ __device__ __forceinline__ void init_split(int n_tiles, int dp_tiles) {
@@ -178,6 +182,12 @@ struct PairWork {
             tile = pair + idx * npairs;
             kb0 = 0;
             kb1 = KB;
+            if (!sk && ks > 1) {
+                const int part = tile / n_tiles;
+                tile -= part * n_tiles;
+                kb0 = (int)((long long)part * KB / ks);
+                kb1 = (int)((long long)(part + 1) * KB / ks);
+            }
             return;
         }
         const long long t = lo / KB + (idx - my_dp);

@@ -183,11 +183,11 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, const uint32_t 
 template <bool SK, typename Release>
 __device__ __forceinline__ void epilogue_direct(const GemmParams &p, uint32_t acc_addr, int ntok, int f, int m0,
                                                 Release release, const SkIO &io, int col0, int fl, uint8_t *stg,
-                                                int lane) {
+                                                int lane, bool with_bias) {
     const bool fok = f < p.N;
     float bias_f = 0.0f, gate_f = 1.0f;
     if (fok) {
-        if (p.bias) bias_f = p.bias_f32 ? reinterpret_cast<const float *>(p.bias)[f]
+        if (p.bias && with_bias) bias_f = p.bias_f32 ? reinterpret_cast<const float *>(p.bias)[f]
                                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.bias)[f]);
         if (p.gate) gate_f = p.gate_f32 ? reinterpret_cast<const float *>(p.gate)[f]
                                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p.gate)[f]);
@@ -237,7 +237,10 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
     work.KB = KG;
     work.pair = pair;
     work.npairs = npairs;
-    work.my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+    work.ks = !SK && p.ksplit > 1 ? p.ksplit : 1;
+    work.n_tiles = n_tiles;
+    const int n_items = n_tiles * work.ks;
+    work.my_tiles = pair < n_items ? (n_items - 1 - pair) / npairs + 1 : 0;
     work.sk = SK;
     // stream-K: full waves of whole tiles first, the rest split
     work.init_split(n_tiles, (n_tiles / npairs) * npairs);
@@ -393,7 +396,8 @@ __global__ void __launch_bounds__(SS_THREADS, 1) gemm_ss_pair_kernel(const __gri
             if (m0 < p.M) {
                 const uint32_t acc_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab.s * BT + half * (BT / 2));
                 epilogue_direct<SK>(p, acc_addr, BT / 2, ft * 256 + (int)rank * 128 + q * 32 + lane, m0, release, io,
-                                    half * (BT / 2), q * 32 + lane, smem + C::OFF_STG + wi * SS_STG_BOX, lane);
+                                    half * (BT / 2), q * 32 + lane, smem + C::OFF_STG + wi * SS_STG_BOX, lane,
+                                    SK || kb0 == 0);
             } else {
                 release();  // no token of this half exists
             }
@@ -472,7 +476,8 @@ static cudaError_t ss_launch_t(const GemmParams &p, int num_sms, cudaStream_t st
     const int n_tiles = ((p.M + BT - 1) / BT) * ((p.N + 255) / 256);
     // stream-K: every pair gets at least one group (the host checked
     // n_tiles * groups >= pairs)
-    const long long work = SK ? (long long)n_tiles * (((p.K + BK - 1) / BK) / GRP) : n_tiles;
+    const long long work = SK ? (long long)n_tiles * (((p.K + BK - 1) / BK) / GRP)
+                              : (long long)n_tiles * (p.ksplit > 1 ? p.ksplit : 1);
     const int pairs = work < max_pairs ? (int)work : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     cfg.numAttrs = 2;
@@ -498,6 +503,31 @@ cudaError_t gemm_ss_pair_launch(int bt, const GemmParams &p, int num_sms, cudaSt
         case 256: return ss_launch_bt<256, 2>(p, num_sms, st);
         default: return cudaErrorInvalidValue;
     }
+}
+
+// k-ranges per tile for a reduce-add epilogue (GemmParams::ksplit): the
+// fewest that minimise waves x max(k-blocks per item, KSPLIT_MIN_KB) + a fill
+// per item. Below ~24 k-blocks an item's k-loop is shorter than a 256 x 256
+// tile's epilogue (~8 us), which then no longer hides behind the next item.
+// On the 1.3B chunk's FFN2 (114 tiles, 140 k-blocks, 74 pairs) it picks 3:
+// 342 items in 5 waves of a third of a tile, against 2 waves of whole tiles.
+int gemm_ss_ksplit(int M, int N, int K, int bt, int pairs) {
+    constexpr int KSPLIT_MIN_KB = 24, FILL_KB = 2;
+    const long long tiles = (long long)((M + bt - 1) / bt) * ((N + 255) / 256);
+    const int kb = (K + BK - 1) / BK;
+    int best = 1;
+    long long best_cost = 0;
+    for (int ks = 1; ks <= 4; ++ks) {
+        if (kb / ks < 2) break;
+        const long long waves = (tiles * ks + pairs - 1) / pairs;
+        const long long per = (kb + ks - 1) / ks;
+        const long long cost = waves * ((per > KSPLIT_MIN_KB ? per : KSPLIT_MIN_KB) + FILL_KB);
+        if (ks == 1 || cost * 20 < best_cost * 19) {  // a new split must win by 5 %
+            best = ks;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 
 // Token tile for an M x N output on `pairs` CTA pairs. A wave of tiles takes

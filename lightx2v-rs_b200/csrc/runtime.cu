@@ -970,6 +970,10 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
             p.streamk = 1;
             if (++ctx->sk_epoch <= 0) ctx->sk_epoch = 1;
             p.epoch = ctx->sk_epoch;
+        } else if (ctx->split_mode == 0 && p.reduce && p.out_f32 && p.tma_y && act == 0) {
+            // gated residual into f32 h: k-ranges of a tile reduce-add on their own
+            p.ksplit = gemm_ss_ksplit((int)rows, (int)N, (int)K, bt, ctx->num_sms / 2);
+            if (p.ksplit > 1 && (long long)((K / 64) / p.kgroup) < p.ksplit) p.ksplit = 1;
         }
         CUDA_TRY(ctx, gemm_ss_pair_launch(bt, p, ctx->num_sms, ctx->stream));
         ctx->launches++;

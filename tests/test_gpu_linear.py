@@ -494,6 +494,41 @@ def test_stream_k_matches_whole_tiles_and_oracle(be, oracle, fmt, M, N, K, bt, p
     assert rel_l2(outs[(2, 0)][rows], want) <= REL_L2
 
 
+@pytest.mark.parametrize("M,N,K", [(4680, 1536, 8960), (1800, 768, 4096)])
+def test_k_split_gated_residual_matches_whole_tiles(be, oracle, M, N, K):
+    """The two-pass kernel cuts the tiles of a gated residual into k-ranges
+    that reduce-add into f32 h on their own (the 1.3B chunk's FFN2: 114
+    tiles on 74 pairs become 342 items of a third of a tile); the bias is
+    added by the first range only. Same bf16 operands as whole tiles (f32
+    sums in another order), and the oracle on sampled rows."""
+    w, q = make_weight("fp8", N, K, seed=151 + K, oracle=oracle)
+    dw = be.weight_fp8(q)
+    x = oracle.normal(152, (M + 40) * K)
+    h0 = oracle.normal(153, (M + 7) * N)
+    mods = oracle.normal(154, 6 * N, 0.5)
+    b = oracle.normal(155, N, 0.01)
+    xb, mb, bb = be.upload(x), be.upload(mods, F32), be.upload(b, F32)
+    outs = {}
+    try:
+        be.set_linear_path(5)
+        for mode in (0, 1):  # automatic (k-split), whole tiles
+            be.set_split_mode(mode)
+            hb = be.upload(h0, F32)
+            be.linear_gate_residual(xb, 40, M, dw, bb, Act.NONE, hb, 7, mb, 5)
+            outs[mode] = be.download(hb).reshape(M + 7, N)
+    finally:
+        be.set_split_mode(0)
+        be.set_linear_path(0)
+    h0 = h0.reshape(M + 7, N)
+    assert np.array_equal(outs[0][:7], h0[:7])
+    assert rel_l2(outs[0][7:] - h0[7:], outs[1][7:] - h0[7:]) <= 1e-5
+    rows = sampled_rows(M, 32)
+    lin = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, bias=b, x_row=40 + int(r), threads=8)[0]
+                    for r in rows])
+    want = oracle.gate_residual(h0[7:][rows].copy(), lin, len(rows), N, mods, 5)
+    assert rel_l2(outs[0][7:][rows] - h0[7:][rows], want - h0[7:][rows]) <= REL_L2
+
+
 @pytest.mark.parametrize("path", [4, 5])
 def test_stream_k_gated_residual_with_offsets(be, oracle, path):
     M, N, K = 1800, 768, 4096

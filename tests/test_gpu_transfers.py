@@ -91,8 +91,13 @@ def test_pipelined_steps_match_steps_run_one_at_a_time(be, oracle):
 
     piped, pq, pt = run([be.alloc(M * D, F32), be.alloc(M * D, F32)], True)
     seq, sq, st = run([be.alloc(M * D, F32)], False)
+    # h: FFN2's gated residual may be cut into k-ranges that reduce-add into
+    # f32 h in whatever order they finish (the two-pass kernel's k-split), so
+    # h agrees to f32 rounding; the plain linears are bit-identical
     for s in range(steps):
-        assert np.array_equal(piped[s], seq[s], equal_nan=True), s
+        assert np.array_equal(np.isnan(piped[s]), np.isnan(seq[s])), s
+        fin = ~np.isnan(seq[s])
+        assert np.linalg.norm(piped[s][fin] - seq[s][fin]) <= 1e-6 * np.linalg.norm(seq[s][fin]), s
     assert np.array_equal(pq, sq, equal_nan=True) and np.array_equal(pt, st, equal_nan=True)
     # and the last step against the oracle on a few rows
     rows = [0, 517, M - 1]
