@@ -337,6 +337,8 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     path: strong scaling); `weak` adds each rank running a whole chunk of
     its own, and `tp_ffn` the chunk's FFN tensor-parallel over the ranks."""
     import torch
+    if args.profile:
+        os.environ["LIGHTX2V_PROFILE"] = "1"
     from lightx2v_cuda import F32, CudaBackend
 
     torch.cuda.set_device(local_rank)
@@ -461,7 +463,9 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
         barrier()
         chunk = chunk_step_measure(args, be, ext, flush, "c4", "fp8", 30, rank, world,
                                    max_over_ranks if world > 1 else None)
-        chunk.pop("_profile", None)
+        prof = chunk.pop("_profile", None)
+        if args.profile:
+            chunk["profile_ms_per_step"] = prof
         barrier()
 
     flops_step = step_flops(M)
