@@ -786,7 +786,17 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     mat = lambda seed, r, c: (rng.normal(seed, r * c, 0.02), rng.normal(seed + 1, r, 0.01))
     wargs = (cfg, [block] * layers, mat(901, d, cfg.patch_in), mat(903, d, cfg.text_dim), mat(905, d, d),
              mat(907, cfg.patch_out, d))
-    model = LightDitCuda(be, *wargs) if world == 1 else TensorParallelDit(be, rank, world, *wargs)
+    if world == 1:
+        model = LightDitCuda(be, *wargs)
+    else:
+        import torch.distributed as dist
+
+        def exchange(blob):  # the CUDA IPC handles of the shared buffers
+            got = [None] * world
+            dist.all_gather_object(got, blob)
+            return got
+
+        model = TensorParallelDit(be, rank, world, *wargs, exchange=exchange)
     prompt = model.prepare_prompt(rng.normal(911, cfg.text_len * cfg.text_dim))
     ft, frames = (lh // cfg.patch) * (lw // cfg.patch), 3
     s = ft * frames
@@ -831,7 +841,8 @@ def chunk_step_measure(args, be, ext, flush, preset: str = "c4", fmt: str = "fp8
     att = 4.0 * cfg.head_dim * cfg.heads * (visible + s * cfg.text_len)
     flops = layers * (blk + att) + ends
     return {"n_gpus": world, "parallelism": ("one GPU" if world == 1 else
-                                             f"tp{world}: heads and FFN features split, all-reduces over NVLink"),
+                                             f"tp{world}: heads and FFN features split; token rows owned per rank, partials reduced and "
+                                             "normalised rows gathered over NVLink peer memory (CUDA IPC)"),
             "workload": f"{preset}: {layers} blocks (dim {d}, {cfg.heads} x {cfg.head_dim} heads, FFN {cfg.ffn_dim}) + "
                         f"patch embed + head, {s} tokens ({frames} frames x {ft}), start frame 12, {fmt} block "
                         f"weights, 12-frame MemRoPE cache", "ms_per_step": ms,

@@ -335,6 +335,53 @@ LX2V_API lx2v_status lx2v_comm_init(lx2v_ctx *ctx, const unsigned char *id, int 
 /* buf[0..len) = sum over the group's ranks of their buf[0..len), in place. */
 LX2V_API lx2v_status lx2v_all_reduce_sum(lx2v_ctx *ctx, lx2v_buf *buf, size_t len);
 
+/* ---- tensor parallelism over NVLink peer memory ---------------------------- */
+/* No counterpart in the reference (it runs on one device). A row-split
+ * linear of a DiT block leaves every rank with a partial product of all M
+ * rows; with the ranks' buffers shared by CUDA IPC, lx2v_tp_reduce_norm does
+ * the reduce-scatter, the residual add, the norm and the all-gather in one
+ * kernel per rank, and lx2v_peers_barrier orders the ranks around it.
+ *
+ * lx2v_buf_ipc_handle writes the CUDA IPC handle of an own buffer (at most
+ * LX2V_IPC_HANDLE_BYTES bytes); the caller sends it to the other processes of
+ * the group (as it does the NCCL id), and lx2v_buf_open_ipc maps a peer's
+ * buffer into this context (len elements of dtype; lx2v_buf_free unmaps it).
+ * Peer buffers are device memory of another GPU: only the calls below and
+ * lx2v_tp_reduce_norm's arguments may take them. */
+#define LX2V_IPC_HANDLE_BYTES 64
+LX2V_API lx2v_status lx2v_buf_ipc_handle(lx2v_ctx *ctx, const lx2v_buf *buf, unsigned char *out, size_t cap);
+LX2V_API lx2v_status lx2v_buf_open_ipc(lx2v_ctx *ctx, const unsigned char *handle, size_t len, int dtype,
+                                       lx2v_buf **out);
+/* A group of `world` ranks (at most 8, one process per GPU), this one being
+ * `rank`. flag_bufs[r] is rank r's flag buffer as this context sees it (its
+ * own buffer at index rank, peers' opened by lx2v_buf_open_ipc): every rank
+ * allocates one of at least world u32 (e.g. world f32 elements, zeroed by
+ * lx2v_buf_alloc) before any rank's first barrier. */
+typedef struct lx2v_peers lx2v_peers;
+LX2V_API lx2v_status lx2v_peers_create(lx2v_ctx *ctx, int rank, int world, lx2v_buf *const *flag_bufs,
+                                       lx2v_peers **out);
+LX2V_API void lx2v_peers_free(lx2v_peers *g);
+/* Barrier on the context's stream: work queued after it on any rank sees the
+ * writes (local and to peer memory) of work queued before it on every rank.
+ * Every rank calls the group's barriers in the same order. The wait is
+ * bounded (lx2v_set_wait_limit_ns); on expiry the next lx2v_sync returns
+ * LX2V_ERR_DEVICE. */
+LX2V_API lx2v_status lx2v_peers_barrier(lx2v_ctx *ctx, lx2v_peers *g);
+/* Rows [row0, row1) of an M x dim block output owned by this rank:
+ *   h[r] += mods[gate] * sum over ranks p (in rank order, f32) of parts[p][r]
+ *   (gate < 0: h[r] += the sum; parts NULL: no add), then
+ *   normed[p][r] = norm(h[r]) for every rank p,
+ * norm as lx2v_layer_norm (kind 0 affine w, b; 1 modulated by norm_mods rows
+ * scale, shift). h is f32; parts and normed are indexed by rank (own buffer
+ * at index rank, peers' opened by IPC). The caller puts a barrier before (the
+ * partials are complete) and after (the outputs are). Replaces the
+ * reference's residual_norm (cpu lib.rs:364-392), or gate_residual followed by
+ * layer_norm, on a block split over the group's GPUs. */
+LX2V_API lx2v_status lx2v_tp_reduce_norm(lx2v_ctx *ctx, lx2v_peers *g, lx2v_buf *const *parts, lx2v_buf *h,
+                                         size_t row0, size_t row1, size_t dim, const lx2v_buf *gate_mods, long gate,
+                                         int kind, const lx2v_buf *w, const lx2v_buf *b, const lx2v_buf *norm_mods,
+                                         size_t scale, size_t shift, float eps, lx2v_buf *const *normed);
+
 /* ---- knobs for tests and benchmarks -------------------------------------- */
 /* Kernel choice for linear: 0 = automatic, 1 = tensor-core GEMM (tcgen05, one
  * CTA per tile), 2 = small-M GEMV, 3 = generic CUDA-core kernel, 4 = tensor-

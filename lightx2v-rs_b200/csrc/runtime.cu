@@ -28,6 +28,7 @@
 #include "attention.h"
 #include "kvcache.h"
 #include "dit_ops.h"
+#include "peer.h"
 
 using namespace lx2v;
 
@@ -96,6 +97,7 @@ struct lx2v_buf {
     size_t len = 0;
     int dtype = LX2V_BF16;
     cudaEvent_t last_use = nullptr;  // recorded on the compute stream after each op that touches the buffer
+    bool ipc = false;                // a peer's buffer mapped by CUDA IPC (closed, not freed)
 };
 
 struct lx2v_weight {
@@ -589,7 +591,10 @@ extern "C" void lx2v_buf_free(lx2v_ctx *ctx, lx2v_buf *buf) {
         cudaSetDevice(ctx->dev);
         cudaStreamSynchronize(ctx->stream);
     }
-    if (buf->ptr) cudaFree(buf->ptr);
+    if (buf->ptr) {
+        if (buf->ipc) cudaIpcCloseMemHandle(buf->ptr);
+        else cudaFree(buf->ptr);
+    }
     if (buf->last_use) cudaEventDestroy(buf->last_use);
     delete buf;
 }
@@ -2122,3 +2127,127 @@ extern "C" lx2v_status lx2v_all_reduce_sum(lx2v_ctx *ctx, lx2v_buf *buf, size_t 
     CUDA_TRY(ctx, note_use(ctx, buf));
     return LX2V_OK;
 }
+
+// ---- tensor parallelism over NVLink peer memory --------------------------------------
+extern "C" lx2v_status lx2v_buf_ipc_handle(lx2v_ctx *ctx, const lx2v_buf *buf, unsigned char *out, size_t cap) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!buf || !buf->ptr || buf->ipc) return fail(ctx, LX2V_ERR_INVALID, "no own device buffer to share");
+    if (!out || cap < sizeof(cudaIpcMemHandle_t)) return fail(ctx, LX2V_ERR_INVALID, "handle buffer too small");
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, buf->ptr));
+    memcpy(out, &h, sizeof h);
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_buf_open_ipc(lx2v_ctx *ctx, const unsigned char *handle, size_t len, int dtype,
+                                         lx2v_buf **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!handle || !out || !valid_dtype(dtype)) return fail(ctx, LX2V_ERR_INVALID, "bad handle, output or dtype");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void *ptr = nullptr;
+    CUDA_TRY(ctx, cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    auto *b = new lx2v_buf();
+    b->ptr = ptr;
+    b->len = len;
+    b->dtype = dtype;
+    b->ipc = true;
+    *out = b;
+    return LX2V_OK;
+}
+
+struct lx2v_peers {
+    int rank = 0, world = 1;
+    PeerFlags flags;
+    unsigned epoch = 0;
+};
+
+extern "C" lx2v_status lx2v_peers_create(lx2v_ctx *ctx, int rank, int world, lx2v_buf *const *flag_bufs,
+                                         lx2v_peers **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !flag_bufs || world < 1 || world > LX2V_MAX_PEERS || rank < 0 || rank >= world)
+        return fail(ctx, LX2V_ERR_INVALID, "bad peer group (rank %d, world %d, at most %d ranks)", rank, world,
+                    LX2V_MAX_PEERS);
+    auto *g = new lx2v_peers();
+    g->rank = rank;
+    g->world = world;
+    memset(&g->flags, 0, sizeof g->flags);
+    for (int r = 0; r < world; ++r) {
+        const lx2v_buf *f = flag_bufs[r];
+        if (!f || !f->ptr || f->len * esize(f->dtype) < (size_t)world * 4) {
+            delete g;
+            return fail(ctx, LX2V_ERR_INVALID, "flag buffer of rank %d holds fewer than %d u32", r, world);
+        }
+        g->flags.flags[r] = (unsigned *)f->ptr;
+    }
+    *out = g;
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_peers_free(lx2v_peers *g) { delete g; }
+
+extern "C" lx2v_status lx2v_peers_barrier(lx2v_ctx *ctx, lx2v_peers *g) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!g) return fail(ctx, LX2V_ERR_INVALID, "null peer group");
+    OpScope ps(ctx, "peer_barrier");
+    if (++g->epoch == 0) g->epoch = 1;
+    CUDA_TRY(ctx, peer_barrier_launch(g->flags, g->world, g->rank, g->epoch, ctx->err_dev, ctx->wait_limit_ns,
+                                      ctx->stream));
+    ctx->launches++;
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_tp_reduce_norm(lx2v_ctx *ctx, lx2v_peers *g, lx2v_buf *const *parts, lx2v_buf *h,
+                                           size_t row0, size_t row1, size_t dim, const lx2v_buf *gate_mods, long gate,
+                                           int kind, const lx2v_buf *w, const lx2v_buf *b, const lx2v_buf *norm_mods,
+                                           size_t scale, size_t shift, float eps, lx2v_buf *const *normed) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!g || !h || !normed) return fail(ctx, LX2V_ERR_INVALID, "null peer group, h or outputs");
+    if (!is_f32(h) || row1 * dim > h->len || row0 > row1)
+        return fail(ctx, LX2V_ERR_INVALID, "h must be f32 holding rows [row0, row1) of width dim");
+    if (!tp_reduce_norm_supported((int)dim))
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "rows of %zu values (a multiple of 8, at most 8192)", dim);
+    if (parts && gate >= 0 && (!gate_mods || gate_mods->len < ((size_t)gate + 1) * dim))
+        return fail(ctx, LX2V_ERR_INVALID, "gate row beyond mods");
+    NormArgs na;  // the norm's parameter checks, on this rank's output
+    if ((s = norm_args(ctx, na, row1, dim, kind, w, b, scale, shift, norm_mods, eps, normed[g->rank]))) return s;
+    TpNormArgs a;
+    memset(&a, 0, sizeof a);
+    for (int r = 0; r < g->world; ++r) {
+        const lx2v_buf *o = normed[r];
+        if (!o || o->len < row1 * dim || o->dtype != normed[g->rank]->dtype)
+            return fail(ctx, LX2V_ERR_INVALID, "output of rank %d holds fewer than row1 x dim or differs in dtype", r);
+        a.outs[r] = o->ptr;
+        if (parts) {
+            const lx2v_buf *p = parts[r];
+            if (!p || p->len < row1 * dim || p->dtype != parts[0]->dtype)
+                return fail(ctx, LX2V_ERR_INVALID, "partial of rank %d holds fewer than row1 x dim or differs in dtype",
+                            r);
+            a.parts[r] = p->ptr;
+        }
+    }
+    a.n_outs = g->world;
+    a.out_f32 = is_f32(normed[g->rank]);
+    a.n_parts = parts ? g->world : 0;
+    a.parts_f32 = parts ? is_f32(parts[0]) : 0;
+    a.h = h->ptr;
+    a.row0 = (int64_t)row0; a.row1 = (int64_t)row1; a.dim = (int)dim;
+    a.gmods = gate_mods ? gate_mods->ptr : nullptr; a.gmods_f32 = is_f32(gate_mods);
+    a.gate = parts && gate >= 0 ? (int)gate : -1;
+    a.kind = kind;
+    a.w = na.w; a.w_f32 = na.w_f32; a.b = na.b; a.b_f32 = na.b_f32;
+    a.nmods = na.mods; a.nmods_f32 = na.mods_f32; a.scale = na.scale; a.shift = na.shift;
+    a.eps = eps;
+    if (row1 == row0) return LX2V_OK;
+    OpScope ps(ctx, "tp_reduce_norm");
+    CUDA_TRY(ctx, tp_reduce_norm_launch(a, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {h, gate_mods, w, b, norm_mods, normed[g->rank]}));
+    return LX2V_OK;
+}
+

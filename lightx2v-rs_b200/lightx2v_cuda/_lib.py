@@ -96,9 +96,17 @@ SIGNATURES = {
     "lx2v_comm_unique_id": (_st, [_vp, _sz]),
     "lx2v_comm_init": (_st, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     "lx2v_all_reduce_sum": (_st, [_vp, _vp, _sz]),
+    "lx2v_buf_ipc_handle": (_st, [_vp, _vp, _vp, _sz]),
+    "lx2v_buf_open_ipc": (_st, [_vp, _vp, _sz, ctypes.c_int, _pp]),
+    "lx2v_peers_create": (_st, [_vp, ctypes.c_int, ctypes.c_int, _pp, _pp]),
+    "lx2v_peers_free": (None, [_vp]),
+    "lx2v_peers_barrier": (_st, [_vp, _vp]),
+    "lx2v_tp_reduce_norm": (_st, [_vp, _vp, _pp, _vp, _sz, _sz, _sz, _vp, ctypes.c_long, ctypes.c_int, _vp, _vp,
+                                  _vp, _sz, _sz, ctypes.c_float, _pp]),
 }
 
 COMM_ID_BYTES = 128
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 

@@ -85,6 +85,20 @@ class KvCache:
             self.handle = None
 
 
+class Peers:
+    """A tensor-parallel peer group (lx2v_peers): this rank, the group size
+    and the flag buffers its barrier uses (kept alive with it)."""
+
+    def __init__(self, be: "CudaBackend", handle: int, rank: int, world: int, flag_bufs: list):
+        self.be, self.handle, self.rank, self.world = be, ctypes.c_void_p(handle), rank, world
+        self._flags = flag_bufs
+
+    def __del__(self):
+        if getattr(self, "handle", None) and self.handle.value:
+            self.be._lib.lx2v_peers_free(self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+
 class CudaBackend:
     """The CUDA backend for one device. Buffers default to bf16, the CUDA
     backend's activation precision (backend.rs:9-11)."""
@@ -420,6 +434,44 @@ class CudaBackend:
     def all_reduce_sum(self, buf: Buf, length: int | None = None):
         """In place: buf[:length] = sum over the group (on this context's stream)."""
         self._check(self._lib.lx2v_all_reduce_sum(self._ctx, buf.handle, buf.len if length is None else length))
+
+    # ---- tensor parallelism over NVLink peer memory (no reference counterpart) --------
+    def ipc_handle(self, buf: Buf) -> bytes:
+        """CUDA IPC handle of an own buffer, for the other processes of a group."""
+        out = ctypes.create_string_buffer(L.IPC_HANDLE_BYTES)
+        self._check(self._lib.lx2v_buf_ipc_handle(self._ctx, buf.handle, out, L.IPC_HANDLE_BYTES))
+        return out.raw
+
+    def open_ipc(self, handle: bytes, length: int, dtype: int) -> Buf:
+        """A peer's buffer mapped into this context (freeing it unmaps it)."""
+        assert len(handle) == L.IPC_HANDLE_BYTES
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_buf_open_ipc(self._ctx, handle, length, dtype, ctypes.byref(h)))
+        return Buf(self, h.value, length, dtype)
+
+    def peers_create(self, rank: int, world: int, flag_bufs: list) -> "Peers":
+        """A peer group; flag_bufs[r] is rank r's flag buffer (own one at index rank)."""
+        arr = (ctypes.c_void_p * world)(*[b.handle.value for b in flag_bufs])
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_peers_create(self._ctx, rank, world, arr, ctypes.byref(h)))
+        return Peers(self, h.value, rank, world, flag_bufs)
+
+    def peers_barrier(self, g: "Peers"):
+        self._check(self._lib.lx2v_peers_barrier(self._ctx, g.handle))
+
+    def tp_reduce_norm(self, g: "Peers", parts: list | None, h: Buf, row0: int, row1: int, dim: int,
+                       gate_mods: Buf | None, gate: int | None, norm, norm_mods: Buf | None, eps: float,
+                       normed: list):
+        """Rows [row0, row1) owned by this rank: h += gate * sum of every rank's
+        partial, then the norm into every rank's output (see the C header)."""
+        kind, w, b, scale, shift = self._norm(norm)
+        n = g.world
+        pa = (ctypes.c_void_p * n)(*[p.handle.value for p in parts]) if parts is not None else None
+        oa = (ctypes.c_void_p * n)(*[o.handle.value for o in normed])
+        self._check(self._lib.lx2v_tp_reduce_norm(
+            self._ctx, g.handle, pa, h.handle, row0, row1, dim, gate_mods.handle if gate_mods is not None else None,
+            -1 if gate is None else gate, kind, w, b, norm_mods.handle if norm_mods is not None else None,
+            scale, shift, eps, oa))
 
     # ---- knobs ---------------------------------------------------------------------
     def set_linear_path(self, path: int):

@@ -178,21 +178,33 @@ class TensorParallelDit:
                  local; the q/k RMS norm spans all heads (cpu lib.rs:433-438),
                  so each rank's per-row sum of squares over its heads is
                  all-reduced (f32, one value per row) before head_split
-                 normalises; out1 is split by its input columns and its
-                 partial products are all-reduced (bias added once);
+                 normalises; out1 is split by its input columns and leaves a
+                 partial product on every rank (bias on rank 0);
       cross-attn q2 and the prompt's K/V the same way (the prompt K RMS too);
-                 out2 split and all-reduced like out1;
-      FFN        TensorParallelFFN (features split, FFN2 partials all-reduced);
-      the rest   patch embed, the norms, the residual stream h and the output
-                 head are replicated, so every rank ends a step with the same h.
+                 out2 split like out1;
+      FFN        FFN1 column-split (GELU local), FFN2 row-split into a partial;
+      rows       rank r owns token rows [r0, r1) of the chunk: after each
+                 partial it adds its rows of every rank's partial (over NVLink
+                 peer memory, CUDA IPC) into its rows of the residual stream h
+                 and writes them normalised into every rank's activation
+                 buffer (lx2v_tp_reduce_norm between two lx2v_peers_barrier),
+                 so the norms run once per row instead of on every rank;
+      the rest   patch embed and the output head run on all rows on every
+                 rank (the head's input is gathered like the others), so every
+                 rank ends a step with the same output.
 
     `blocks` etc. are the host weights of lightx2v_cuda.dit.LightDitCuda; every
     rank holds the same host copy and uploads only its shard."""
 
     def __init__(self, be, rank: int, world: int, cfg, blocks, patch, text1, text2, proj_out, memrope=None,
-                 partial_dtype: int = L.BF16):
+                 partial_dtype: int = L.BF16, exchange=None):
         from .dit import Block, Linear, MemRopeConfig, upload_weight as up
         self.be, self.rank, self.world, self.cfg = be, rank, world, cfg
+        # exchange(bytes) -> [bytes of rank 0, ..., rank world-1]: the host
+        # channel that carries the CUDA IPC handles of the shared buffers
+        # (torch.distributed, a launcher's store, ...); needed for world > 1
+        assert world == 1 or exchange is not None, "a tensor-parallel group needs an exchange for IPC handles"
+        self.exchange = exchange
         self.memrope = memrope or MemRopeConfig()
         self.partial_dtype = partial_dtype
         d, hd = cfg.dim, cfg.head_dim
@@ -247,20 +259,45 @@ class TensorParallelDit:
             out.append((k, v))
         return out
 
+    def _share(self, buf):
+        """Every rank's instance of `buf` (a collective over the group): own
+        buffer at index rank, the peers' mapped by CUDA IPC."""
+        if self.world == 1:
+            return [buf]
+        handles = self.exchange(self.be.ipc_handle(buf))
+        return [buf if r == self.rank else self.be.open_ipc(hd, buf.len, buf.dtype) for r, hd in enumerate(handles)]
+
     def workspace(self, chunk_frames: int, frame_tokens: int, rope_cos, rope_sin):
+        """Buffers of one chunk. Each rank owns rows [r0, r1) of the chunk's
+        tokens (sequence parallelism): it keeps those rows of the residual
+        stream h current and normalises them for every rank; the partial
+        products, the normalised activations and the barrier flags are shared
+        with the peers by CUDA IPC (a collective: every rank calls this in
+        the same order)."""
         from types import SimpleNamespace
         be, c = self.be, self.cfg
         s, d, dl = chunk_frames * frame_tokens, c.dim, self.dl
         cap = self.memrope.cache_frames * frame_tokens
-        return SimpleNamespace(
-            tokens=s, frame_tokens=frame_tokens,
+        rows = split_points(s, self.world, 1)
+        part, normed = be.alloc(s * d, self.partial_dtype), be.alloc(s * d)
+        ws = SimpleNamespace(
+            tokens=s, frame_tokens=frame_tokens, r0=rows[self.rank], r1=rows[self.rank + 1],
             caches=[be.kv_cache_new(self.nl, c.head_dim, cap) for _ in self.blocks],
-            h=be.alloc(s * d, L.F32), normed=be.alloc(s * d), qkv=be.alloc(s * 3 * dl), q=be.alloc(s * dl),
+            h=be.alloc(s * d, L.F32), normed=normed, qkv=be.alloc(s * 3 * dl), q=be.alloc(s * dl),
             k=be.alloc(s * dl), v=be.alloc(s * dl), attn=be.alloc(s * dl), q2=be.alloc(s * dl),
-            part=be.alloc(s * d, self.partial_dtype), ss_q=be.alloc(s, L.F32), ss_k=be.alloc(s, L.F32),
+            hid=be.alloc(s * self.ffns[0].local), part=part, ss_q=be.alloc(s, L.F32), ss_k=be.alloc(s, L.F32),
             patches=be.alloc(s * max(c.patch_in, c.patch_out)),
             rope_cos=be.upload(np.asarray(rope_cos, np.float32), L.F32),
             rope_sin=be.upload(np.asarray(rope_sin, np.float32), L.F32))
+        ws.parts, ws.normeds = self._share(part), self._share(normed)
+        flags = be.alloc(self.world, L.F32)  # u32 barrier slots, zeroed
+        be.sync()  # zeroed before any peer's first barrier can write it
+        ws.peers = be.peers_create(self.rank, self.world, self._share(flags))
+        return ws
+
+    def row_range(self, ws) -> tuple[int, int]:
+        """The chunk rows whose residual stream this rank keeps current."""
+        return ws.r0, ws.r1
 
     def patch_embed(self, ws, latent, c: int, t: int, h: int, w: int):
         be = self.be
@@ -268,15 +305,32 @@ class TensorParallelDit:
         be.linear(ws.patches, 0, ws.tokens, self.patch.w, self.patch.b, L.ACT_NONE, ws.h, 0)
 
     def forward_chunk(self, ws, mods, head_mods, prompt, start_frame: int, out):
-        """dit.rs:569-782 on this rank's shard; h and out end replicated."""
+        """dit.rs:569-782 on this rank's shard; out ends replicated, h current
+        on this rank's rows [ws.r0, ws.r1).
+
+        After each row-split linear (out1, out2, FFN2) every rank holds a
+        partial product of all rows; between two barriers, one kernel per rank
+        adds its rows of every rank's partial (gated) into h and writes those
+        rows normalised into every rank's activation buffer, which is what the
+        next column-split linear (q2, FFN1, the next block's QKV, the head)
+        reads. The FFN's gated residual and the next block's (or the head's)
+        layer_norm are one such step."""
         from .dit import GATE_FFN, GATE_MSA, SCALE_FFN, SCALE_MSA, SHIFT_FFN, SHIFT_MSA
         be, c = self.be, self.cfg
         s, d, hd, nl, dl, eps = ws.tokens, c.dim, c.head_dim, self.nl, self.dl, c.eps
+        r0, r1, g = ws.r0, ws.r1, ws.peers
         rope = (ws.rope_cos, ws.rope_sin)
         token_temporal = start_frame + np.arange(s) // ws.frame_tokens
         tq = token_temporal.astype(np.int32)
+
+        def step(parts, gate_mods, gate, norm, norm_mods):
+            be.peers_barrier(g)  # every rank's partial (and the previous readers of the outputs) done
+            be.tp_reduce_norm(g, parts, ws.h, r0, r1, d, gate_mods, gate, norm, norm_mods, eps, ws.normeds)
+            be.peers_barrier(g)  # every rank's rows of the output written
+
+        step(None, None, None, ("mod", SCALE_MSA, SHIFT_MSA), mods[0])
+        n_blocks = len(self.blocks)
         for li, (bl, m) in enumerate(zip(self.blocks, mods)):
-            be.layer_norm(ws.h, s, d, ("mod", SCALE_MSA, SHIFT_MSA), m, eps, ws.normed)
             be.linear(ws.normed, 0, s, bl.qkv.w, bl.qkv.b, L.ACT_NONE, ws.qkv, 0)
             be.row_sumsq(ws.qkv, s, 3 * dl, 0, dl, ws.ss_q)
             be.row_sumsq(ws.qkv, s, 3 * dl, dl, dl, ws.ss_k)
@@ -290,8 +344,7 @@ class TensorParallelDit:
             be.kv_cache_memrope_update(cache, self.memrope, ws.frame_tokens)
             be.kv_cache_attention(ws.q, s, tq, cache, ws.attn)
             be.linear(ws.attn, 0, s, bl.out1.w, bl.out1.b, L.ACT_NONE, ws.part, 0)
-            self._reduce(ws.part, s * d)
-            be.residual_norm(ws.h, ws.part, s, d, m, GATE_MSA, ("affine", bl.norm2_w, bl.norm2_b), eps, ws.normed)
+            step(ws.parts, m, GATE_MSA, ("affine", bl.norm2_w, bl.norm2_b), None)
             k2, v2 = prompt[li]
             be.linear(ws.normed, 0, s, bl.q2.w, bl.q2.b, L.ACT_NONE, ws.q2, 0)
             be.row_sumsq(ws.q2, s, dl, 0, dl, ws.ss_q)
@@ -299,8 +352,12 @@ class TensorParallelDit:
             be.head_split_rms(ws.q2, s, dl, 0, nl, hd, bl.norm_q2, ws.ss_q, d, None, eps, ws.q)
             be.attention(ws.q, k2, v2, nl, s, c.text_len, hd, ws.attn)
             be.linear(ws.attn, 0, s, bl.out2.w, bl.out2.b, L.ACT_NONE, ws.part, 0)
-            self._reduce(ws.part, s * d)
-            be.residual_norm(ws.h, ws.part, s, d, m, None, ("mod", SCALE_FFN, SHIFT_FFN), eps, ws.normed)
-            self.ffns[li].forward(ws.normed, s, ws.h, m, GATE_FFN)
-        be.layer_norm(ws.h, s, d, ("mod", 1, 0), head_mods, eps, ws.normed)
+            step(ws.parts, m, None, ("mod", SCALE_FFN, SHIFT_FFN), m)
+            ffn = self.ffns[li]
+            be.linear(ws.normed, 0, s, ffn.w1, ffn.b1, L.ACT_GELU_TANH, ws.hid, 0)
+            be.linear(ws.hid, 0, s, ffn.w2, ffn.b2, L.ACT_NONE, ws.part, 0)
+            if li + 1 < n_blocks:
+                step(ws.parts, m, GATE_FFN, ("mod", SCALE_MSA, SHIFT_MSA), mods[li + 1])
+            else:
+                step(ws.parts, m, GATE_FFN, ("mod", 1, 0), head_mods)
         be.linear(ws.normed, 0, s, self.proj_out.w, self.proj_out.b, L.ACT_NONE, out, 0)

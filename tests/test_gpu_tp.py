@@ -139,20 +139,26 @@ def _dit_rank_main(rank, world, port, q):
         embeds = rng.normal(911, cfg.text_len * cfg.text_dim)
         mods = [be.upload(rng.normal(920 + l, 6 * d, 0.1), F32) for l in range(cfg.layers)]
         head = be.upload(rng.normal(930, 2 * d, 0.1), F32)
-        models = [TensorParallelDit(be, rank, world, *args)]
+        def exchange(blob):
+            got = [None] * world
+            dist.all_gather_object(got, blob)
+            return got
+
+        models = [TensorParallelDit(be, rank, world, *args, exchange=exchange)]
         if rank == 0:
             models.append(LightDitCuda(be, *args))  # the unsplit model on one GPU
         results = []
         for mdl in models:
             prompt = mdl.prepare_prompt(embeds)
             ws = mdl.workspace(frames, ft, cos, sin)
+            rows = mdl.row_range(ws) if hasattr(mdl, "row_range") else (0, s)
             out = be.alloc(s * cfg.patch_out, F32)
             outs = []
             for chunk in range(4):
                 be.write(ws.h, rng.normal(940 + chunk, s * d))
                 mdl.forward_chunk(ws, mods, head, prompt, 3 * chunk, out)
-                outs.append((be.download(out), be.download(ws.h)))
-            results.append(outs)
+                outs.append((be.download(out), be.download(ws.h).reshape(s, d)[rows[0]:rows[1]]))
+            results.append((rows, outs))
         q.put((rank, results))
         dist.barrier()
     finally:
@@ -161,10 +167,11 @@ def _dit_rank_main(rank, world, port, q):
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 def test_tensor_parallel_dit_chunk_steps_match_one_gpu():
-    # heads split 6 + 6, the q/k RMS sums of squares and the out1 / out2 /
-    # FFN2 partials all-reduced (bf16 partials); four chunks through the
-    # MemRoPE caches; rank 0's output and residual stream against the unsplit
-    # model on one GPU, and h identical on both ranks
+    # heads split 6 + 6, the q/k RMS sums of squares all-reduced, the out1 /
+    # out2 / FFN2 partials (bf16) reduced over NVLink peer memory onto each
+    # rank's rows, normalised and gathered; four chunks through the MemRoPE
+    # caches; the output (identical on both ranks) and the residual stream
+    # assembled from each rank's rows against the unsplit model on one GPU
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -179,10 +186,13 @@ def test_tensor_parallel_dit_chunk_steps_match_one_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    tp0, one = res[0][0], res[0][1]
-    tp1 = res[1][0]
+    (rows0, tp0), (_, one) = res[0][0], res[0][1]
+    rows1, tp1 = res[1][0]
+    assert rows0[0] == 0 and rows0[1] == rows1[0] and rows1[1] == one[0][1].shape[0]
     for chunk in range(4):
-        assert np.array_equal(tp0[chunk][1], tp1[chunk][1])  # h replicated
-        for got, want in zip(tp0[chunk], one[chunk]):
+        assert np.array_equal(tp0[chunk][0], tp1[chunk][0])  # the output is replicated
+        # each rank keeps its own rows of the residual stream current
+        h = np.concatenate([tp0[chunk][1], tp1[chunk][1]])
+        for got, want in ((tp0[chunk][0], one[chunk][0]), (h, one[chunk][1])):
             assert np.isfinite(got).all()
             assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-2, chunk
