@@ -230,6 +230,13 @@ LX2V_API lx2v_status lx2v_head_split_rms(lx2v_ctx *ctx, const lx2v_buf *src, siz
                                          const lx2v_buf *sin, float eps, lx2v_buf *out);
 /* Backend::patchify: latent [c, t, h, w] -> tokens [t*(h/p)*(w/p), c*p*p],
  * feature c*p^2 + kh*p + kw. */
+/* lx2v_head_split_rms with the row statistic summed from `parts` slices of
+ * sumsq ([parts][rows], added in order): the slices are the ranks' sums from
+ * lx2v_row_sumsq_peers. */
+LX2V_API lx2v_status lx2v_head_split_rms_parts(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                               size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                               const lx2v_buf *sumsq, size_t parts, size_t rms_dim,
+                                               const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out);
 LX2V_API lx2v_status lx2v_patchify(lx2v_ctx *ctx, const lx2v_buf *latent, size_t c, size_t t, size_t h, size_t w,
                                    size_t p, lx2v_buf *out);
 /* Backend::unpatchify: the inverse of lx2v_patchify. */
@@ -377,6 +384,14 @@ LX2V_API lx2v_status lx2v_peers_barrier(lx2v_ctx *ctx, lx2v_peers *g);
  * partials are complete) and after (the outputs are). Replaces the
  * reference's residual_norm (cpu lib.rs:364-392), or gate_residual followed by
  * layer_norm, on a block split over the group's GPUs. */
+/* lx2v_row_sumsq over the group: this rank's row sums of squares of columns
+ * [col_off, col_off + width) into outs[p][rank * rows + r] for every rank p
+ * (each out f32 of world * rows; own buffer at index rank, peers' by IPC).
+ * After a barrier, lx2v_head_split_rms_parts with parts = world adds the
+ * ranks' sums in rank order: the cross-head q/k RMS of a head-split block
+ * without a collective library. */
+LX2V_API lx2v_status lx2v_row_sumsq_peers(lx2v_ctx *ctx, lx2v_peers *g, const lx2v_buf *src, size_t rows,
+                                          size_t src_stride, size_t col_off, size_t width, lx2v_buf *const *outs);
 LX2V_API lx2v_status lx2v_tp_reduce_norm(lx2v_ctx *ctx, lx2v_peers *g, lx2v_buf *const *parts, lx2v_buf *h,
                                          size_t row0, size_t row1, size_t dim, const lx2v_buf *gate_mods, long gate,
                                          int kind, const lx2v_buf *w, const lx2v_buf *b, const lx2v_buf *norm_mods,

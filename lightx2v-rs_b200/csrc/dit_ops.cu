@@ -105,6 +105,13 @@ __global__ void __launch_bounds__(ROW_THREADS) residual_norm_kernel(NormArgs a, 
     norm_row(vals, a, r, red);
 }
 
+// Row r's sum of squares over all heads: the parts (one per rank) added in order.
+__device__ __forceinline__ float summed_sumsq(const HeadSplitArgs &a, int64_t r) {
+    float t = 0.0f;
+    for (int p = 0; p < a.sumsq_parts; ++p) t += a.sumsq[p * a.sumsq_stride + r];
+    return t;
+}
+
 // One row of src: columns [col_off, col_off + heads * hd), optional RMS over
 // all of them times w[j], optional RoPE on interleaved pairs of each head,
 // written to out[h][r][:]. Thread t takes the pairs t, t + 128, ...
@@ -126,7 +133,7 @@ __global__ void __launch_bounds__(ROW_THREADS) head_split_kernel(HeadSplitArgs a
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < NP; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];  // zeros past the row add nothing
-        const float ms = a.sumsq ? a.sumsq[r] / (float)a.rms_dim : block_sum(ss, red) / (float)d;
+        const float ms = a.sumsq ? summed_sumsq(a, r) / (float)a.rms_dim : block_sum(ss, red) / (float)d;
         const float inv = 1.0f / sqrtf(ms + a.eps);
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
@@ -282,7 +289,7 @@ __global__ void __launch_bounds__(512) head_split_vec_kernel(HeadSplitArgs a) {
         float ss = 0.0f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
-        const float ms = a.sumsq ? a.sumsq[r] / (float)a.rms_dim : block_sum_any(ss, red) / (float)d;
+        const float ms = a.sumsq ? summed_sumsq(a, r) / (float)a.rms_dim : block_sum_any(ss, red) / (float)d;
         const float inv = 1.0f / sqrtf(ms + a.eps);
         float w[8];
         ld8(a.rms_w, a.w_f32, j0, w);

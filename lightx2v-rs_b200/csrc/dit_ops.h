@@ -25,7 +25,9 @@ struct HeadSplitArgs {
     int64_t rows, src_stride, col_off;
     int heads, head_dim;
     const void *rms_w; int w_f32;     // null: no RMS norm
-    const float *sumsq;               // null: the RMS statistic is this row's own; else [rows] sums of
+    const float *sumsq;               // null: the RMS statistic is this row's own; else [parts][rows] sums of
+    int sumsq_parts;                  //   squares (the parts added; one per tensor-parallel rank)
+    int64_t sumsq_stride;             //   elements between parts
     int rms_dim;                      //   squares over rms_dim values (all heads, summed across ranks)
     const void *cos, *sin; int cs_f32; // null: no RoPE; [rows][head_dim / 2]
     float eps;

@@ -165,7 +165,37 @@ __global__ void __launch_bounds__(1024) tp_reduce_norm_kernel(TpNormArgs a) {
     }
 }
 
+// One warp per row: the sum of squares of its columns, into every rank's slot.
+__global__ void __launch_bounds__(256) row_sumsq_peers_kernel(PeerRowSums a) {
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= a.rows) return;
+    const int64_t base = r * a.stride + a.col_off;
+    float s = 0.0f;
+    if (!a.src_f32 && a.width % 8 == 0 && base % 8 == 0) {
+        for (int j = lane * 8; j < a.width; j += 256) {
+            float v[8];
+            ld8(a.src, 0, base + j, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s += v[k] * v[k];
+        }
+    } else {
+        for (int j = lane; j < a.width; j += 32) {
+            const float v = a.src_f32 ? reinterpret_cast<const float *>(a.src)[base + j]
+                                      : __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.src)[base + j]);
+            s += v * v;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    if (lane < a.n_outs) a.outs[lane][a.slot + r] = s;
+}
+
 }  // namespace
+
+cudaError_t row_sumsq_peers_launch(const PeerRowSums &a, cudaStream_t st) {
+    row_sumsq_peers_kernel<<<(unsigned)((a.rows + 7) / 8), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t peer_barrier_launch(const PeerFlags &f, int world, int rank, unsigned epoch, int *err, uint64_t limit_ns,
                                 cudaStream_t st) {

@@ -32,6 +32,18 @@ struct TpNormArgs {
     int out_f32, n_outs;
 };
 
+// Row sums of squares of columns [col_off, col_off + width) of src, written
+// at outs[p][slot + r] for every rank p (the slot of this rank).
+struct PeerRowSums {
+    const void *src; int src_f32;
+    int64_t rows, stride, col_off;
+    int width;
+    float *outs[LX2V_MAX_PEERS];
+    int n_outs;
+    int64_t slot;
+};
+cudaError_t row_sumsq_peers_launch(const PeerRowSums &a, cudaStream_t st);
+
 cudaError_t peer_barrier_launch(const PeerFlags &f, int world, int rank, unsigned epoch, int *err, uint64_t limit_ns,
                                 cudaStream_t st);
 bool tp_reduce_norm_supported(int dim);  // dim a multiple of 8, at most 8192

@@ -1695,7 +1695,7 @@ extern "C" lx2v_status lx2v_residual_norm(lx2v_ctx *ctx, lx2v_buf *h, const lx2v
 static lx2v_status head_split_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
                                    size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
                                    const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos, const lx2v_buf *sin,
-                                   float eps, lx2v_buf *out);
+                                   float eps, lx2v_buf *out, size_t parts = 1);
 
 extern "C" lx2v_status lx2v_head_split(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
                                        size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
@@ -1712,6 +1712,16 @@ extern "C" lx2v_status lx2v_head_split_rms(lx2v_ctx *ctx, const lx2v_buf *src, s
         return fail(ctx, LX2V_ERR_INVALID, "head_split_rms needs the RMS weight, the row sums and their width");
     return head_split_impl(ctx, src, rows, src_stride, col_off, heads, head_dim, rms_w, sumsq, rms_dim, cos, sin, eps,
                            out);
+}
+
+extern "C" lx2v_status lx2v_head_split_rms_parts(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
+                                                 size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
+                                                 const lx2v_buf *sumsq, size_t parts, size_t rms_dim,
+                                                 const lx2v_buf *cos, const lx2v_buf *sin, float eps, lx2v_buf *out) {
+    if (!rms_w || !sumsq || rms_dim == 0 || parts == 0)
+        return fail(ctx, LX2V_ERR_INVALID, "head_split_rms_parts needs the RMS weight, the row sums and their width");
+    return head_split_impl(ctx, src, rows, src_stride, col_off, heads, head_dim, rms_w, sumsq, rms_dim, cos, sin, eps,
+                           out, parts);
 }
 
 extern "C" lx2v_status lx2v_row_sumsq(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
@@ -1734,10 +1744,10 @@ extern "C" lx2v_status lx2v_row_sumsq(lx2v_ctx *ctx, const lx2v_buf *src, size_t
 static lx2v_status head_split_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t rows, size_t src_stride,
                                    size_t col_off, size_t heads, size_t head_dim, const lx2v_buf *rms_w,
                                    const lx2v_buf *sumsq, size_t rms_dim, const lx2v_buf *cos, const lx2v_buf *sin,
-                                   float eps, lx2v_buf *out) {
+                                   float eps, lx2v_buf *out, size_t parts) {
     lx2v_status s = enter(ctx);
     if (s) return s;
-    if (sumsq && (sumsq->dtype != LX2V_F32 || sumsq->len < rows))
+    if (sumsq && (sumsq->dtype != LX2V_F32 || sumsq->len < rows * parts))
         return fail(ctx, LX2V_ERR_INVALID, "row sums of squares must be f32, one per row");
     const size_t d = heads * head_dim;
     if (!src || !out || head_dim == 0 || head_dim % 2) return fail(ctx, LX2V_ERR_INVALID, "null src/out or odd head_dim");
@@ -1759,6 +1769,7 @@ static lx2v_status head_split_impl(lx2v_ctx *ctx, const lx2v_buf *src, size_t ro
     a.heads = (int)heads; a.head_dim = (int)head_dim;
     a.rms_w = rms_w ? rms_w->ptr : nullptr; a.w_f32 = is_f32(rms_w);
     a.sumsq = sumsq ? (const float *)sumsq->ptr : nullptr; a.rms_dim = (int)rms_dim;
+    a.sumsq_parts = sumsq ? (int)parts : 0; a.sumsq_stride = (int64_t)rows;
     a.cos = cos ? cos->ptr : nullptr; a.sin = sin ? sin->ptr : nullptr; a.cs_f32 = is_f32(cos);
     a.eps = eps;
     a.out = out->ptr; a.out_f32 = is_f32(out);
@@ -2248,6 +2259,33 @@ extern "C" lx2v_status lx2v_tp_reduce_norm(lx2v_ctx *ctx, lx2v_peers *g, lx2v_bu
     CUDA_TRY(ctx, tp_reduce_norm_launch(a, ctx->stream));
     ctx->launches++;
     CUDA_TRY(ctx, note_uses(ctx, {h, gate_mods, w, b, norm_mods, normed[g->rank]}));
+    return LX2V_OK;
+}
+
+extern "C" lx2v_status lx2v_row_sumsq_peers(lx2v_ctx *ctx, lx2v_peers *g, const lx2v_buf *src, size_t rows,
+                                            size_t src_stride, size_t col_off, size_t width, lx2v_buf *const *outs) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!g || !src || !outs) return fail(ctx, LX2V_ERR_INVALID, "null peer group, source or outputs");
+    if (col_off + width > src_stride || (rows && (rows - 1) * src_stride + col_off + width > src->len))
+        return fail(ctx, LX2V_ERR_INVALID, "row_sumsq columns beyond src");
+    PeerRowSums a;
+    memset(&a, 0, sizeof a);
+    for (int r = 0; r < g->world; ++r) {
+        const lx2v_buf *o = outs[r];
+        if (!o || o->dtype != LX2V_F32 || o->len < rows * (size_t)g->world)
+            return fail(ctx, LX2V_ERR_INVALID, "sums of rank %d: f32 of world x rows elements needed", r);
+        a.outs[r] = (float *)o->ptr;
+    }
+    a.n_outs = g->world;
+    a.slot = (int64_t)g->rank * (int64_t)rows;
+    a.src = src->ptr; a.src_f32 = is_f32(src);
+    a.rows = (int64_t)rows; a.stride = (int64_t)src_stride; a.col_off = (int64_t)col_off; a.width = (int)width;
+    if (rows == 0) return LX2V_OK;
+    OpScope ps(ctx, "row_sumsq_peers");
+    CUDA_TRY(ctx, row_sumsq_peers_launch(a, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {src, outs[g->rank]}));
     return LX2V_OK;
 }
 

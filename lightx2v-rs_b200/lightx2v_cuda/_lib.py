@@ -101,6 +101,9 @@ SIGNATURES = {
     "lx2v_peers_create": (_st, [_vp, ctypes.c_int, ctypes.c_int, _pp, _pp]),
     "lx2v_peers_free": (None, [_vp]),
     "lx2v_peers_barrier": (_st, [_vp, _vp]),
+    "lx2v_row_sumsq_peers": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _pp]),
+    "lx2v_head_split_rms_parts": (_st, [_vp, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp,
+                                        ctypes.c_float, _vp]),
     "lx2v_tp_reduce_norm": (_st, [_vp, _vp, _pp, _vp, _sz, _sz, _sz, _vp, ctypes.c_long, ctypes.c_int, _vp, _vp,
                                   _vp, _sz, _sz, ctypes.c_float, _pp]),
 }

@@ -459,6 +459,20 @@ class CudaBackend:
     def peers_barrier(self, g: "Peers"):
         self._check(self._lib.lx2v_peers_barrier(self._ctx, g.handle))
 
+    def row_sumsq_peers(self, g: "Peers", src: Buf, rows: int, src_stride: int, col_off: int, width: int,
+                        outs: list):
+        """This rank's row sums of squares into its slot of every rank's [world][rows] buffer."""
+        oa = (ctypes.c_void_p * g.world)(*[o.handle.value for o in outs])
+        self._check(self._lib.lx2v_row_sumsq_peers(self._ctx, g.handle, src.handle, rows, src_stride, col_off,
+                                                   width, oa))
+
+    def head_split_rms_parts(self, src: Buf, rows: int, src_stride: int, col_off: int, heads: int, head_dim: int,
+                             rms_w: Buf, sumsq: Buf, parts: int, rms_dim: int, rope, eps: float, out: Buf):
+        cos, sin = (rope[0].handle, rope[1].handle) if rope is not None else (None, None)
+        self._check(self._lib.lx2v_head_split_rms_parts(self._ctx, src.handle, rows, src_stride, col_off, heads,
+                                                        head_dim, rms_w.handle, sumsq.handle, parts, rms_dim, cos,
+                                                        sin, eps, out.handle))
+
     def tp_reduce_norm(self, g: "Peers", parts: list | None, h: Buf, row0: int, row1: int, dim: int,
                        gate_mods: Buf | None, gate: int | None, norm, norm_mods: Buf | None, eps: float,
                        normed: list):

@@ -176,9 +176,9 @@ class TensorParallelDit:
       attention  rank r owns heads [h_r, h_{r+1}): the fused QKV keeps those
                  heads' rows, so q, k, v, the KV cache and the attention are
                  local; the q/k RMS norm spans all heads (cpu lib.rs:433-438),
-                 so each rank's per-row sum of squares over its heads is
-                 all-reduced (f32, one value per row) before head_split
-                 normalises; out1 is split by its input columns and leaves a
+                 so each rank writes its per-row sum of squares over its heads
+                 into every rank's [world][rows] array (peer memory), and
+                 head_split adds the ranks' sums in order; out1 is split by its input columns and leaves a
                  partial product on every rank (bias on rank 0);
       cross-attn q2 and the prompt's K/V the same way (the prompt K RMS too);
                  out2 split like out1;
@@ -285,11 +285,13 @@ class TensorParallelDit:
             caches=[be.kv_cache_new(self.nl, c.head_dim, cap) for _ in self.blocks],
             h=be.alloc(s * d, L.F32), normed=normed, qkv=be.alloc(s * 3 * dl), q=be.alloc(s * dl),
             k=be.alloc(s * dl), v=be.alloc(s * dl), attn=be.alloc(s * dl), q2=be.alloc(s * dl),
-            hid=be.alloc(s * self.ffns[0].local), part=part, ss_q=be.alloc(s, L.F32), ss_k=be.alloc(s, L.F32),
+            hid=be.alloc(s * self.ffns[0].local), part=part,
             patches=be.alloc(s * max(c.patch_in, c.patch_out)),
             rope_cos=be.upload(np.asarray(rope_cos, np.float32), L.F32),
             rope_sin=be.upload(np.asarray(rope_sin, np.float32), L.F32))
         ws.parts, ws.normeds = self._share(part), self._share(normed)
+        # the ranks' per-row q / k sums of squares, [world][rows] on every rank
+        ws.ssq, ws.ssk = (self._share(be.alloc(self.world * s, L.F32)) for _ in range(2))
         flags = be.alloc(self.world, L.F32)  # u32 barrier slots, zeroed
         be.sync()  # zeroed before any peer's first barrier can write it
         ws.peers = be.peers_create(self.rank, self.world, self._share(flags))
@@ -332,12 +334,14 @@ class TensorParallelDit:
         n_blocks = len(self.blocks)
         for li, (bl, m) in enumerate(zip(self.blocks, mods)):
             be.linear(ws.normed, 0, s, bl.qkv.w, bl.qkv.b, L.ACT_NONE, ws.qkv, 0)
-            be.row_sumsq(ws.qkv, s, 3 * dl, 0, dl, ws.ss_q)
-            be.row_sumsq(ws.qkv, s, 3 * dl, dl, dl, ws.ss_k)
-            self._reduce(ws.ss_q, s)
-            self._reduce(ws.ss_k, s)
-            be.head_split_rms(ws.qkv, s, 3 * dl, 0, nl, hd, bl.norm_q1, ws.ss_q, d, rope, eps, ws.q)
-            be.head_split_rms(ws.qkv, s, 3 * dl, dl, nl, hd, bl.norm_k1, ws.ss_k, d, rope, eps, ws.k)
+            be.row_sumsq_peers(g, ws.qkv, s, 3 * dl, 0, dl, ws.ssq)
+            be.row_sumsq_peers(g, ws.qkv, s, 3 * dl, dl, dl, ws.ssk)
+            be.peers_barrier(g)
+            me = self.rank
+            be.head_split_rms_parts(ws.qkv, s, 3 * dl, 0, nl, hd, bl.norm_q1, ws.ssq[me], self.world, d, rope, eps,
+                                    ws.q)
+            be.head_split_rms_parts(ws.qkv, s, 3 * dl, dl, nl, hd, bl.norm_k1, ws.ssk[me], self.world, d, rope, eps,
+                                    ws.k)
             be.head_split(ws.qkv, s, 3 * dl, 2 * dl, nl, hd, None, None, eps, ws.v)
             cache = ws.caches[li]
             be.kv_cache_put(cache, ws.k, ws.v, s, token_temporal)
@@ -347,9 +351,10 @@ class TensorParallelDit:
             step(ws.parts, m, GATE_MSA, ("affine", bl.norm2_w, bl.norm2_b), None)
             k2, v2 = prompt[li]
             be.linear(ws.normed, 0, s, bl.q2.w, bl.q2.b, L.ACT_NONE, ws.q2, 0)
-            be.row_sumsq(ws.q2, s, dl, 0, dl, ws.ss_q)
-            self._reduce(ws.ss_q, s)
-            be.head_split_rms(ws.q2, s, dl, 0, nl, hd, bl.norm_q2, ws.ss_q, d, None, eps, ws.q)
+            # every rank read ssq (its QKV head_split) before the out1 step's barriers
+            be.row_sumsq_peers(g, ws.q2, s, dl, 0, dl, ws.ssq)
+            be.peers_barrier(g)
+            be.head_split_rms_parts(ws.q2, s, dl, 0, nl, hd, bl.norm_q2, ws.ssq[me], self.world, d, None, eps, ws.q)
             be.attention(ws.q, k2, v2, nl, s, c.text_len, hd, ws.attn)
             be.linear(ws.attn, 0, s, bl.out2.w, bl.out2.b, L.ACT_NONE, ws.part, 0)
             step(ws.parts, m, None, ("mod", SCALE_FFN, SHIFT_FFN), m)
