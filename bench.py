@@ -602,6 +602,9 @@ def measure_configs(be, ext, flush, args, peak, hbm, src, which=("c1", "c3")):
         if getattr(args, "m", None):
             ms_ = tuple(m for m in ms_ if m in args.m)
         cases += [("c3", "q4", m, k, n) for (k, n) in ((1536, 8960), (8960, 1536)) for m in ms_]
+        if "c3full" not in which:
+            # NVFP4 (no reference counterpart) on the C3 shape at the chunk's token count
+            cases.append(("nvfp4", "nvfp4", 4680, 1536, 8960))
     weights, hostq = {}, {}
     for _c, fmt, m, k, n in cases:
         if (fmt, k, n) in weights:
@@ -610,6 +613,9 @@ def measure_configs(be, ext, flush, args, peak, hbm, src, which=("c1", "c3")):
             q = quant.Q8.quantize(rng.normal(2, n * k, 0.02), n, k)
             wbytes = n * k + n * (k // q.group) * 4
             weights[(fmt, k, n)] = (be.weight_q8(q), wbytes, "Q8 (reference quantizer)")
+        elif fmt == "nvfp4":
+            q = quant.Nvfp4.quantize(rng.normal(7 + k, n * k, 0.02), n, k)
+            weights[(fmt, k, n)] = (be.weight_nvfp4(q), q.bytes(), "NVFP4 (e2m1 codes, e4m3 block-16 scales)")
         else:
             q = quant.Q4.quantize(rng.normal(7 + k, n * k, 0.02), n, k, 64, True)
             wbytes = n * k // 2 + n * (k // 64) * 4

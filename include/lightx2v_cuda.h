@@ -58,7 +58,7 @@ enum { LX2V_ACT_NONE = 0, LX2V_ACT_GELU_TANH = 1 };
 enum { LX2V_BF16 = 0, LX2V_F32 = 1 };
 
 /* Storage format of a weight matrix (quant.rs:27-43). */
-enum { LX2V_W_BF16 = 0, LX2V_W_Q8 = 1, LX2V_W_Q4 = 2, LX2V_W_FP8 = 3 };
+enum { LX2V_W_BF16 = 0, LX2V_W_Q8 = 1, LX2V_W_Q4 = 2, LX2V_W_FP8 = 3, LX2V_W_NVFP4 = 4 };
 
 typedef struct lx2v_ctx lx2v_ctx;
 typedef struct lx2v_buf lx2v_buf;
@@ -134,6 +134,16 @@ LX2V_API lx2v_status lx2v_weight_q4(lx2v_ctx *ctx, const uint8_t *packed, const 
  * reference's own e4m3_to_f32 (quant.rs:409-420), not hardware e4m3. */
 LX2V_API lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const float *scales, size_t rows,
                             size_t cols, size_t group, lx2v_weight **out);
+/* NVFP4 micro-block weight (no counterpart in the reference, whose design
+ * names it as the next quantisation, docs/design.md:137-145): fp4 e2m1 codes
+ * packed two per byte like Q4 (element 2i in the low nibble), one e4m3 scale
+ * byte per 16 consecutive values of a row [rows * cols / 16] and one f32
+ * global scale. w = e2m1(code) * (e4m3(block scale) * global scale), the
+ * bracket rounded to f32 once (OCP e4m3). cols a multiple of 32. Linear runs
+ * it through the two-pass kernel (bf16 decode, then the CTA-pair GEMM) or
+ * the generic kernel; lx2v_weight_dequant_f32 gives the exact f32 values. */
+LX2V_API lx2v_status lx2v_weight_nvfp4(lx2v_ctx *ctx, const uint8_t *packed, const uint8_t *block_scales,
+                                       float global_scale, size_t rows, size_t cols, lx2v_weight **out);
 LX2V_API void lx2v_weight_free(lx2v_ctx *ctx, lx2v_weight *w);
 /* Format, rows, cols and group of a weight. */
 LX2V_API lx2v_status lx2v_weight_info(lx2v_ctx *ctx, const lx2v_weight *w, int *format, size_t *rows,

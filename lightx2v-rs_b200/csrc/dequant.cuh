@@ -36,13 +36,13 @@
 
 namespace lx2v {
 
-enum : int { FMT_BF16 = 0, FMT_Q8 = 1, FMT_Q4 = 2, FMT_FP8 = 3 };
+enum : int { FMT_BF16 = 0, FMT_Q8 = 1, FMT_Q4 = 2, FMT_FP8 = 3, FMT_NVFP4 = 4 };
 
 struct WeightView {
     int fmt;
     int n, k, group;
     const uint8_t *codes;
-    const float *scales_t;  // Q8 / FP8: [G][N]
+    const float *scales_t;  // Q8 / FP8: [G][N]; NVFP4: [K/16][N] effective scales (block e4m3 x global)
     const uint32_t *sz_t;   // Q4: [G][N], half2 bits (lo = scale, hi = zero)
     const uint8_t *flags;   // FP8: [ceil(K/32)][N]
 };
@@ -203,6 +203,31 @@ __device__ __forceinline__ void q4_products(const uint2 raw, float s, float z, f
     }
 }
 
+// NVFP4 (fp4 e2m1 codes, one e4m3 scale per 16 values, one f32 global scale;
+// no counterpart in the reference, which names it as its next quantisation):
+// a code's value {0, 0.5, 1, 1.5, 2, 3, 4, 6} (bit 3 the sign), built as an
+// f32 bit pattern; the weight is value x (block scale x global scale), the
+// bracket formed in f32 once per block at upload.
+__host__ __device__ __forceinline__ float e2m1_value(uint32_t c) {
+    const uint32_t m = c & 7u;
+    const uint32_t bits = m < 2u ? (m ? 0x3F000000u : 0u) : ((((m >> 1) + 126u) << 23) | ((m & 1u) << 22));
+    const uint32_t v = bits | ((c & 8u) << 28);
+    float f;
+    memcpy(&f, &v, 4);
+    return f;
+}
+// 16 packed codes (element 2i in the low nibble, as Q4 packs them) -> value x s.
+__device__ __forceinline__ void nvfp4_products(const uint2 raw, float s, float2 (&p)[8]) {
+    const uint32_t w[2] = {raw.x, raw.y};
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t b = (w[j] >> (8 * i)) & 0xFFu;
+            p[4 * j + i] = make_float2(e2m1_value(b & 0xFu) * s, e2m1_value(b >> 4) * s);
+        }
+}
+
 __device__ __forceinline__ void q4_scale_zero(uint32_t sz, float &s, float &z) {
     const __half2 h = *reinterpret_cast<const __half2 *>(&sz);
     s = __low2float(h);
@@ -247,6 +272,8 @@ __device__ __forceinline__ void unit_to_bf16(const uint4 raw, const uint4 raw2, 
         q8_products(raw, s, p);
     } else if (FMT == FMT_Q4) {
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
+    } else if (FMT == FMT_NVFP4) {
+        nvfp4_products(make_uint2(raw.x, raw.y), s, p);
     } else {
         if (fp8_mode != 0) {
             const PackedUnit u = fp8_unit_special(raw, s, fp8_mode);
@@ -268,6 +295,8 @@ __device__ __forceinline__ void unit_to_f32(const uint4 raw, float s, float z, i
         q8_products(raw, s, p);
     } else if (FMT == FMT_Q4) {
         q4_products(make_uint2(raw.x, raw.y), s, z, p);
+    } else if (FMT == FMT_NVFP4) {
+        nvfp4_products(make_uint2(raw.x, raw.y), s, p);
     } else {
         if (fp8_mode != 2) {
             fp8_magnitudes(raw, s, p);
@@ -304,6 +333,8 @@ __device__ __forceinline__ float dq_elem(const WeightView &w, int64_t n, int64_t
             const uint32_t c = (w.codes[i >> 1] >> (4 * (i & 1))) & 0xFu;
             return ((float)c - z) * s;
         }
+        case FMT_NVFP4:
+            return e2m1_value((w.codes[i >> 1] >> (4 * (i & 1))) & 0xFu) * w.scales_t[g * w.n + n];
         default:
             return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(w.codes)[i]);
     }
@@ -316,7 +347,8 @@ __host__ __device__ inline bool unit_path_ok(int fmt, int k, int group) {
     switch (fmt) {
         case FMT_Q8:
         case FMT_FP8: return k % 16 == 0;
-        case FMT_Q4: return k % 32 == 0;
+        case FMT_Q4:
+        case FMT_NVFP4: return k % 32 == 0;
         default: return k % 8 == 0;
     }
 }

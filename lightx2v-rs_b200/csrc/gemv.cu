@@ -281,6 +281,7 @@ bool gemv_supported(const LinearArgs &a) {
                    (a.K % 64 == 0 && a.group % 64 == 0 && a.K % a.group == 0 && a.K <= 49152);
         case FMT_Q8:
         case FMT_FP8: return a.K % 64 == 0 && a.group % 16 == 0;
+        case FMT_NVFP4: return false;  // two-pass or generic kernel
         default: return a.K % 64 == 0;
     }
 }

@@ -82,6 +82,9 @@ __global__ void dequant_units_kernel(WeightView w, float *out) {
             float s, z;
             q4_scale_zero(w.sz_t[g * w.n + n], s, z);
             unit_to_f32<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), s, z, 0, v);
+        } else if (FMT == FMT_NVFP4) {
+            const uint2 raw = *reinterpret_cast<const uint2 *>(w.codes + base / 2);
+            unit_to_f32<FMT_NVFP4>(make_uint4(raw.x, raw.y, 0, 0), w.scales_t[g * w.n + n], 0.0f, 0, v);
         } else if (FMT == FMT_BF16) {
             const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(w.codes) + base;
 #pragma unroll
@@ -130,6 +133,10 @@ __global__ void __launch_bounds__(256) dequant_bf16_kernel(WeightView w, __nv_bf
             float s, z;
             q4_scale_zero(__ldg(w.sz_t + g * w.n + n), s, z);
             unit_to_bf16<FMT_Q4>(make_uint4(raw.x, raw.y, 0, 0), make_uint4(0, 0, 0, 0), s, z, 0, o);
+        } else if (FMT == FMT_NVFP4) {
+            const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(w.codes + base / 2));
+            unit_to_bf16<FMT_NVFP4>(make_uint4(raw.x, raw.y, 0, 0), make_uint4(0, 0, 0, 0),
+                                    __ldg(w.scales_t + g * w.n + n), 0.0f, 0, o);
         } else {
             const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(w.codes + base));
             const int mode = FMT == FMT_FP8 ? __ldg(w.flags + (int64_t)(k0 / 32) * w.n + n) : 0;
@@ -161,6 +168,7 @@ cudaError_t dequant_bf16_launch(int fmt, const uint8_t *codes, const float *scal
     switch (fmt) {
         case FMT_Q8: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_Q8>, w, out);
         case FMT_Q4: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_Q4>, w, out);
+        case FMT_NVFP4: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_NVFP4>, w, out);
         default: return cudaLaunchKernelEx(&cfg, dequant_bf16_kernel<FMT_FP8>, w, out);
     }
 }
@@ -176,6 +184,7 @@ cudaError_t dequant_f32_launch(int fmt, const uint8_t *codes, const float *scale
             case FMT_Q8: dequant_units_kernel<FMT_Q8><<<g, 256, 0, st>>>(w, out); break;
             case FMT_Q4: dequant_units_kernel<FMT_Q4><<<g, 256, 0, st>>>(w, out); break;
             case FMT_FP8: dequant_units_kernel<FMT_FP8><<<g, 256, 0, st>>>(w, out); break;
+            case FMT_NVFP4: dequant_units_kernel<FMT_NVFP4><<<g, 256, 0, st>>>(w, out); break;
             default: dequant_units_kernel<FMT_BF16><<<g, 256, 0, st>>>(w, out); break;
         }
     } else {

@@ -21,6 +21,7 @@
 #include <mutex>
 #include <string>
 #include <vector>
+#include <limits>
 
 #include "../../include/lightx2v_cuda.h"
 #include "dequant.cuh"
@@ -719,6 +720,36 @@ extern "C" lx2v_status lx2v_weight_fp8(lx2v_ctx *ctx, const uint8_t *q, const fl
     return LX2V_OK;
 }
 
+// e4m3 as the OCP FP8 format defines it (NVFP4 block scales): exponent-field-0
+// codes are m/8 * 2^-6, 0x7F / 0xFF NaN.
+static float e4m3_ocp(uint8_t c) {
+    const float sign = (c & 0x80u) ? -1.0f : 1.0f;
+    const int e = (c >> 3) & 0xF, m = c & 7;
+    if (e == 0xF && m == 7) return std::numeric_limits<float>::quiet_NaN();
+    if (e == 0) return sign * ((float)m / 8.0f) * 0x1p-6f;
+    return sign * (1.0f + (float)m / 8.0f) * std::ldexp(1.0f, e - 7);
+}
+
+extern "C" lx2v_status lx2v_weight_nvfp4(lx2v_ctx *ctx, const uint8_t *packed, const uint8_t *block_scales,
+                                         float global_scale, size_t rows, size_t cols, lx2v_weight **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !packed || !block_scales) return fail(ctx, LX2V_ERR_INVALID, "null codes, scales or output");
+    if ((s = check_shape(ctx, rows, cols, 16))) return s;
+    if (cols % 32 != 0) return fail(ctx, LX2V_ERR_UNSUPPORTED, "NVFP4 rows of a multiple of 32 values");
+    OpScope ps(ctx, "weight_nvfp4");
+    auto *w = new lx2v_weight();
+    w->fmt = LX2V_W_NVFP4; w->rows = rows; w->cols = cols; w->group = 16;
+    const size_t G = cols / 16;
+    std::vector<float> eff(rows * G);  // block scale x global scale, one f32 rounding
+    for (size_t i = 0; i < rows * G; ++i) eff[i] = e4m3_ocp(block_scales[i]) * global_scale;
+    auto st = transpose_scales(eff.data(), rows, G);
+    if ((s = upload_codes_scales(ctx, w, packed, rows * cols / 2, &st, nullptr))) { weight_release(w); return s; }
+    if ((s = plan_workspaces(ctx, LX2V_W_NVFP4, rows, cols))) { weight_release(w); return s; }
+    *out = w;
+    return LX2V_OK;
+}
+
 extern "C" lx2v_status lx2v_weight_q4(lx2v_ctx *ctx, const uint8_t *packed, const float *scales,
                                       const float *zeros, size_t rows, size_t cols, size_t group,
                                       lx2v_weight **out) {
@@ -900,6 +931,11 @@ static lx2v_status linear_queue(lx2v_ctx *ctx, const char *opname, const lx2v_bu
     const bool ss_ok = x->dtype == LX2V_BF16 && K % 16 == 0 && N % 16 == 0 &&
                        unit_path_ok(w->fmt, (int)K, (int)w->group) && rows >= 16;
     int path = ctx->path;
+    if (path == 0 && w->fmt == LX2V_W_NVFP4) {
+        // NVFP4 runs the two-pass linear (decode to bf16, then the CTA-pair
+        // GEMM) at any token count, else the generic kernel
+        path = ss_ok && N >= 256 && K % 64 == 0 ? 5 : 3;
+    }
     if (path == 0) {
         if (rows <= 16 && gemv_ok) path = 2;
         else if (ss_ok && N >= 256 && K % 64 == 0 &&  // whole 64-wide k-blocks, the shapes it is tested on

@@ -27,7 +27,7 @@ ACT_NONE = 0
 ACT_GELU_TANH = 1
 BF16 = 0
 F32 = 1
-W_BF16, W_Q8, W_Q4, W_FP8 = 0, 1, 2, 3
+W_BF16, W_Q8, W_Q4, W_FP8, W_NVFP4 = 0, 1, 2, 3, 4
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -55,6 +55,7 @@ SIGNATURES = {
     "lx2v_weight_q8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
     "lx2v_weight_q4": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _pp]),
     "lx2v_weight_fp8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
+    "lx2v_weight_nvfp4": (_st, [_vp, _vp, _vp, ctypes.c_float, _sz, _sz, _pp]),
     "lx2v_weight_free": (None, [_vp, _vp]),
     "lx2v_weight_info": (_st, [_vp, _vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_sz),
                                ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),

@@ -226,6 +226,16 @@ class CudaBackend:
                                               q.rows, q.cols, q.group, ctypes.byref(h)))
         return Weight(self, h.value, q.rows, q.cols, L.W_FP8, q.group)
 
+    def weight_nvfp4(self, q) -> Weight:
+        """NVFP4 weight (no reference counterpart): packed e2m1 codes, e4m3 block
+        scales, f32 global scale (lightx2v_cuda.quant.Nvfp4)."""
+        packed = np.ascontiguousarray(q.q, np.uint8)
+        scales = np.ascontiguousarray(q.scales, np.uint8)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_weight_nvfp4(self._ctx, packed.ctypes.data, scales.ctypes.data,
+                                                float(q.global_scale), q.rows, q.cols, ctypes.byref(h)))
+        return Weight(self, h.value, q.rows, q.cols, L.W_NVFP4, 16)
+
     def weight_dequant_f32(self, w: Weight) -> np.ndarray:
         """Test hook: the device's decode of `w` as f32 [rows*cols]."""
         out = np.empty(w.rows * w.cols, np.float32)

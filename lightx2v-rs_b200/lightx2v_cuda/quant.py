@@ -321,6 +321,83 @@ class Fp8E4M3:
         return self.q.size + 4 * self.scales.size
 
 
+# ---- NVFP4 (no counterpart in the reference) ----------------------------------------
+# The reference names NVFP4 (micro-block fp4 e2m1 codes, one e4m3 scale per 16
+# values, one f32 global scale) as its next quantisation (docs/design.md:
+# 137-145, quant.rs:13-16, 361-364) but does not implement it, so this is the
+# format's definition here: w = e2m1(code) * (e4m3(block scale) * global), the
+# bracket rounded to f32 once, e4m3 as the OCP format (exponent-field-0 codes
+# are subnormals m/8 * 2^-6). The device decode (lx2v_weight_nvfp4) matches
+# `dequantize` bit for bit.
+E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+NVFP4_BLOCK = 16
+
+
+def e4m3_ocp_table() -> np.ndarray:
+    """The 256 OCP e4m3 codes as f32 (0x7F / 0xFF NaN)."""
+    c = np.arange(256, dtype=np.uint32)
+    sign = np.where(c & 0x80, -1.0, 1.0)
+    e, m = (c >> 3) & 0xF, (c & 7).astype(np.float64)
+    v = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e.astype(np.float64) - 7))
+    v = (sign * v).astype(np.float32)
+    v[(c & 0x7F) == 0x7F] = np.nan
+    return v
+
+
+def _nearest_code(x: np.ndarray, values: np.ndarray) -> np.ndarray:
+    """Index of the nearest entry of the ascending `values` (ties to the lower)."""
+    hi = np.clip(np.searchsorted(values, x), 1, len(values) - 1)
+    lo = hi - 1
+    return np.where(np.abs(x - values[lo]) <= np.abs(values[hi] - x), lo, hi)
+
+
+@dataclass
+class Nvfp4:
+    q: np.ndarray          # u8 packed, element 2i in the low nibble [rows * cols / 2]
+    scales: np.ndarray     # u8 e4m3 block scales [rows * cols / 16]
+    global_scale: float
+    rows: int
+    cols: int
+
+    @staticmethod
+    def quantize(data, rows: int, cols: int) -> "Nvfp4":
+        """The usual two-level recipe: global = amax / (6 * 448), block scale
+        = e4m3(block amax / 6 / global) (nearest, at most 448), code = nearest
+        e2m1 of w / (block scale * global)."""
+        assert cols % 32 == 0, cols
+        w = np.asarray(data, np.float32).reshape(rows, cols)
+        amax = float(np.max(np.abs(w))) if w.size else 0.0
+        gs = np.float32(amax / (6.0 * 448.0)) if amax > 0 else np.float32(1.0)
+        blocks = w.reshape(rows, cols // NVFP4_BLOCK, NVFP4_BLOCK)
+        bmax = np.max(np.abs(blocks), axis=2)
+        table = e4m3_ocp_table()
+        pos = table[:0x7F]                        # codes 0x00..0x7E, ascending 0 .. 448
+        want = np.minimum(bmax / np.float32(6.0) / gs, np.float32(448.0)).astype(np.float32)
+        sc = _nearest_code(want, pos).astype(np.uint8)
+        eff = (pos[sc] * gs).astype(np.float32)  # block scale x global, one f32 rounding
+        safe = np.where(eff > 0, eff, np.float32(1.0))
+        r = (blocks / safe[:, :, None]).astype(np.float32)
+        mag = _nearest_code(np.minimum(np.abs(r), np.float32(6.0)), E2M1_VALUES).astype(np.uint8)
+        code = (mag | np.where(r < 0, 8, 0).astype(np.uint8)).reshape(-1)
+        code[np.repeat(eff.reshape(-1) == 0, NVFP4_BLOCK)] = 0
+        packed = (code[0::2] | (code[1::2] << 4)).astype(np.uint8)
+        return Nvfp4(packed, sc.reshape(-1), float(gs), rows, cols)
+
+    def codes(self) -> np.ndarray:
+        c = np.empty(self.rows * self.cols, np.uint8)
+        c[0::2], c[1::2] = self.q & 0xF, self.q >> 4
+        return c
+
+    def dequantize(self) -> np.ndarray:
+        c = self.codes().astype(np.int64)
+        val = np.where(c & 8, -1.0, 1.0).astype(np.float32) * E2M1_VALUES[c & 7]
+        eff = (e4m3_ocp_table()[self.scales] * np.float32(self.global_scale)).astype(np.float32)
+        return (val.reshape(-1, NVFP4_BLOCK) * eff[:, None]).astype(np.float32).reshape(-1)
+
+    def bytes(self) -> int:
+        return self.q.size + self.scales.size + 4
+
+
 # ---- WeightQuant (quant.rs:27-132) ------------------------------------------------
 @dataclass(frozen=True)
 class WeightQuant:

@@ -689,3 +689,43 @@ def test_stream_k_linear_replays_in_a_cuda_graph(be, oracle, path):
         be.set_split_mode(0)
     want = oracle.linear(be.download(x_sets[0]), M, q.dequantize(), N, K, bias=be.download(bb), act=1, threads=8)
     assert rel_l2(wants[0].reshape(M, N), want) <= REL_L2
+
+
+# ---- NVFP4 (no reference counterpart; the format's own definition as the oracle) -----------
+def test_nvfp4_device_decode_is_bit_exact(be, oracle):
+    rows, cols = 96, 1536
+    q = quant.Nvfp4.quantize(oracle.normal(161, rows * cols, 0.02), rows, cols)
+    got = be.weight_dequant_f32(be.weight_nvfp4(q))
+    assert np.array_equal(got.view(np.uint32), q.dequantize().view(np.uint32))
+
+
+@pytest.mark.parametrize("M,N,K", [(4680, 1536, 1536), (300, 8960, 1536), (40, 200, 512), (4, 512, 256)])
+def test_nvfp4_linear_matches_oracle(be, oracle, M, N, K):
+    # two-pass (bf16 decode + CTA-pair GEMM) for the first two, the generic kernel for the others
+    q = quant.Nvfp4.quantize(oracle.normal(171 + N, N * K, 0.02), N, K)
+    dw = be.weight_nvfp4(q)
+    x = oracle.normal(172, (M + 1) * K)
+    b = oracle.normal(173, N, 0.01)
+    xb, bb = be.upload(x), be.upload(b, F32)
+    yb = be.alloc(M * N, F32)
+    be.linear(xb, 1, M, dw, bb, Act.GELU_TANH, yb, 0)
+    y = be.download(yb).reshape(M, N)
+    rows = sampled_rows(M, 24)
+    want = np.stack([oracle.linear(x, 1, q.dequantize(), N, K, bias=b, act=1, x_row=1 + int(r), threads=8)[0]
+                     for r in rows])
+    assert rel_l2(y[rows], want) <= REL_L2
+
+
+def test_nvfp4_is_refused_by_the_kernels_that_do_not_take_it(be, oracle):
+    from lightx2v_cuda import _lib as L
+    q = quant.Nvfp4.quantize(oracle.normal(181, 512 * 512, 0.02), 512, 512)
+    dw = be.weight_nvfp4(q)
+    xb, yb = be.upload(oracle.normal(182, 512 * 512)), be.alloc(512 * 512, F32)
+    try:
+        for path in (1, 2, 4):
+            be.set_linear_path(path)
+            with pytest.raises(L.Lx2vError) as e:
+                be.linear(xb, 0, 512, dw, None, Act.NONE, yb, 0)
+            assert e.value.status == L.ERR_UNSUPPORTED
+    finally:
+        be.set_linear_path(0)

@@ -117,3 +117,31 @@ def test_fp8_concat_rejects_mismatched_parts(oracle):
     b = quant.Fp8E4M3.quantize(oracle.normal(2, 4 * 128), 4, 128)
     with pytest.raises(AssertionError):
         quant.Fp8E4M3.concat([a, b])
+
+
+# ---- NVFP4 (no counterpart in the reference: the format's definition) ---------------------
+def test_nvfp4_codes_lie_on_the_e2m1_grid_times_the_block_scale(oracle):
+    rows, cols = 48, 512
+    w = oracle.normal(61, rows * cols, 0.02)
+    q = quant.Nvfp4.quantize(w, rows, cols)
+    assert q.q.size == rows * cols // 2 and q.scales.size == rows * cols // 16
+    d = q.dequantize().reshape(-1, 16)
+    eff = (quant.e4m3_ocp_table()[q.scales] * np.float32(q.global_scale)).astype(np.float32)
+    c = q.codes().astype(np.int64).reshape(-1, 16)
+    val = np.where(c & 8, -1.0, 1.0).astype(np.float32) * quant.E2M1_VALUES[c & 7]
+    assert np.array_equal(d, (val * eff[:, None]).astype(np.float32))  # w = e2m1(code) x (block x global)
+    ratio = val
+    # nearest grid point: the error is at most half the widest gap (6 - 4) times the scale
+    err = np.abs(d - np.asarray(w, np.float32).reshape(-1, 16))
+    assert np.all(err <= eff[:, None] * 1.0 + 1e-12)
+    assert np.linalg.norm(d.reshape(-1) - w) / np.linalg.norm(w) < 0.12
+    # the largest value of a block uses (nearly) the top of the e2m1 range
+    assert np.max(np.abs(ratio)) == 6.0
+
+
+def test_nvfp4_zero_weight_and_ocp_e4m3_table():
+    q = quant.Nvfp4.quantize(np.zeros(4 * 64, np.float32), 4, 64)
+    assert np.all(q.dequantize() == 0)
+    t = quant.e4m3_ocp_table()
+    assert t[0x7E] == 448.0 and t[0x08] == 2.0 ** -6 and t[0x01] == 2.0 ** -9
+    assert np.isnan(t[0x7F]) and np.isnan(t[0xFF]) and t[0xBE] == -1.75
