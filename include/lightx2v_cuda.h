@@ -201,6 +201,27 @@ LX2V_API lx2v_status lx2v_causal_attention_temporal(lx2v_ctx *ctx, const lx2v_bu
                                                     size_t head_dim, const int32_t *tq, const int32_t *tk,
                                                     lx2v_buf *out);
 
+/* ---- sparse attention (backend.rs:309-331) ------------------------------- */
+/* Backend::sparse_prepare / sparse_attention: LightX2V video sparse attention
+ * over a (T, H, W) token grid tiled into 4x4x4 cubes (crates/lightx2v-core/
+ * src/sparse.rs), computed as the CPU reference does (cpu lib.rs:496-606):
+ * coarse attention over mean-pooled tiles, the top-k key tiles per query tile
+ * by the coarse scores (ties to the lower tile), fine attention to the
+ * selected tiles' tokens, out = coarse * gate + fine. lx2v_sparse_prepare
+ * takes the reference's TilePlan as is: slot_src [num_tiles * 64] (source
+ * token per slot, 0xFFFFFFFF padding), block_sizes [num_tiles], the token
+ * count, the heads and head_dim of the calls, SparseSpec's topk and scale.
+ * q, k, v, gate are [heads, seq, head_dim], out [seq, heads * head_dim]. The
+ * fine stage runs the attention kernels with a per-head token mask, so
+ * heads * seq^2 bits must stay within 512 MiB (LX2V_ERR_UNSUPPORTED beyond). */
+typedef struct lx2v_sparse lx2v_sparse;
+LX2V_API lx2v_status lx2v_sparse_prepare(lx2v_ctx *ctx, const uint32_t *slot_src, const uint32_t *block_sizes,
+                                         size_t num_tiles, size_t seq, size_t heads, size_t head_dim, size_t topk,
+                                         float scale, lx2v_sparse **out);
+LX2V_API void lx2v_sparse_free(lx2v_ctx *ctx, lx2v_sparse *sp);
+LX2V_API lx2v_status lx2v_sparse_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k, const lx2v_buf *v,
+                                           const lx2v_buf *gate, const lx2v_sparse *sp, lx2v_buf *out);
+
 /* ---- norms, head_split, patchify, dmd_step (backend.rs:214-273, 392-428) -- */
 /* NormKind (backend.rs:47-53): kind 0 = Affine { w, b } (out = LN(x) * w + b,
  * w and b of dim elements), 1 = Mod { scale, shift } (out = LN(x) *

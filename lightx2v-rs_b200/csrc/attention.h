@@ -23,6 +23,7 @@ struct alignas(64) AttnParams {
     int mask_mode;        // ATT_MASK_*
     const uint32_t *mask_bits;  // [sq][mask_words] (bit k % 32 of word k / 32: key k visible)
     int mask_words;
+    int64_t mask_head_stride;   // words between the heads' masks (0: one mask for all heads)
     const int *tq;        // [sq] temporal index of each query (mask_mode TEMPORAL)
     const int *tk;        // [sk] temporal index of each key
     const int2 *tk_range; // [ceil(sk / 128)] (min, max) tk of each key block
@@ -43,6 +44,7 @@ struct AttnSimtParams {
     int mask_mode;
     const uint32_t *mask_bits;
     int mask_words;
+    int64_t mask_head_stride;
     const int *tq, *tk;
 };
 

@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                     uint32_t w = 0;
                     const int kc = k0 + c * 32;
                     if (p.mask_mode == ATT_MASK_BITS && q_ok && kc < p.sk) {
-                        w = __ldg(p.mask_bits + (int64_t)q * p.mask_words + (kc >> 5));
+                        w = __ldg(p.mask_bits + h * p.mask_head_stride + (int64_t)q * p.mask_words + (kc >> 5));
                     } else if (p.mask_mode == ATT_MASK_TEMPORAL && q_ok) {
 #pragma unroll 1
                         for (int b = 0; b < 32; ++b)
@@ -440,7 +440,8 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(AttnSimtParams p) {
     for (int k = threadIdx.x; k < p.sk; k += blockDim.x) {
         bool vis = true;
         if (p.mask_mode == ATT_MASK_TEMPORAL) vis = p.tk[k] <= p.tq[q];
-        else if (p.mask_mode == ATT_MASK_BITS) vis = (p.mask_bits[(int64_t)q * p.mask_words + (k >> 5)] >> (k & 31)) & 1u;
+        else if (p.mask_mode == ATT_MASK_BITS)
+            vis = (p.mask_bits[h * p.mask_head_stride + (int64_t)q * p.mask_words + (k >> 5)] >> (k & 31)) & 1u;
         float s = -INFINITY;
         if (vis) {
             const int64_t kbase = ((int64_t)h * p.k_rows + k) * D;

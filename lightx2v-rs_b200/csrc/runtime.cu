@@ -30,6 +30,7 @@
 #include "kvcache.h"
 #include "dit_ops.h"
 #include "peer.h"
+#include "sparse.h"
 
 using namespace lx2v;
 
@@ -1177,6 +1178,9 @@ struct AttnMaskArgs {
     const uint8_t *mask = nullptr;  // [sq][sk] bool, nonzero = allowed
     const int32_t *tq = nullptr;    // [sq]
     const int32_t *tk = nullptr;    // [sk]
+    // ATT_MASK_BITS already on the device: [heads][sq][ceil(sk/32)] words
+    // (sparse attention's per-head selection), instead of the host bool mask
+    const uint32_t *dev_bits = nullptr;
 };
 
 // q [heads][q_rows][d] (the first sq rows of each head are the queries),
@@ -1196,7 +1200,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     const size_t vt_bytes = tc ? align_up(heads * 128 * sk_pad * 2, 256) : 0;
     const size_t words = (sk + 31) / 32;
     size_t mask_bytes = 0;
-    if (m.mode == ATT_MASK_BITS) mask_bytes = sq * words * 4;
+    if (m.mode == ATT_MASK_BITS && !m.dev_bits) mask_bytes = sq * words * 4;
     else if (m.mode == ATT_MASK_TEMPORAL) mask_bytes = (sq + sk) * 4 + (n_qt + n_kb) * 8 + n_qt * 4;
     lx2v_status s = ensure_att_workspace(ctx, vt_bytes + align_up(mask_bytes, 256) + 256);
     if (s) return s;
@@ -1206,7 +1210,9 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     const int *tq_dev = nullptr, *tk_dev = nullptr;
     const int2 *tqr_dev = nullptr, *tkr_dev = nullptr;
     const int *order_dev = nullptr;
-    if (m.mode == ATT_MASK_BITS) {
+    if (m.mode == ATT_MASK_BITS && m.dev_bits) {
+        bits_dev = m.dev_bits;
+    } else if (m.mode == ATT_MASK_BITS) {
         void *stage = nullptr;
         if ((s = att_host_staging(ctx, mask_bytes, &stage))) return s;
         uint32_t *bits = (uint32_t *)stage;
@@ -1284,6 +1290,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
         p.mask_mode = m.mode;
         p.mask_bits = bits_dev; p.mask_words = (int)words;
+        p.mask_head_stride = m.dev_bits ? (int64_t)(sq * words) : 0;
         p.tq = tq_dev; p.tk = tk_dev; p.tq_range = tqr_dev; p.tk_range = tkr_dev;
         p.tile_order = order_dev;
         p.err = ctx->err_dev;
@@ -1305,6 +1312,7 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     p.heads = (int)heads; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
     p.q_rows = (int)q_rows; p.k_rows = (int)k_rows;
     p.mask_mode = m.mode; p.mask_bits = bits_dev; p.mask_words = (int)words;
+    p.mask_head_stride = m.dev_bits ? (int64_t)(sq * words) : 0;
     p.tq = tq_dev; p.tk = tk_dev;
     CUDA_TRY(ctx, attention_simt_launch(p, ctx->stream));
     ctx->launches++;
@@ -2322,6 +2330,123 @@ extern "C" lx2v_status lx2v_row_sumsq_peers(lx2v_ctx *ctx, lx2v_peers *g, const 
     CUDA_TRY(ctx, row_sumsq_peers_launch(a, ctx->stream));
     ctx->launches++;
     CUDA_TRY(ctx, note_uses(ctx, {src, outs[g->rank]}));
+    return LX2V_OK;
+}
+
+// ---- sparse attention (backend.rs:309-331, crates/lightx2v-core/src/sparse.rs) ---------------
+struct lx2v_sparse {
+    int heads = 0, seq = 0, d = 0, nt = 0, topk = 0, sel_words = 0, words = 0;
+    float scale = 0.0f;
+    uint32_t *slot_src = nullptr;
+    int *block_sizes = nullptr, *token_tile = nullptr;
+    float *pooled = nullptr;  // cq, ck, cv, coarse_out: 4 x [heads][nt][d]
+    uint32_t *sel = nullptr, *bits = nullptr;
+};
+
+static void sparse_release(lx2v_sparse *sp) {
+    if (!sp) return;
+    cudaFree(sp->slot_src); cudaFree(sp->block_sizes); cudaFree(sp->token_tile);
+    cudaFree(sp->pooled); cudaFree(sp->sel); cudaFree(sp->bits);
+    delete sp;
+}
+
+// The fine stage's per-head token mask is heads x seq x seq bits.
+static constexpr size_t SPARSE_MASK_MAX_BYTES = 512ull << 20;
+
+extern "C" lx2v_status lx2v_sparse_prepare(lx2v_ctx *ctx, const uint32_t *slot_src, const uint32_t *block_sizes,
+                                           size_t num_tiles, size_t seq, size_t heads, size_t head_dim, size_t topk,
+                                           float scale, lx2v_sparse **out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!out || !slot_src || !block_sizes || num_tiles == 0 || seq == 0 || heads == 0 || head_dim == 0 ||
+        topk == 0 || topk > num_tiles)
+        return fail(ctx, LX2V_ERR_INVALID, "bad sparse plan (tiles %zu, seq %zu, heads %zu, topk %zu)", num_tiles, seq,
+                    heads, topk);
+    const size_t words = (seq + 31) / 32;
+    if (heads * seq * words * 4 > SPARSE_MASK_MAX_BYTES || num_tiles > 16384 || seq > (1u << 30))
+        return fail(ctx, LX2V_ERR_UNSUPPORTED, "sparse attention over %zu tokens x %zu heads: the fine-stage mask "
+                    "would exceed %zu MiB", seq, heads, SPARSE_MASK_MAX_BYTES >> 20);
+    // host checks of the plan: every token in exactly one slot, tile sizes as the slots say
+    std::vector<int> token_tile(seq, -1), sizes(num_tiles);
+    for (size_t t = 0; t < num_tiles; ++t) {
+        if (block_sizes[t] > (uint32_t)VSA_TILE) return fail(ctx, LX2V_ERR_INVALID, "tile %zu holds > 64 tokens", t);
+        sizes[t] = (int)block_sizes[t];
+        for (size_t i = 0; i < VSA_TILE; ++i) {
+            const uint32_t tok = slot_src[t * VSA_TILE + i];
+            const bool real = i < block_sizes[t];
+            if (real != (tok != 0xFFFFFFFFu) || (real && (tok >= seq || token_tile[tok] >= 0)))
+                return fail(ctx, LX2V_ERR_INVALID, "slot %zu of tile %zu disagrees with the plan", i, t);
+            if (real) token_tile[tok] = (int)t;
+        }
+    }
+    for (size_t i = 0; i < seq; ++i)
+        if (token_tile[i] < 0) return fail(ctx, LX2V_ERR_INVALID, "token %zu is in no tile", i);
+    auto *sp = new lx2v_sparse();
+    sp->heads = (int)heads; sp->seq = (int)seq; sp->d = (int)head_dim; sp->nt = (int)num_tiles;
+    sp->topk = (int)topk; sp->scale = scale; sp->words = (int)words; sp->sel_words = (int)((num_tiles + 31) / 32);
+    const size_t hnd = heads * num_tiles * head_dim;
+    cudaError_t e = cudaMalloc(&sp->slot_src, num_tiles * VSA_TILE * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sp->block_sizes, num_tiles * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sp->token_tile, seq * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sp->pooled, 4 * hnd * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sp->sel, heads * num_tiles * sp->sel_words * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sp->bits, heads * seq * words * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(sp->slot_src, slot_src, num_tiles * VSA_TILE * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(sp->block_sizes, sizes.data(), num_tiles * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(sp->token_tile, token_tile.data(), seq * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        sparse_release(sp);
+        return fail(ctx, e == cudaErrorMemoryAllocation ? LX2V_ERR_OOM : LX2V_ERR_CUDA, "sparse state: %s",
+                    cudaGetErrorString(e));
+    }
+    *out = sp;
+    return LX2V_OK;
+}
+
+extern "C" void lx2v_sparse_free(lx2v_ctx *ctx, lx2v_sparse *sp) {
+    if (!sp) return;
+    if (ctx) {
+        cudaSetDevice(ctx->dev);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    sparse_release(sp);
+}
+
+extern "C" lx2v_status lx2v_sparse_attention(lx2v_ctx *ctx, const lx2v_buf *q, const lx2v_buf *k, const lx2v_buf *v,
+                                             const lx2v_buf *gate, const lx2v_sparse *sp, lx2v_buf *out) {
+    lx2v_status s = enter(ctx);
+    if (s) return s;
+    if (!sp || !gate) return fail(ctx, LX2V_ERR_INVALID, "null sparse state or gate");
+    const size_t n = (size_t)sp->heads * sp->seq * sp->d;
+    if (!q || !k || !v || q->len < n || k->len < n || v->len < n || gate->len < n)
+        return fail(ctx, LX2V_ERR_INVALID, "q / k / v / gate hold fewer than heads x seq x head_dim");
+    if (q->dtype != k->dtype || k->dtype != v->dtype)
+        return fail(ctx, LX2V_ERR_INVALID, "q, k and v must have the same element type");
+    if (out == gate) return fail(ctx, LX2V_ERR_INVALID, "output aliases the gate");
+    VsaArgs a;
+    memset(&a, 0, sizeof a);
+    a.heads = sp->heads; a.seq = sp->seq; a.d = sp->d; a.nt = sp->nt; a.topk = sp->topk; a.scale = sp->scale;
+    a.q = q->ptr; a.k = k->ptr; a.v = v->ptr; a.qkv_f32 = is_f32(q);
+    a.gate = gate->ptr; a.gate_f32 = is_f32(gate);
+    a.out = out ? out->ptr : nullptr; a.out_f32 = is_f32(out);
+    a.slot_src = sp->slot_src; a.block_sizes = sp->block_sizes; a.token_tile = sp->token_tile;
+    const size_t hnd = (size_t)sp->heads * sp->nt * sp->d;
+    a.cq = sp->pooled; a.ck = sp->pooled + hnd; a.cv = sp->pooled + 2 * hnd; a.coarse_out = sp->pooled + 3 * hnd;
+    a.sel = sp->sel; a.sel_words = sp->sel_words; a.bits = sp->bits; a.words = sp->words;
+    {
+        OpScope ps(ctx, "sparse_select");
+        CUDA_TRY(ctx, vsa_select_launch(a, ctx->stream));
+        ctx->launches += 3;
+    }
+    AttnMaskArgs m;
+    m.mode = ATT_MASK_BITS;
+    m.dev_bits = sp->bits;
+    if ((s = attention_buffers(ctx, "sparse_attention", q, k, v, sp->heads, sp->seq, sp->seq, sp->d, m, out)))
+        return s;
+    OpScope ps(ctx, "sparse_combine");
+    CUDA_TRY(ctx, vsa_combine_launch(a, ctx->stream));
+    ctx->launches++;
+    CUDA_TRY(ctx, note_uses(ctx, {q, k, v, gate, out}));
     return LX2V_OK;
 }
 

@@ -55,6 +55,9 @@ SIGNATURES = {
     "lx2v_weight_q8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
     "lx2v_weight_q4": (_st, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _pp]),
     "lx2v_weight_fp8": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _pp]),
+    "lx2v_sparse_prepare": (_st, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_float, _pp]),
+    "lx2v_sparse_free": (None, [_vp, _vp]),
+    "lx2v_sparse_attention": (_st, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "lx2v_weight_nvfp4": (_st, [_vp, _vp, _vp, ctypes.c_float, _sz, _sz, _pp]),
     "lx2v_weight_free": (None, [_vp, _vp]),
     "lx2v_weight_info": (_st, [_vp, _vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_sz),

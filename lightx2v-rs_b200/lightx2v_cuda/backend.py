@@ -85,6 +85,18 @@ class KvCache:
             self.handle = None
 
 
+class Sparse:
+    """Sparse-attention state of one token grid (lx2v_sparse)."""
+
+    def __init__(self, be: "CudaBackend", handle: int, spec):
+        self.be, self.handle, self.spec = be, ctypes.c_void_p(handle), spec
+
+    def __del__(self):
+        if getattr(self, "handle", None) and self.handle.value and getattr(self.be, "_ctx", None):
+            self.be._lib.lx2v_sparse_free(self.be._ctx, self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+
 class Peers:
     """A tensor-parallel peer group (lx2v_peers): this rank, the group size
     and the flag buffers its barrier uses (kept alive with it)."""
@@ -444,6 +456,22 @@ class CudaBackend:
     def all_reduce_sum(self, buf: Buf, length: int | None = None):
         """In place: buf[:length] = sum over the group (on this context's stream)."""
         self._check(self._lib.lx2v_all_reduce_sum(self._ctx, buf.handle, buf.len if length is None else length))
+
+    # ---- sparse attention, backend.rs:309-331 -------------------------------------------
+    def sparse_prepare(self, spec) -> Sparse:
+        """spec: lightx2v_cuda.vsa.SparseSpec (the reference's SparseSpec)."""
+        p = spec.plan
+        slots = np.ascontiguousarray(p.slot_src, np.uint32)
+        sizes = np.ascontiguousarray(p.block_sizes, np.uint32)
+        h = ctypes.c_void_p()
+        self._check(self._lib.lx2v_sparse_prepare(self._ctx, slots.ctypes.data, sizes.ctypes.data, p.num_tiles(),
+                                                  p.seq, spec.heads, spec.head_dim, spec.topk, spec.scale,
+                                                  ctypes.byref(h)))
+        return Sparse(self, h.value, spec)
+
+    def sparse_attention(self, q: Buf, k: Buf, v: Buf, gate: Buf, sp: Sparse, out: Buf):
+        self._check(self._lib.lx2v_sparse_attention(self._ctx, q.handle, k.handle, v.handle, gate.handle,
+                                                    sp.handle, out.handle))
 
     # ---- tensor parallelism over NVLink peer memory (no reference counterpart) --------
     def ipc_handle(self, buf: Buf) -> bytes:

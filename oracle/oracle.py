@@ -380,3 +380,60 @@ class KvCacheRef:
             del self.kinds[f * ft:(f + 1) * ft]
         for f in range(min(sink_frames, n_frames())):
             self.kinds[f * ft:(f + 1) * ft] = [SINK] * ft
+
+
+def sparse_attention(q, k, v, gate, slot_src, block_sizes, seq: int, heads: int, d: int, topk: int,
+                     scale: float) -> np.ndarray:
+    """CpuBackend::sparse_attention, crates/lightx2v-cpu/src/lib.rs:500-606 (the
+    VSA of crates/lightx2v-core/src/sparse.rs): per head, tile means (x / n
+    added in slot order), coarse softmax attention over the tiles
+    (softmax_row, lib.rs:155-166), the top-k key tiles per query tile (higher
+    score first, ties to the lower tile), fine attention from every token to
+    the selected tiles' tokens, out = coarse * gate + fine, [seq, heads * d].
+    q, k, v, gate are f32 [heads, seq, d]. Loops over tiles and tokens as the
+    reference runs them; the dot products and the fine softmax in f32."""
+    q, k, v, gate = (np.asarray(a, np.float32).reshape(heads, seq, d) for a in (q, k, v, gate))
+    nt = len(block_sizes)
+    tile_tokens = [[int(s) for s in slot_src[t * 64:t * 64 + int(block_sizes[t])]] for t in range(nt)]
+    token_tile = np.zeros(seq, np.int64)
+    for t, toks in enumerate(tile_tokens):
+        token_tile[toks] = t
+    out = np.zeros((seq, heads, d), np.float32)
+    sc = np.float32(scale)
+
+    def softmax(row):
+        m = np.float32(-np.inf)
+        for x in row:
+            m = max(m, x)
+        e = np.exp((row - m).astype(np.float32)).astype(np.float32)
+        s = np.float32(0.0)
+        for x in e:
+            s = np.float32(s + x)
+        return (e * (np.float32(1.0) / s)).astype(np.float32)
+
+    for h in range(heads):
+        cq = np.zeros((nt, d), np.float32)
+        ck = np.zeros((nt, d), np.float32)
+        cv = np.zeros((nt, d), np.float32)
+        for t, toks in enumerate(tile_tokens):
+            n = np.float32(max(len(toks), 1))
+            for tok in toks:
+                cq[t] = (cq[t] + q[h, tok] / n).astype(np.float32)
+                ck[t] = (ck[t] + k[h, tok] / n).astype(np.float32)
+                cv[t] = (cv[t] + v[h, tok] / n).astype(np.float32)
+        coarse = np.zeros((nt, d), np.float32)
+        selected = []
+        for qi in range(nt):
+            row = np.array([np.float32(np.dot(cq[qi], ck[ki])) * sc for ki in range(nt)], np.float32)
+            row = softmax(row)
+            coarse[qi] = (row[:, None] * cv).sum(axis=0, dtype=np.float32)
+            order = sorted(range(nt), key=lambda ki: (-row[ki], ki))
+            selected.append(order[:topk])
+        for tok in range(seq):
+            qt = int(token_tile[tok])
+            keys = [kt for t in selected[qt] for kt in tile_tokens[t]]
+            s = (k[h, keys] @ q[h, tok]).astype(np.float32) * sc
+            p = softmax(s.astype(np.float32))
+            fine = (p[:, None] * v[h, keys]).sum(axis=0, dtype=np.float32)
+            out[tok, h] = coarse[qt] * gate[h, tok] + fine
+    return out.reshape(seq, heads * d)

@@ -195,3 +195,48 @@ def test_attention_argument_errors(be):
     with pytest.raises(L.Lx2vError) as e:
         be.attention(qb, kb, kb, 2, 8, 8, 128, qb)     # output aliases q
     assert e.value.status == L.ERR_INVALID
+
+
+# ---- sparse attention (backend.rs:309-331; VSA, cpu lib.rs:496-606) -------------------------
+def test_check_sparse_is_dense_at_zero_sparsity(be, oracle):
+    # crates/lightx2v-model/src/check.rs:227-255, tolerance 1e-5: sparsity 0
+    # keeps every tile, gate 0 removes the coarse term
+    from lightx2v_cuda import vsa
+    heads, d, grid = 1, 8, (4, 4, 4)
+    seq = 64
+    x = oracle.normal(11, 3 * heads * seq * d)  # q, k, v drawn in turn from one stream
+    q, k, v = np.split(x, 3)
+    qb, kb, vb = be.upload(q, F32), be.upload(k, F32), be.upload(v, F32)
+    gb = be.upload(np.zeros(heads * seq * d), F32)
+    sp = be.sparse_prepare(vsa.SparseSpec.new(grid, heads, d, 0.0))
+    ob, ob2 = be.alloc(seq * d, F32), be.alloc(seq * d, F32)
+    be.sparse_attention(qb, kb, vb, gb, sp, ob)
+    be.attention(qb, kb, vb, heads, seq, seq, d, ob2)
+    assert np.max(np.abs(be.download(ob) - be.download(ob2))) <= 1e-5
+
+
+@pytest.mark.parametrize("grid,heads,d,sparsity,dtype", [
+    ((4, 8, 8), 2, 8, 0.5, F32),      # 4 tiles, keep 2
+    ((5, 6, 7), 2, 8, 0.6, F32),      # partial tiles, 8 of them, keep 4
+    ((4, 8, 12), 3, 128, 0.5, BF16),  # tensor-core fine stage, 6 tiles, keep 3
+])
+def test_sparse_attention_matches_oracle(be, oracle, grid, heads, d, sparsity, dtype):
+    from lightx2v_cuda import vsa
+    spec = vsa.SparseSpec.new(grid, heads, d, sparsity)
+    seq = spec.plan.seq
+    n = heads * seq * d
+    q, k, v = (oracle.normal(60 + i, n) for i in range(3))
+    gate = oracle.normal(63, n, 0.5)
+    qb, kb, vb = (be.upload(a, dtype) for a in (q, k, v))
+    gb = be.upload(gate, F32)
+    sp = be.sparse_prepare(spec)
+    ob = be.alloc(seq * heads * d, F32)
+    be.sparse_attention(qb, kb, vb, gb, sp, ob)
+    got = be.download(ob)
+    # the oracle on the values the device holds
+    qh, kh, vh = (be.download(b) for b in (qb, kb, vb))
+    want = oracle.sparse_attention(qh, kh, vh, gate, spec.plan.slot_src, spec.plan.block_sizes, seq, heads, d,
+                                   spec.topk, spec.scale).reshape(-1)
+    tol = 1e-4 if dtype == F32 else REL_L2
+    assert rel_l2(got, want) <= tol
+    assert np.isfinite(got).all()
