@@ -16,11 +16,17 @@
 //   O  += P_j V_j       tcgen05.mma with A = P_j from TMEM and B = V_j^T from
 //                       shared memory (V is given transposed, [D][keys]),
 //                       D = O in TMEM
-// S is double-buffered, so the softmax of block j overlaps the tensor core's
-// S_{j+1} and P_{j-1} V_{j-1}. The running max m only moves when a row's
-// new maximum exceeds it by more than 2^8 (then O is rescaled once in TMEM);
-// otherwise exp2 arguments stay <= 8 and the final O / l uses the same m, so
-// the result is the exact softmax up to rounding.
+// The live key blocks alternate between two softmax warpgroups: block i goes
+// to warpgroup i % 2, which has its own S buffer, running max m, row sum l and
+// accumulator O in TMEM. Each warpgroup's chain (softmax of its block, then
+// P V, then the next S into the same buffer) runs while the other
+// warpgroup's chain holds the tensor core, and neither waits for the other
+// until the epilogue, which merges the two halves:
+//   out = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)),
+//   m = max(m_0, m_1).
+// A running max only moves when a row's new maximum exceeds it by more than
+// 2^8 (then that O is rescaled once in TMEM); otherwise exp2 arguments stay
+// <= 8, so the result is the exact softmax up to rounding.
 //
 // Masks: none; a bit mask [sq][ceil(sk/32)] (the trait's boolean mask);
 // or the DiT's MemRoPE rule tk[key] <= tq[query] with per-block ranges of
@@ -30,12 +36,15 @@
 // all -inf row does.
 //
 // Warp roles (384 threads, one CTA per SM: TMEM 512 columns):
-//   warp 0      TMA producer: Q once, then K_j / V_j^T into a 2-stage ring
-//   warp 1      TMEM allocator and MMA issuer (one thread)
-//   warps 4-11  softmax, then the epilogue (O / l -> out): two warpgroups,
-//               each taking half of every S block's key columns (and half of
-//               O's columns) for all 128 query rows, so that every scheduler
-//               runs two softmax warps
+//   warps 0-7   softmax, then the epilogue (merge, / l -> out): two
+//               warpgroups taking alternate key blocks, so that every
+//               scheduler runs one softmax warp of each (warp w reads TMEM
+//               lanes 32 (w % 4) .. + 31); 208 registers a thread, so that a
+//               thread holds a whole 128-key row of S
+//   warp 8      TMA producer of Q (once) and K_j (3-stage ring)
+//   warp 9      TMEM allocator and MMA issuer (one thread)
+//   warp 10     TMA producer of V_j^T (2-stage ring)
+//   warp 11     idle (warpgroup 2 gives its registers to the softmax)
 // Every mbarrier wait is bounded; on expiry the kernel records an error
 // word, drains its own copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -55,17 +64,21 @@ namespace {
 constexpr int AT_D = 128;       // head_dim of the tensor-core kernel
 constexpr int AT_BQ = 128;      // queries per CTA (TMEM lanes)
 constexpr int AT_BK = 128;      // keys per block
-constexpr int AT_NS = 2;        // K / V ring stages
+constexpr int AT_NK = 3;        // K ring stages
+constexpr int AT_NV = 2;        // V ring stages
 constexpr int AT_TILE = 128 * 128 * 2;  // one 128 x 128 bf16 tile: two 64-column SW128 boxes
 constexpr int AT_HALF = AT_TILE / 2;
 constexpr int AT_OFF_K = AT_TILE;                   // after Q
-constexpr int AT_OFF_V = AT_OFF_K + AT_NS * AT_TILE;
-constexpr int AT_OFF_BAR = AT_OFF_V + AT_NS * AT_TILE;
-// q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2], p_full[2], pv_done, o_full, drain
-constexpr int AT_NUM_BARS = 1 + 4 * AT_NS + 2 + 2 + 3;
-constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16 + (512 + 256 + 4) * 4;
-constexpr int AT_TMEM_COLS = 512;  // O: 0-127, S/P buffers: 128-255, 256-383
+constexpr int AT_OFF_V = AT_OFF_K + AT_NK * AT_TILE;
+constexpr int AT_OFF_BAR = AT_OFF_V + AT_NV * AT_TILE;
+// q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2], o_full, drain
+constexpr int AT_NUM_BARS = 1 + 2 * AT_NK + 2 * AT_NV + 2 + 2 + 2;
+constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16 + 512 * 4;
+constexpr int AT_TMEM_COLS = 512;  // O_0: 0-127, O_1: 128-255, S_0 / P_0: 256-383, S_1 / P_1: 384-511
 constexpr float AT_RESCALE_LOG2 = 8.0f;
+// registers a block needs after the warpgroups' setmaxnreg: warpgroup 2 (producers,
+// MMA issuer) at 72 a thread, the two softmax warpgroups at 208
+constexpr int AT_REG_SPLIT = 128 * 72 + 256 * 208;
 
 static_assert(AT_SMEM <= 227 * 1024, "shared memory budget");
 
@@ -75,17 +88,16 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// Whether key block j can hold a key that some query of the tile sees, and
-// whether every query of the tile sees every key of it (no per-element mask).
-__device__ __forceinline__ bool block_live(const AttnParams &p, int j, int2 tqr) {
-    if (p.mask_mode != ATT_MASK_TEMPORAL) return true;
-    return p.tk_range[j].x <= tqr.y;
-}
-__device__ __forceinline__ bool block_full(const AttnParams &p, int j, int2 tqr) {
-    if ((j + 1) * AT_BK > p.sk) return false;
-    if (p.mask_mode == ATT_MASK_NONE) return true;
-    if (p.mask_mode == ATT_MASK_TEMPORAL) return p.tk_range[j].y <= tqr.x;
-    return false;
+// Whether key block j can hold a key that some query of the tile sees
+// (bit 0), and whether every query of the tile sees every key of it, so that
+// it needs no per-element mask (bit 1).
+__device__ __forceinline__ uint32_t block_flags(const AttnParams &p, int j, int2 tqr) {
+    const int2 r = p.mask_mode == ATT_MASK_TEMPORAL ? p.tk_range[j] : make_int2(0, 0);
+    const bool live = p.mask_mode != ATT_MASK_TEMPORAL || r.x <= tqr.y;
+    bool full = (j + 1) * AT_BK <= p.sk;
+    if (p.mask_mode == ATT_MASK_TEMPORAL) full = full && r.y <= tqr.x;
+    else if (p.mask_mode != ATT_MASK_NONE) full = false;
+    return (live ? 1u : 0u) | (full ? 2u : 0u);
 }
 
 __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_constant__ AttnParams p) {
@@ -94,13 +106,12 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AT_OFF_BAR);
     uint64_t *q_full = bars;
     uint64_t *k_full = q_full + 1;
-    uint64_t *k_empty = k_full + AT_NS;
-    uint64_t *v_full = k_empty + AT_NS;
-    uint64_t *v_empty = v_full + AT_NS;
-    uint64_t *s_full = v_empty + AT_NS;   // [2]
+    uint64_t *k_empty = k_full + AT_NK;
+    uint64_t *v_full = k_empty + AT_NK;
+    uint64_t *v_empty = v_full + AT_NV;
+    uint64_t *s_full = v_empty + AT_NV;   // [2]
     uint64_t *p_full = s_full + 2;        // [2]
-    uint64_t *pv_done = p_full + 2;
-    uint64_t *o_full = pv_done + 1;
+    uint64_t *o_full = p_full + 2;
     uint64_t *drain = o_full + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
@@ -118,69 +129,83 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < AT_NS; ++s) {
+        for (int s = 0; s < AT_NK; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < AT_NV; ++s) {
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&p_full[b], 8);
+            mbar_init(&p_full[b], 4);
         }
-        mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
-        *reinterpret_cast<volatile int *>(reinterpret_cast<float *>(tmem_slot + 4) + 768) = 0;  // softmax abort flag
         fence_mbar_init();
         tma_prefetch_desc(&p.tmap_q);
         tma_prefetch_desc(&p.tmap_k);
         tma_prefetch_desc(&p.tmap_vt);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, AT_TMEM_COLS);
+    if (warp == 9) tmem_alloc(tmem_slot, AT_TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
+    if (warp >= 8) {
+    // Registers: the kernel is launched with 168 a thread (384 x 168 =
+    // 64512). Warpgroup 2 (producer, MMA issuer, two idle warps) gives back
+    // down to 72 and the softmax warpgroups take 208, which holds a whole
+    // 128-key row of S: 128 x 72 + 256 x 208 = 62464 <= 64512.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;" ::: "memory");
+    if (warp == 8 || warp == 10) {
+        // ---------------- TMA producers: warp 8 Q and K_j, warp 10 V_j^T ----------------
+        // (separate threads, so that a K load never waits behind the
+        // release of a V stage, which comes only after that block's softmax)
         if (lane == 0) {
-            int last_k[AT_NS], last_v[AT_NS];
-            for (int s = 0; s < AT_NS; ++s) last_k[s] = last_v[s] = -1;
-            const int qrow = h * p.q_rows + qt * AT_BQ;
-            mbar_arrive_expect_tx(q_full, AT_TILE);
-            tma_load_2d(smem, &p.tmap_q, q_full, 0, qrow);
-            tma_load_2d(smem + AT_HALF, &p.tmap_q, q_full, 64, qrow);
-            Ring ks, vs;
-            bool ok = true;
-            for (int j = 0; j < nblk && ok; ++j) {
-                if (!block_live(p, j, tqr)) continue;
-                if (!mbar_wait_bounded(&k_empty[ks.s], ks.ph ^ 1, err, lim)) { ok = false; break; }
-                uint8_t *kd = smem + AT_OFF_K + ks.s * AT_TILE;
-                const int krow = h * p.k_rows + j * AT_BK;
-                mbar_arrive_expect_tx(&k_full[ks.s], AT_TILE);
-                tma_load_2d(kd, &p.tmap_k, &k_full[ks.s], 0, krow);
-                tma_load_2d(kd + AT_HALF, &p.tmap_k, &k_full[ks.s], 64, krow);
-                last_k[ks.s] = ks.ph;
-                ks.next<AT_NS>();
-                if (!mbar_wait_bounded(&v_empty[vs.s], vs.ph ^ 1, err, lim)) { ok = false; break; }
-                uint8_t *vd = smem + AT_OFF_V + vs.s * AT_TILE;
-                mbar_arrive_expect_tx(&v_full[vs.s], AT_TILE);
-                tma_load_2d(vd, &p.tmap_vt, &v_full[vs.s], j * AT_BK, h * AT_D);
-                tma_load_2d(vd + AT_HALF, &p.tmap_vt, &v_full[vs.s], j * AT_BK + 64, h * AT_D);
-                last_v[vs.s] = vs.ph;
-                vs.next<AT_NS>();
+            const bool is_k = warp == 8;
+            uint64_t *full = is_k ? k_full : v_full;
+            uint64_t *empty = is_k ? k_empty : v_empty;
+            const int ns = is_k ? AT_NK : AT_NV;
+            int last[AT_NK];
+            for (int s = 0; s < AT_NK; ++s) last[s] = -1;
+            if (is_k) {
+                const int qrow = h * p.q_rows + qt * AT_BQ;
+                mbar_arrive_expect_tx(q_full, AT_TILE);
+                tma_load_2d(smem, &p.tmap_q, q_full, 0, qrow);
+                tma_load_2d(smem + AT_HALF, &p.tmap_q, q_full, 64, qrow);
+            }
+            int st = 0;
+            uint32_t ph = 0;
+            for (int j = 0; j < nblk; ++j) {
+                if (!(block_flags(p, j, tqr) & 1u)) continue;
+                if (!mbar_wait_bounded(&empty[st], ph ^ 1, err, lim)) break;
+                mbar_arrive_expect_tx(&full[st], AT_TILE);
+                if (is_k) {
+                    uint8_t *kd = smem + AT_OFF_K + st * AT_TILE;
+                    const int krow = h * p.k_rows + j * AT_BK;
+                    tma_load_2d(kd, &p.tmap_k, &full[st], 0, krow);
+                    tma_load_2d(kd + AT_HALF, &p.tmap_k, &full[st], 64, krow);
+                } else {
+                    uint8_t *vd = smem + AT_OFF_V + st * AT_TILE;
+                    tma_load_2d(vd, &p.tmap_vt, &full[st], j * AT_BK, h * AT_D);
+                    tma_load_2d(vd + AT_HALF, &p.tmap_vt, &full[st], j * AT_BK + 64, h * AT_D);
+                }
+                last[st] = (int)ph;
+                if (++st == ns) {
+                    st = 0;
+                    ph ^= 1u;
+                }
             }
             // every issued load lands before the kernel can leave
-            mbar_wait_bounded(q_full, 0, nullptr, drain_lim);
-            for (int s = 0; s < AT_NS; ++s) {
-                if (last_k[s] >= 0) mbar_wait_bounded(&k_full[s], (uint32_t)last_k[s], nullptr, drain_lim);
-                if (last_v[s] >= 0) mbar_wait_bounded(&v_full[s], (uint32_t)last_v[s], nullptr, drain_lim);
-            }
+            if (is_k) mbar_wait_bounded(q_full, 0, nullptr, drain_lim);
+            for (int s = 0; s < ns; ++s)
+                if (last[s] >= 0) mbar_wait_bounded(&full[s], (uint32_t)last[s], nullptr, drain_lim);
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 9) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16_f32(128, 128);
@@ -189,27 +214,30 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
             tc_fence_after();
             Ring ks, vs;
             int it = 0;
+            // block i (counted over live blocks) belongs to softmax warpgroup
+            // i % 2: S_i goes to its S buffer, P_i V_i into its accumulator
             auto issue_pv = [&](int i) -> bool {
-                if (!mbar_wait_bounded(&p_full[i & 1], (uint32_t)((i >> 1) & 1), err, lim)) return false;
+                const int wg = i & 1;
+                if (!mbar_wait_bounded(&p_full[wg], (uint32_t)((i >> 1) & 1), err, lim)) return false;
                 if (!mbar_wait_bounded(&v_full[vs.s], vs.ph, err, lim)) return false;
                 tc_fence_after();
-                const uint32_t pbuf = tmem + 128u + (uint32_t)((i & 1) * 128);
+                const uint32_t pbuf = tmem + 256u + (uint32_t)(wg * 128);
+                const uint32_t obuf = tmem + (uint32_t)(wg * 128);
                 const uint32_t v_addr = smem_u32(smem + AT_OFF_V + vs.s * AT_TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t b = smem_desc_sw128(v_addr + (kk >> 2) * AT_HALF) + (uint64_t)((kk & 3) * 2);
-                    mma_ts_f16(tmem, pbuf + (uint32_t)(kk * 8), b, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts_f16(obuf, pbuf + (uint32_t)(kk * 8), b, idesc, (i >= 2 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&v_empty[vs.s]);
-                mma_commit(pv_done);
-                vs.next<AT_NS>();
+                vs.next<AT_NV>();
                 return true;
             };
             for (int j = 0; j < nblk && ok; ++j) {
-                if (!block_live(p, j, tqr)) continue;
+                if (!(block_flags(p, j, tqr) & 1u)) continue;
                 if (!mbar_wait_bounded(&k_full[ks.s], ks.ph, err, lim)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sbuf = tmem + 128u + (uint32_t)((it & 1) * 128);
+                const uint32_t sbuf = tmem + 256u + (uint32_t)((it & 1) * 128);
                 const uint32_t k_addr = smem_u32(smem + AT_OFF_K + ks.s * AT_TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
@@ -219,7 +247,7 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                 }
                 mma_commit(&s_full[it & 1]);
                 mma_commit(&k_empty[ks.s]);
-                ks.next<AT_NS>();
+                ks.next<AT_NK>();
                 if (it >= 1 && !issue_pv(it - 1)) { ok = false; break; }
                 ++it;
             }
@@ -229,55 +257,57 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
             mbar_wait_bounded(drain, 0, nullptr, drain_lim);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
         // ---------------- softmax + epilogue ----------------
-        // Two warpgroups share each query row: warpgroup wg takes the key
-        // columns [64 wg, 64 wg + 64) of every S block (and the same half of
-        // O's columns). Thread = query row (TMEM lane). The halves' row maxima
-        // meet in shared memory, so both warpgroups use the same running max.
-        const int wg = (warp - 4) >> 2;
+        // Warpgroup wg takes the live key blocks of parity wg (block number
+        // it, counted over live blocks, with it % 2 == wg): whole 128-key rows
+        // of S_wg, its own running max m and row sum l, and its own
+        // accumulator O_wg. The two warpgroups never wait for each other
+        // inside the loop, so one's TMEM loads and max overlap the other's
+        // exponentials. Thread = query row (TMEM lane).
+        const int wg = warp >> 2;
         const int r = (warp & 3) * 32 + lane;
         const int q = qt * AT_BQ + r;
         const bool q_ok = q < p.sq;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t o_col = (uint32_t)(wg * 128);
+        const uint32_t s_col = 256u + (uint32_t)(wg * 128);
         const int tq_row = (p.mask_mode == ATT_MASK_TEMPORAL && q_ok) ? p.tq[q] : 0;
-        float *xmax = reinterpret_cast<float *>(tmem_slot + 4);  // [2 blocks][2 warpgroups][128 rows]
-        volatile int *abort_flag = reinterpret_cast<volatile int *>(xmax + 768);
         const float NEG_INF = -INFINITY;
+        const float sc = p.scale_log2;
         float m_run = NEG_INF, l = 0.0f;
-        int it = 0;
+        int it = 0, n_mine = 0;
         bool ok = true;
-        // Both warpgroups meet at a named barrier every block, so neither may
-        // leave the loop alone: a failed wait only sets abort_flag, and both
-        // leave together right after the next barrier.
         for (int j = 0; j < nblk; ++j) {
-            if (!block_live(p, j, tqr)) continue;
-            const bool full = block_full(p, j, tqr);
+            const uint32_t bf = block_flags(p, j, tqr);
+            if (!(bf & 1u)) continue;
+            const bool mine = (it & 1) == wg;
+            ++it;
+            if (!mine) continue;
+            const int i = n_mine++;
+            const bool full = (bf & 2u) != 0;
             int okw = 1;
-            if (lane == 0) okw = mbar_wait_bounded(&s_full[it & 1], (uint32_t)((it >> 1) & 1), err, lim) ? 1 : 0;
+            if (lane == 0) okw = mbar_wait_bounded(&s_full[wg], (uint32_t)(i & 1), err, lim) ? 1 : 0;
             okw = __shfl_sync(0xFFFFFFFFu, okw, 0);
-            if (!okw && lane == 0) *abort_flag = 1;
+            if (!okw) { ok = false; break; }  // warp-uniform; the waits of the others end on the error word
             tc_fence_after();
-            const uint32_t scol = 128u + (uint32_t)((it & 1) * 128);
-            // this half's 64 raw scores: two loads in flight, one wait
-            uint32_t sv[64];
-            if (okw) {
-                tmem_ld_32x32b_x32(lane_base + scol + (uint32_t)(wg * 64), *reinterpret_cast<uint32_t(*)[32]>(sv));
-                tmem_ld_32x32b_x32(lane_base + scol + (uint32_t)(wg * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-                tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv));
-                tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-            } else {
+            // the block's 128 raw scores: four loads in flight, then the waits
+            uint32_t sv[128];
 #pragma unroll
-                for (int i = 0; i < 64; ++i) sv[i] = 0xFF800000u;
-            }
+            for (int c = 0; c < 4; ++c)
+                tmem_ld_32x32b_x32(lane_base + s_col + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * c));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(sv + 32 * c));
             if (!full) {
                 // some query of the tile does not see all of this block: the
-                // visibility bits of the row's 64 keys (a rolled loop), then
+                // visibility bits of the row's 128 keys (a rolled loop), then
                 // -inf where hidden
-                const int k0 = j * AT_BK + wg * 64;
-                uint32_t vm[2];
+                const int k0 = j * AT_BK;
+                uint32_t vm[4];
 #pragma unroll 1
-                for (int c = 0; c < 2; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     uint32_t w = 0;
                     const int kc = k0 + c * 32;
                     if (p.mask_mode == ATT_MASK_BITS && q_ok && kc < p.sk) {
@@ -294,85 +324,82 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                     vm[c] = w;
                 }
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (!((vm[i >> 5] >> (i & 31)) & 1u)) sv[i] = 0xFF800000u;  // -inf
+                for (int k = 0; k < 128; ++k)
+                    if (!((vm[k >> 5] >> (k & 31)) & 1u)) sv[k] = 0xFF800000u;  // -inf
             }
-            // row max of the raw scores (scale > 0 commutes with max), both halves
+            // row max of the raw scores (scale > 0 commutes with max)
             float mx0 = NEG_INF, mx1 = NEG_INF, mx2 = NEG_INF, mx3 = NEG_INF;
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
-                mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
-                mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
-                mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
-                mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
+            for (int k = 0; k < 128; k += 4) {
+                mx0 = fmaxf(mx0, __uint_as_float(sv[k]));
+                mx1 = fmaxf(mx1, __uint_as_float(sv[k + 1]));
+                mx2 = fmaxf(mx2, __uint_as_float(sv[k + 2]));
+                mx3 = fmaxf(mx3, __uint_as_float(sv[k + 3]));
             }
-            float *xm = xmax + (it & 1) * 256;
-            xm[wg * 128 + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-            // also orders both halves' S loads before either half's P stores
-            // (P overwrites S's first 64 columns, half of which the other
-            // warpgroup reads)
-            tc_fence_before();
-            named_bar_sync(1, 256);
-            tc_fence_after();
-            if (*abort_flag) { ok = false; break; }
-            const float mx = fmaxf(xm[r], xm[128 + r]) * p.scale_log2;
+            const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sc;
             const float m_new = fmaxf(m_run, mx);
             const bool need = m_run != NEG_INF && m_new > m_run + AT_RESCALE_LOG2;
             if (__any_sync(0xFFFFFFFFu, need)) {
-                // O holds P_0..P_{it-1} V scaled by 2^-m_run: wait for the last
-                // of those products, then rescale this warp's rows (this
-                // warpgroup's half of the columns) in TMEM
-                if (lane == 0) okw = mbar_wait_bounded(pv_done, (uint32_t)((it - 1) & 1), err, lim) ? 1 : 0;
-                okw = __shfl_sync(0xFFFFFFFFu, okw, 0);
-                if (!okw && lane == 0) *abort_flag = 1;  // both warpgroups leave at the next barrier
-                tc_fence_after();
+                // O_wg holds this warpgroup's earlier P V products scaled by
+                // 2^-m_run. The last of them (block i-1 of this warpgroup) was
+                // issued before the product that filled S_wg, so the S_wg
+                // wait above has already seen it complete: rescale this
+                // warp's rows of O_wg in TMEM.
                 const float corr = need ? ex2(m_run - m_new) : 1.0f;
 #pragma unroll 1
-                for (int c = 0; c < 2 && okw; ++c) {
-                    const uint32_t oc = (uint32_t)(wg * 64 + c * 32);
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t oc = o_col + (uint32_t)(c * 32);
                     uint32_t t[32];
                     tmem_ld_32x32b_x32(lane_base + oc, t);
                     tmem_wait_ld_regs(t);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
+                    for (int k = 0; k < 32; ++k) t[k] = __float_as_uint(__uint_as_float(t[k]) * corr);
                     tmem_st_32x32b_x16(lane_base + oc, *reinterpret_cast<uint32_t(*)[16]>(t));
                     tmem_st_32x32b_x16(lane_base + oc + 16u, *reinterpret_cast<uint32_t(*)[16]>(t + 16));
                 }
-                tmem_wait_st();
                 if (need) {
                     l *= corr;
                     m_run = m_new;
                 }
             }
-            if (m_run == NEG_INF) m_run = m_new;  // nothing visible so far: O holds zeros
+            if (m_run == NEG_INF) m_run = m_new;  // nothing visible so far: O_wg holds zeros
             const float nm = m_run == NEG_INF ? 0.0f : -m_run;
-            const float sc = p.scale_log2;
-            uint32_t pk[32];
+            // P = exp2(S * scale - m) as bf16 pairs over the first 64 columns
+            // of S_wg (all 128 scores are already in registers)
             float ls0 = 0.0f, ls1 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float a = ex2(fmaf(__uint_as_float(sv[2 * i]), sc, nm));
-                const float b = ex2(fmaf(__uint_as_float(sv[2 * i + 1]), sc, nm));
-                ls0 += a;
-                ls1 += b;
-                pk[i] = pack_bf16x2(a, b);
+            for (int c = 0; c < 4; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float a = ex2(fmaf(__uint_as_float(sv[32 * c + 2 * k]), sc, nm));
+                    const float b = ex2(fmaf(__uint_as_float(sv[32 * c + 2 * k + 1]), sc, nm));
+                    ls0 += a;
+                    ls1 += b;
+                    pk[k] = pack_bf16x2(a, b);
+                }
+                tmem_st_32x32b_x16(lane_base + s_col + (uint32_t)(c * 16), pk);
             }
             l += ls0 + ls1;
-            // keys [64 wg, 64 wg + 64) -> P columns [32 wg, 32 wg + 32)
-            tmem_st_32x32b_x16(lane_base + scol + (uint32_t)(wg * 32), *reinterpret_cast<uint32_t(*)[16]>(pk));
-            tmem_st_32x32b_x16(lane_base + scol + (uint32_t)(wg * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[it & 1]);
-            ++it;
+            if (lane == 0) mbar_arrive(&p_full[wg]);
         }
-        // ---------------- epilogue: out[q, h*D + c] = O / l ----------------
-        // every softmax thread arrives here (also after an error) for the row-sum exchange
-        float *xl = xmax + 512;
-        xl[wg * 128 + r] = l;
+        // ---------------- epilogue: out[q, h*D + c] = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) ----------------
+        // with a_w = 2^(m_w - max(m_0, m_1)); every softmax thread arrives
+        // here (also after an error) for the exchange of m and l
+        float *xm = reinterpret_cast<float *>(tmem_slot + 4);  // [2 warpgroups][128 rows] m, then l
+        xm[wg * 128 + r] = m_run;
+        xm[256 + wg * 128 + r] = l;
         named_bar_sync(1, 256);
-        const float lt = xl[r] + xl[128 + r];
+        const float m0 = xm[r], m1 = xm[128 + r];
+        const float mt = fmaxf(m0, m1);
+        // a warpgroup that saw nothing of this row (or had no block at all:
+        // O_w never written) contributes nothing
+        const float a0 = m0 == NEG_INF ? 0.0f : ex2(m0 - mt);
+        const float a1 = m1 == NEG_INF ? 0.0f : ex2(m1 - mt);
+        const float lt = xm[256 + r] * a0 + xm[384 + r] * a1;
         if (ok && it > 0) {
             int okw = 1;
             if (lane == 0) okw = mbar_wait_bounded(o_full, 0, err, lim) ? 1 : 0;
@@ -382,32 +409,34 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
         if (ok) {
             tc_fence_after();
             const float inv = 1.0f / lt;  // lt == 0 (no visible key): NaN, as the reference
+            // this warpgroup writes output columns [64 wg, 64 wg + 64)
             const int64_t obase = (int64_t)q * p.heads * AT_D + (int64_t)h * AT_D + wg * 64;
-#pragma unroll
+#pragma unroll 1
             for (int c = 0; c < 2; ++c) {
-                uint32_t t[32];
-                if (it > 0) {
-                    tmem_ld_32x32b_x32(lane_base + (uint32_t)(wg * 64 + c * 32), t);
-                    tmem_wait_ld_regs(t);
-                } else {
+                const uint32_t oc = (uint32_t)(wg * 64 + c * 32);
+                uint32_t t0[32], t1[32];
+                tmem_ld_32x32b_x32(lane_base + oc, t0);
+                tmem_ld_32x32b_x32(lane_base + 128u + oc, t1);
+                tmem_wait_ld_regs(t0);
+                tmem_wait_ld_regs(t1);
+                float o[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) t[i] = 0u;
+                for (int k = 0; k < 32; ++k) {
+                    const float v0 = a0 != 0.0f ? __uint_as_float(t0[k]) * a0 : 0.0f;
+                    const float v1 = a1 != 0.0f ? __uint_as_float(t1[k]) * a1 : 0.0f;
+                    o[k] = (v0 + v1) * inv;
                 }
                 if (!q_ok) continue;
                 if (p.out_f32) {
                     float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + obase + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(__uint_as_float(t[4 * i]) * inv, __uint_as_float(t[4 * i + 1]) * inv,
-                                             __uint_as_float(t[4 * i + 2]) * inv, __uint_as_float(t[4 * i + 3]) * inv);
+                    for (int k = 0; k < 8; ++k) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
                 } else {
                     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + obase + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        dst[i] = make_uint4(pack_bf16x2(__uint_as_float(t[8 * i]) * inv, __uint_as_float(t[8 * i + 1]) * inv),
-                                            pack_bf16x2(__uint_as_float(t[8 * i + 2]) * inv, __uint_as_float(t[8 * i + 3]) * inv),
-                                            pack_bf16x2(__uint_as_float(t[8 * i + 4]) * inv, __uint_as_float(t[8 * i + 5]) * inv),
-                                            pack_bf16x2(__uint_as_float(t[8 * i + 6]) * inv, __uint_as_float(t[8 * i + 7]) * inv));
+                    for (int k = 0; k < 4; ++k)
+                        dst[k] = make_uint4(pack_bf16x2(o[8 * k], o[8 * k + 1]), pack_bf16x2(o[8 * k + 2], o[8 * k + 3]),
+                                            pack_bf16x2(o[8 * k + 4], o[8 * k + 5]), pack_bf16x2(o[8 * k + 6], o[8 * k + 7]));
                 }
             }
         }
@@ -416,7 +445,7 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, AT_TMEM_COLS);
+    if (warp == 9) tmem_dealloc(tmem, AT_TMEM_COLS);
 }
 
 // ---- generic kernel (any head_dim <= 256, f32 or bf16 buffers) ----------------
@@ -506,6 +535,13 @@ cudaError_t attention_tc_launch(const AttnParams &p, cudaStream_t st) {
     if (!slot || slot->load() == 0) {
         cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
         if (e != cudaSuccess) return e;
+        // the warpgroups' register split (setmaxnreg: 128 x 72 + 256 x 208)
+        // must fit in what the block is launched with, or the increase
+        // would wait forever: refuse to launch a build that has fewer
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, attention_tc_kernel);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs * 384 < AT_REG_SPLIT) return cudaErrorInvalidConfiguration;
         if (slot) slot->store(1);
     }
     const int n_qt = (p.sq + AT_BQ - 1) / AT_BQ;
