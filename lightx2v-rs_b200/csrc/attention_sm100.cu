@@ -72,7 +72,7 @@ constexpr int AT_OFF_K = AT_TILE;                   // after Q
 constexpr int AT_OFF_V = AT_OFF_K + AT_NK * AT_TILE;
 constexpr int AT_OFF_BAR = AT_OFF_V + AT_NV * AT_TILE;
 // q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2], o_full, drain
-constexpr int AT_NUM_BARS = 1 + 2 * AT_NK + 2 * AT_NV + 2 + 2 + 2;
+constexpr int AT_NUM_BARS = 1 + 2 * AT_NK + 2 * AT_NV + 2 + 4 + 2;
 constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16 + 512 * 4;
 constexpr int AT_TMEM_COLS = 512;  // O_0: 0-127, O_1: 128-255, S_0 / P_0: 256-383, S_1 / P_1: 384-511
 constexpr float AT_RESCALE_LOG2 = 8.0f;
@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
     uint64_t *v_full = k_empty + AT_NK;
     uint64_t *v_empty = v_full + AT_NV;
     uint64_t *s_full = v_empty + AT_NV;   // [2]
-    uint64_t *p_full = s_full + 2;        // [2]
-    uint64_t *o_full = p_full + 2;
+    uint64_t *p_full = s_full + 2;        // [2 warpgroups][2 halves]
+    uint64_t *o_full = p_full + 4;
     uint64_t *drain = o_full + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
@@ -139,7 +139,8 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&p_full[b], 4);
+            mbar_init(&p_full[2 * b], 4);
+            mbar_init(&p_full[2 * b + 1], 4);
         }
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
@@ -218,16 +219,21 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
             // i % 2: S_i goes to its S buffer, P_i V_i into its accumulator
             auto issue_pv = [&](int i) -> bool {
                 const int wg = i & 1;
-                if (!mbar_wait_bounded(&p_full[wg], (uint32_t)((i >> 1) & 1), err, lim)) return false;
                 if (!mbar_wait_bounded(&v_full[vs.s], vs.ph, err, lim)) return false;
-                tc_fence_after();
                 const uint32_t pbuf = tmem + 256u + (uint32_t)(wg * 128);
                 const uint32_t obuf = tmem + (uint32_t)(wg * 128);
                 const uint32_t v_addr = smem_u32(smem + AT_OFF_V + vs.s * AT_TILE);
+                // P arrives in two halves of 64 keys: the first half's
+                // products start while the softmax still computes the second
+                for (int hf = 0; hf < 2; ++hf) {
+                    if (!mbar_wait_bounded(&p_full[2 * wg + hf], (uint32_t)((i >> 1) & 1), err, lim)) return false;
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t b = smem_desc_sw128(v_addr + (kk >> 2) * AT_HALF) + (uint64_t)((kk & 3) * 2);
-                    mma_ts_f16(obuf, pbuf + (uint32_t)(kk * 8), b, idesc, (i >= 2 || kk > 0) ? 1u : 0u);
+                    for (int k4 = 0; k4 < 4; ++k4) {
+                        const int kk = 4 * hf + k4;
+                        const uint64_t b = smem_desc_sw128(v_addr + hf * AT_HALF) + (uint64_t)(k4 * 2);
+                        mma_ts_f16(obuf, pbuf + (uint32_t)(kk * 8), b, idesc, (i >= 2 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 mma_commit(&v_empty[vs.s]);
                 vs.next<AT_NV>();
@@ -379,12 +385,14 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                     pk[k] = pack_bf16x2(a, b);
                 }
                 tmem_st_32x32b_x16(lane_base + s_col + (uint32_t)(c * 16), pk);
+                if (c == 1 || c == 3) {  // keys [0, 64) and [64, 128) of P are in TMEM
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p_full[2 * wg + (c >> 1)]);
+                }
             }
             l += ls0 + ls1;
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[wg]);
         }
         // ---------------- epilogue: out[q, h*D + c] = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) ----------------
         // with a_w = 2^(m_w - max(m_0, m_1)); every softmax thread arrives
