@@ -20,8 +20,10 @@
 // to warpgroup i % 2, which has its own S buffer, running max m, row sum l and
 // accumulator O in TMEM. Each warpgroup's chain (softmax of its block, then
 // P V, then the next S into the same buffer) runs while the other
-// warpgroup's chain holds the tensor core, and neither waits for the other
-// until the epilogue, which merges the two halves:
+// warpgroup's chain holds the tensor core. P is handed over in two halves of
+// 64 keys, so the first half's products run while the softmax computes the
+// second. Neither warpgroup waits for the other until the epilogue, which
+// merges the two halves:
 //   out = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)),
 //   m = max(m_0, m_1).
 // A running max only moves when a row's new maximum exceeds it by more than
