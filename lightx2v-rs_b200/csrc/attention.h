@@ -14,7 +14,8 @@ enum : int { ATT_MASK_NONE = 0, ATT_MASK_BITS = 1, ATT_MASK_TEMPORAL = 2 };
 struct alignas(64) AttnParams {
     CUtensorMap tmap_q;   // Q bf16 [heads * q_rows][128], box {64, 128}, 128-byte swizzle
     CUtensorMap tmap_k;   // K bf16 [heads * k_rows][128], box {64, 128}, 128-byte swizzle
-    CUtensorMap tmap_vt;  // V^T bf16 [heads * 128][sk_pad], box {64, 128}, 128-byte swizzle
+    CUtensorMap tmap_v;   // V bf16 as stored, 3-D {128, sk, heads} (head stride k_rows rows), box {64, 128, 1},
+                          // 128-byte swizzle: keys >= sk of a head arrive as zeros
     void *out;            // [sq][heads * 128], bf16 or f32
     int out_f32;
     int heads, sq, sk;
@@ -50,8 +51,4 @@ struct AttnSimtParams {
 
 cudaError_t attention_tc_launch(const AttnParams &p, cudaStream_t st);
 cudaError_t attention_simt_launch(const AttnSimtParams &p, cudaStream_t st);
-// V [heads][k_rows][128] (bf16 or f32) -> V^T [heads][128][sk_pad] bf16, zero for keys >= sk.
-cudaError_t transpose_v_launch(const void *v, int v_f32, int heads, int k_rows, int sk, int sk_pad,
-                               __nv_bfloat16 *vt, cudaStream_t st);
-
 }  // namespace lx2v

@@ -13,9 +13,9 @@
 //   P_j = exp2(S_j * log2(e)/sqrt(D) - m)   softmax warps, thread = query row:
 //                       tcgen05.ld the row, mask, max, exp2, row sum, bf16 P
 //                       written back over S_j in TMEM
-//   O  += P_j V_j       tcgen05.mma with A = P_j from TMEM and B = V_j^T from
-//                       shared memory (V is given transposed, [D][keys]),
-//                       D = O in TMEM
+//   O  += P_j V_j       tcgen05.mma with A = P_j from TMEM and B = V_j from
+//                       shared memory as stored ([keys][D]: an MN-major
+//                       operand, D contiguous), D = O in TMEM
 // The live key blocks alternate between two softmax warpgroups: block i goes
 // to warpgroup i % 2, which has its own S buffer, running max m, row sum l and
 // accumulator O in TMEM. Each warpgroup's chain (softmax of its block, then
@@ -45,7 +45,7 @@
 //               thread holds a whole 128-key row of S
 //   warp 8      TMA producer of Q (once) and K_j (3-stage ring)
 //   warp 9      TMEM allocator and MMA issuer (one thread)
-//   warp 10     TMA producer of V_j^T (2-stage ring)
+//   warp 10     TMA producer of V_j (2-stage ring; keys past sk arrive as zeros)
 //   warp 11     idle (warpgroup 2 gives its registers to the softmax)
 // Every mbarrier wait is bounded; on expiry the kernel records an error
 // word, drains its own copies and MMAs, frees TMEM and returns.
@@ -73,7 +73,7 @@ constexpr int AT_HALF = AT_TILE / 2;
 constexpr int AT_OFF_K = AT_TILE;                   // after Q
 constexpr int AT_OFF_V = AT_OFF_K + AT_NK * AT_TILE;
 constexpr int AT_OFF_BAR = AT_OFF_V + AT_NV * AT_TILE;
-// q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2], o_full, drain
+// q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2][2 halves], o_full, drain
 constexpr int AT_NUM_BARS = 1 + 2 * AT_NK + 2 * AT_NV + 2 + 4 + 2;
 constexpr int AT_SMEM = 1024 + AT_OFF_BAR + AT_NUM_BARS * 8 + 16 + 512 * 4;
 constexpr int AT_TMEM_COLS = 512;  // O_0: 0-127, O_1: 128-255, S_0 / P_0: 256-383, S_1 / P_1: 384-511
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
         fence_mbar_init();
         tma_prefetch_desc(&p.tmap_q);
         tma_prefetch_desc(&p.tmap_k);
-        tma_prefetch_desc(&p.tmap_vt);
+        tma_prefetch_desc(&p.tmap_v);
     }
     if (warp == 9) tmem_alloc(tmem_slot, AT_TMEM_COLS);
     tc_fence_before();
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
     // 128-key row of S: 128 x 72 + 256 x 208 = 62464 <= 64512.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 72;" ::: "memory");
     if (warp == 8 || warp == 10) {
-        // ---------------- TMA producers: warp 8 Q and K_j, warp 10 V_j^T ----------------
+        // ---------------- TMA producers: warp 8 Q and K_j, warp 10 V_j ----------------
         // (separate threads, so that a K load never waits behind the
         // release of a V stage, which comes only after that block's softmax)
         if (lane == 0) {
@@ -193,8 +193,8 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                     tma_load_2d(kd + AT_HALF, &p.tmap_k, &full[st], 64, krow);
                 } else {
                     uint8_t *vd = smem + AT_OFF_V + st * AT_TILE;
-                    tma_load_2d(vd, &p.tmap_vt, &full[st], j * AT_BK, h * AT_D);
-                    tma_load_2d(vd + AT_HALF, &p.tmap_vt, &full[st], j * AT_BK + 64, h * AT_D);
+                    tma_load_3d(vd, &p.tmap_v, &full[st], 0, j * AT_BK, h);
+                    tma_load_3d(vd + AT_HALF, &p.tmap_v, &full[st], 64, j * AT_BK, h);
                 }
                 last[st] = (int)ph;
                 if (++st == ns) {
@@ -212,6 +212,11 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16_f32(128, 128);
+            // P V reads B = V_j as stored: MN-major (bit 16 of the instruction
+            // descriptor), 128-byte swizzle; each 64-column half of D is one
+            // TMA box of 128 keys x 128 B (LBO: the 16 KB between the halves),
+            // 8 keys per 1 KB swizzle atom (SBO), 16 keys (2 KB) per MMA
+            const uint32_t idesc_pv = idesc | (1u << 16);
             const uint32_t q_addr = smem_u32(smem);
             bool ok = mbar_wait_bounded(q_full, 0, err, lim);
             tc_fence_after();
@@ -233,8 +238,8 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
 #pragma unroll
                     for (int k4 = 0; k4 < 4; ++k4) {
                         const int kk = 4 * hf + k4;
-                        const uint64_t b = smem_desc_sw128(v_addr + hf * AT_HALF) + (uint64_t)(k4 * 2);
-                        mma_ts_f16(obuf, pbuf + (uint32_t)(kk * 8), b, idesc, (i >= 2 || kk > 0) ? 1u : 0u);
+                        const uint64_t b = smem_desc_sw128_mn(v_addr + (uint32_t)(kk * 2048), AT_HALF);
+                        mma_ts_f16(obuf, pbuf + (uint32_t)(kk * 8), b, idesc_pv, (i >= 2 || kk > 0) ? 1u : 0u);
                     }
                 }
                 mma_commit(&v_empty[vs.s]);
@@ -518,25 +523,6 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(AttnSimtParams p) {
     }
 }
 
-// ---- V [heads][rows][D] (bf16 or f32) -> V^T [heads][D][sk_pad] bf16, zero past sk ----
-__global__ void transpose_v_kernel(const void *v, int v_f32, int heads, int k_rows, int sk, int sk_pad,
-                                   __nv_bfloat16 *vt) {
-    __shared__ float tile[32][33];
-    const int h = blockIdx.z;
-    const int k0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int k = k0 + i, c = c0 + threadIdx.x;
-        float x = 0.0f;
-        if (k < sk) x = ld_act(v, v_f32, ((int64_t)h * k_rows + k) * AT_D + c);
-        tile[i][threadIdx.x] = x;
-    }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int c = c0 + i, k = k0 + threadIdx.x;
-        if (k < sk_pad) vt[((int64_t)h * AT_D + c) * sk_pad + k] = __float2bfloat16_rn(tile[threadIdx.x][i]);
-    }
-}
-
 }  // namespace
 
 cudaError_t attention_tc_launch(const AttnParams &p, cudaStream_t st) {
@@ -571,11 +557,5 @@ cudaError_t attention_simt_launch(const AttnSimtParams &p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t transpose_v_launch(const void *v, int v_f32, int heads, int k_rows, int sk, int sk_pad,
-                               __nv_bfloat16 *vt, cudaStream_t st) {
-    dim3 grid((sk_pad + 31) / 32, AT_D / 32, heads);
-    transpose_v_kernel<<<grid, dim3(32, 8), 0, st>>>(v, v_f32, heads, k_rows, sk, sk_pad, vt);
-    return cudaGetLastError();
-}
 
 }  // namespace lx2v

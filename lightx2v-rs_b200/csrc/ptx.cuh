@@ -165,6 +165,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
 }
+// 3-D tiled load global -> shared (coordinates innermost first); elements
+// outside the tensor's extent arrive as zeros.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
+                                            int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
 // 2-D tiled store shared -> global (bulk async-group).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t c0,
                                              int32_t c1) {
@@ -360,6 +370,20 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
     d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
     d |= (uint64_t)2 << 61;                         // layout: SWIZZLE_128B
+    return d;
+}
+
+// Shared-memory matrix descriptor for an MN-major operand in the 128-byte-
+// swizzled canonical layout: rows of 128 B hold 64 consecutive MN elements
+// of one k, 8 rows (8 k) per 1024-B atom (stride byte offset), and the next
+// 64 MN elements `mn_stride` bytes further on (leading byte offset).
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr, uint32_t mn_stride) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((mn_stride >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
     return d;
 }
 

@@ -67,7 +67,7 @@ struct lx2v_ctx {
     size_t gemv_ws_floats = 0;
     int *gemv_arrivals = nullptr;
     size_t gemv_tiles = 0;
-    void *att_ws = nullptr;      // attention: V^T copy, mask bits / temporal indices
+    void *att_ws = nullptr;      // attention: mask bits / temporal indices
     size_t att_ws_bytes = 0;
     void *kv_tmp = nullptr;      // KV cache: staging of row moves (splice / evict)
     size_t kv_tmp_bytes = 0;
@@ -1138,7 +1138,7 @@ extern "C" lx2v_status lx2v_gate_residual(lx2v_ctx *ctx, lx2v_buf *h, const lx2v
 }
 
 // ---- attention (backend.rs:275-307) ------------------------------------------------------
-// Grow-only workspace of the attention calls (V^T and the mask data).
+// Grow-only workspace of the attention calls (the mask data).
 static lx2v_status ensure_att_workspace(lx2v_ctx *ctx, size_t bytes) {
     if (ctx->att_ws_bytes >= bytes) return LX2V_OK;
     if (ctx->att_ws) {
@@ -1196,16 +1196,14 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
     const bool tc = d == 128 && !q_f32 && !kv_f32;
     const size_t sk_pad = align_up(sk, 128);
     const size_t n_qt = (sq + 127) / 128, n_kb = sk_pad / 128;
-    // workspace: [V^T bf16 heads*128*sk_pad][mask bits sq*words u32 | tq, tk, tq ranges, tk ranges]
-    const size_t vt_bytes = tc ? align_up(heads * 128 * sk_pad * 2, 256) : 0;
+    // workspace: [mask bits sq*words u32 | tq, tk, tq ranges, tk ranges]
     const size_t words = (sk + 31) / 32;
     size_t mask_bytes = 0;
     if (m.mode == ATT_MASK_BITS && !m.dev_bits) mask_bytes = sq * words * 4;
     else if (m.mode == ATT_MASK_TEMPORAL) mask_bytes = (sq + sk) * 4 + (n_qt + n_kb) * 8 + n_qt * 4;
-    lx2v_status s = ensure_att_workspace(ctx, vt_bytes + align_up(mask_bytes, 256) + 256);
+    lx2v_status s = ensure_att_workspace(ctx, align_up(mask_bytes, 256) + 256);
     if (s) return s;
-    char *ws = (char *)ctx->att_ws;
-    char *mws = ws + vt_bytes;
+    char *mws = (char *)ctx->att_ws;
     const uint32_t *bits_dev = nullptr;
     const int *tq_dev = nullptr, *tk_dev = nullptr;
     const int2 *tqr_dev = nullptr, *tkr_dev = nullptr;
@@ -1269,9 +1267,6 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         order_dev = tk_dev + sk;
     }
     if (tc) {
-        __nv_bfloat16 *vt = (__nv_bfloat16 *)ws;
-        CUDA_TRY(ctx, transpose_v_launch(v, kv_f32, (int)heads, (int)k_rows, (int)sk, (int)sk_pad, vt, ctx->stream));
-        ctx->launches++;
         AttnParams p;
         memset(&p, 0, sizeof p);
         if ((s = make_map(ctx, &p.tmap_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, heads * q_rows, 64, 128,
@@ -1280,9 +1275,21 @@ static lx2v_status attention_queue(lx2v_ctx *ctx, const char *opname, const void
         if ((s = make_map(ctx, &p.tmap_k, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, heads * k_rows, 64, 128,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
             return s;
-        if ((s = make_map(ctx, &p.tmap_vt, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sk_pad, heads * 128, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_128B)))
-            return s;
+        // V as stored, [heads][k_rows][128], seen as {128, sk, heads}: the
+        // keys of a head past sk are outside the map and load as zeros (their
+        // P is 0, and 0 times whatever the cache holds there must stay 0)
+        {
+            cuuint64_t dims[3] = {128, sk, heads};
+            cuuint64_t strides[2] = {128 * 2, (cuuint64_t)k_rows * 128 * 2};
+            cuuint32_t box[3] = {64, 128, 1};
+            cuuint32_t estr[3] = {1, 1, 1};
+            CUresult r = ctx->encode(&p.tmap_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(v), dims,
+                                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS)
+                return fail(ctx, LX2V_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for V %zux%zux%zu", (int)r,
+                            (size_t)128, sk, heads);
+        }
         p.out = out->ptr;
         p.out_f32 = out->dtype == LX2V_F32;
         p.heads = (int)heads; p.sq = (int)sq; p.sk = (int)sk;
