@@ -5,9 +5,10 @@
 // CPU reference: crates/lightx2v-cpu/src/lib.rs:328-459 and 806-874; trait
 // crates/lightx2v-core/src/backend.rs:214-273, 392-428.
 //
-// All of them are HBM-bound: one CTA per row, the row held in registers
-// between its two passes (statistics, then the normalised output), so each
-// row is read once and written once.
+// All of them are HBM-bound: the row is held in registers between its two
+// passes (statistics, then the normalised output), so each row is read once
+// and written once. Rows of 256 G values (G up to 12) run one warp per row;
+// other widths one CTA per row.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -318,6 +319,152 @@ __global__ void __launch_bounds__(512) head_split_vec_kernel(HeadSplitArgs a) {
     st8(a.out, a.out_f32, ((int64_t)h * a.rows + r) * a.head_dim + e, o);
 }
 
+// ---- one warp per row (8 rows a CTA) --------------------------------------
+// For rows of 256 G values: lane l holds the groups of 8 values l, l + 32,
+// ..., so every lane has G 16-byte loads in flight and the row statistics are
+// warp shuffles, not CTA barriers (the one-CTA-per-row kernels above were
+// latency-bound at 1.6-3.7 TB/s on the chunk's rows).
+constexpr int WROWS = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+}
+
+// head_split of a bf16 source row (the same arithmetic as head_split_vec_kernel).
+template <int G>
+__global__ void __launch_bounds__(32 * WROWS) head_split_warp_kernel(HeadSplitArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * WROWS + (threadIdx.x >> 5);
+    if (r >= a.rows) return;  // whole warps leave together
+    const int d = 256 * G;
+    const __nv_bfloat16 *src = reinterpret_cast<const __nv_bfloat16 *>(a.src) + r * a.src_stride + a.col_off;
+    uint4 raw[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) raw[g] = *reinterpret_cast<const uint4 *>(src + (g * 32 + lane) * 8);
+    float inv = 1.0f;
+    if (a.rms_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float x[8];
+            unpack8(raw[g], x);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
+        }
+        const float ms = a.sumsq ? summed_sumsq(a, r) / (float)a.rms_dim : warp_sum(ss) / (float)d;
+        inv = 1.0f / sqrtf(ms + a.eps);
+    }
+    const int hd = a.head_dim;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int j0 = (g * 32 + lane) * 8;
+        float x[8];
+        unpack8(raw[g], x);
+        if (a.rms_w) {
+            float w[8];
+            ld8(a.rms_w, a.w_f32, j0, w);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = x[k] * inv * w[k];
+        }
+        const int h = j0 / hd, e = j0 % hd;
+        float o[8];
+        if (a.cos) {
+            const int64_t ci = r * (hd / 2) + e / 2;
+            float c[4], sn[4];
+            if (a.cs_f32) {
+                const float4 c4 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.cos) + ci);
+                const float4 s4 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.sin) + ci);
+                c[0] = c4.x; c[1] = c4.y; c[2] = c4.z; c[3] = c4.w;
+                sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    c[k] = ld_v(a.cos, 0, ci + k);
+                    sn[k] = ld_v(a.sin, 0, ci + k);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                o[2 * k] = x[2 * k] * c[k] - x[2 * k + 1] * sn[k];
+                o[2 * k + 1] = x[2 * k] * sn[k] + x[2 * k + 1] * c[k];
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = x[k];
+        }
+        st8(a.out, a.out_f32, ((int64_t)h * a.rows + r) * hd + e, o);
+    }
+}
+
+// layer_norm (RESID false) / residual_norm (RESID true) of a row of 256 G
+// values (the same arithmetic as norm_vec_kernel).
+template <int G, bool RESID>
+__global__ void __launch_bounds__(32 * WROWS) norm_warp_kernel(NormArgs a, void *h, int h_f32, const void *res,
+                                                              int res_f32, int gate) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * WROWS + (threadIdx.x >> 5);
+    if (r >= a.rows) return;
+    float v[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int j0 = (g * 32 + lane) * 8;
+        const int64_t i0 = r * a.dim + j0;
+        if (RESID) {
+            float hv[8], av[8], gg[8];
+            ld8(h, h_f32, i0, hv);
+            ld8(res, res_f32, i0, av);
+            if (gate >= 0) ld8(a.mods, a.mods_f32, (int64_t)gate * a.dim + j0, gg);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[g][k] = hv[k] + av[k] * (gate >= 0 ? gg[k] : 1.0f);
+            st8(h, h_f32, i0, v[g]);
+        } else {
+            ld8(a.x, a.x_f32, i0, v[g]);
+        }
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += v[g][k];
+    const float mean = warp_sum(s) / (float)a.dim;
+    float vs = 0.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float c = v[g][k] - mean;
+            vs += c * c;
+        }
+    const float var = warp_sum(vs) / (float)a.dim;
+    const float inv = 1.0f / sqrtf(var + a.eps);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int j0 = (g * 32 + lane) * 8;
+        float p[8], q[8], o[8];
+        if (a.kind == 0) {
+            ld8(a.w, a.w_f32, j0, p);
+            ld8(a.b, a.b_f32, j0, q);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = (v[g][k] - mean) * inv * p[k] + q[k];
+        } else {
+            ld8(a.mods, a.mods_f32, (int64_t)a.scale * a.dim + j0, p);
+            ld8(a.mods, a.mods_f32, (int64_t)a.shift * a.dim + j0, q);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = (v[g][k] - mean) * inv * (1.0f + p[k]) + q[k];
+        }
+        st8(a.out, a.out_f32, r * a.dim + j0, o);
+    }
+}
+
 // One row per CTA: the sum of squares of `width` values, f32.
 __global__ void __launch_bounds__(ROW_THREADS) row_sumsq_kernel(const void *src, int src_f32, int64_t stride,
                                                                 int64_t col_off, int width, float *out) {
@@ -346,8 +493,41 @@ bool row_op_supported(int dim) { return dim > 0 && dim <= ROW_THREADS * ROW_PER_
 // when dim % 256 == 0).
 static bool vec_ok(int dim) { return dim % 256 == 0 && dim <= 4096; }
 
+// Warp-per-row instantiations: rows of 256 G values.
+template <bool RESID>
+static bool norm_warp_launch(const NormArgs &a, void *h, int h_f32, const void *res, int res_f32, int gate,
+                             cudaStream_t st) {
+    if (a.dim % 256 != 0) return false;
+    const unsigned grid = (unsigned)((a.rows + WROWS - 1) / WROWS);
+    switch (a.dim / 256) {
+#define LX2V_NORM_G(G)                                                                                  \
+    case G:                                                                                             \
+        norm_warp_kernel<G, RESID><<<grid, 32 * WROWS, 0, st>>>(a, h, h_f32, res, res_f32, gate);       \
+        return true;
+        LX2V_NORM_G(1) LX2V_NORM_G(2) LX2V_NORM_G(3) LX2V_NORM_G(4) LX2V_NORM_G(6) LX2V_NORM_G(8) LX2V_NORM_G(12)
+#undef LX2V_NORM_G
+        default: return false;
+    }
+}
+static bool head_split_warp_launch(const HeadSplitArgs &a, cudaStream_t st) {
+    const int d = a.heads * a.head_dim;
+    if (a.src_f32 || d % 256 != 0 || a.head_dim % 8 != 0 || a.src_stride % 8 != 0 || a.col_off % 8 != 0)
+        return false;
+    const unsigned grid = (unsigned)((a.rows + WROWS - 1) / WROWS);
+    switch (d / 256) {
+#define LX2V_HS_G(G)                                                   \
+    case G:                                                            \
+        head_split_warp_kernel<G><<<grid, 32 * WROWS, 0, st>>>(a);     \
+        return true;
+        LX2V_HS_G(1) LX2V_HS_G(2) LX2V_HS_G(3) LX2V_HS_G(4) LX2V_HS_G(6) LX2V_HS_G(8) LX2V_HS_G(12)
+#undef LX2V_HS_G
+        default: return false;
+    }
+}
+
 cudaError_t layer_norm_launch(const NormArgs &a, cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    if (norm_warp_launch<false>(a, nullptr, 0, nullptr, 0, -1, st)) return cudaGetLastError();
     if (vec_ok(a.dim)) {
         norm_vec_kernel<false><<<(unsigned)a.rows, a.dim / 8, 0, st>>>(a, nullptr, 0, nullptr, 0, -1);
         return cudaGetLastError();
@@ -359,6 +539,7 @@ cudaError_t layer_norm_launch(const NormArgs &a, cudaStream_t st) {
 cudaError_t residual_norm_launch(const NormArgs &a, void *h, int h_f32, const void *res, int res_f32, int gate,
                                  cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    if (norm_warp_launch<true>(a, h, h_f32, res, res_f32, gate, st)) return cudaGetLastError();
     if (vec_ok(a.dim)) {
         norm_vec_kernel<true><<<(unsigned)a.rows, a.dim / 8, 0, st>>>(a, h, h_f32, res, res_f32, gate);
         return cudaGetLastError();
@@ -369,6 +550,7 @@ cudaError_t residual_norm_launch(const NormArgs &a, void *h, int h_f32, const vo
 
 cudaError_t head_split_launch(const HeadSplitArgs &a, cudaStream_t st) {
     if (a.rows == 0) return cudaSuccess;
+    if (head_split_warp_launch(a, st)) return cudaGetLastError();
     const int d = a.heads * a.head_dim;
     // 8 values a thread never straddle a head; src rows, the column offset and
     // the RoPE rows stay 16-byte aligned

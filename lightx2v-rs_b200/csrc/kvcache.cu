@@ -35,6 +35,18 @@ __global__ void kv_copy_rows_kernel(const void *src, int src_f32, int64_t src_hs
     }
 }
 
+// The same copy between equal element types, 16 bytes a thread: rows of
+// row_vec uint4 per head (head strides in rows).
+__global__ void kv_copy_rows_vec_kernel(const uint4 *src, int64_t src_hs, int64_t src_row0, uint4 *dst,
+                                        int64_t dst_hs, int64_t dst_row0, int64_t rows, int row_vec, int heads) {
+    const int64_t per_head = rows * row_vec;
+    const int64_t total = per_head * heads;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t h = i / per_head, e = i % per_head;
+        dst[(h * dst_hs + dst_row0) * row_vec + e] = src[(h * src_hs + src_row0) * row_vec + e];
+    }
+}
+
 // ema rows <- (1 - alpha) * ema + alpha * frame rows (memrope.rs ema_update),
 // in f32 on the stored bf16 values.
 __global__ void kv_ema_kernel(__nv_bfloat16 *data, int64_t hs, int64_t ema_row0, int64_t src_row0, int64_t rows,
@@ -62,8 +74,20 @@ cudaError_t kv_copy_rows_launch(const void *src, int src_f32, int64_t src_hs, in
                                 cudaStream_t st) {
     if (rows <= 0 || heads <= 0) return cudaSuccess;
     if (src_f32 == dst_f32) {
-        // same element type: one strided copy, a row block per head
         const size_t es = src_f32 ? 4 : 2;
+        if (((size_t)d * es) % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+            reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+            // same element type, 16-byte rows: a vector copy on the SMs (the
+            // strided cudaMemcpy2DAsync ran at ~1.5 TB/s on the chunk's K / V)
+            const int row_vec = (int)((size_t)d * es / 16);
+            const int64_t n = rows * row_vec * heads;
+            const int64_t b = (n + 255) / 256;
+            kv_copy_rows_vec_kernel<<<(int)(b < 148 * 16 ? b : 148 * 16), 256, 0, st>>>(
+                reinterpret_cast<const uint4 *>(src), src_hs, src_row0, reinterpret_cast<uint4 *>(dst), dst_hs,
+                dst_row0, rows, row_vec, heads);
+            return cudaGetLastError();
+        }
+        // same element type otherwise: one strided copy, a row block per head
         return cudaMemcpy2DAsync((char *)dst + (size_t)dst_row0 * d * es, (size_t)dst_hs * d * es,
                                  (const char *)src + (size_t)src_row0 * d * es, (size_t)src_hs * d * es,
                                  (size_t)rows * d * es, (size_t)heads, cudaMemcpyDeviceToDevice, st);
