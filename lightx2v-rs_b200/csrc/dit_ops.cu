@@ -364,6 +364,19 @@ __global__ void __launch_bounds__(32 * WROWS) head_split_warp_kernel(HeadSplitAr
         inv = 1.0f / sqrtf(ms + a.eps);
     }
     const int hd = a.head_dim;
+    // when head_dim divides 256, a lane's 8 values sit at the same offset of
+    // their head in every group: its RoPE angles are loaded once, before any
+    // store (a load after a store cannot be moved above it)
+    const bool rope_once = a.cos && 256 % hd == 0;
+    float c1[4], s1[4];
+    if (rope_once) {
+        const int64_t ci = r * (hd / 2) + ((lane * 8) % hd) / 2;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            c1[k] = ld_v(a.cos, a.cs_f32, ci + k);
+            s1[k] = ld_v(a.sin, a.cs_f32, ci + k);
+        }
+    }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const int j0 = (g * 32 + lane) * 8;
@@ -380,7 +393,13 @@ __global__ void __launch_bounds__(32 * WROWS) head_split_warp_kernel(HeadSplitAr
         if (a.cos) {
             const int64_t ci = r * (hd / 2) + e / 2;
             float c[4], sn[4];
-            if (a.cs_f32) {
+            if (rope_once) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    c[k] = c1[k];
+                    sn[k] = s1[k];
+                }
+            } else if (a.cs_f32) {
                 const float4 c4 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.cos) + ci);
                 const float4 s4 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.sin) + ci);
                 c[0] = c4.x; c[1] = c4.y; c[2] = c4.z; c[3] = c4.w;
@@ -414,21 +433,26 @@ __global__ void __launch_bounds__(32 * WROWS) norm_warp_kernel(NormArgs a, void 
     const int64_t r = (int64_t)blockIdx.x * WROWS + (threadIdx.x >> 5);
     if (r >= a.rows) return;
     float v[G][8];
+    // every load of the row first, then the stores to h (a load after a store
+    // to a buffer that may alias it could not be moved above the store)
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const int j0 = (g * 32 + lane) * 8;
         const int64_t i0 = r * a.dim + j0;
         if (RESID) {
-            float hv[8], av[8], gg[8];
-            ld8(h, h_f32, i0, hv);
+            float av[8], gg[8];
+            ld8(h, h_f32, i0, v[g]);
             ld8(res, res_f32, i0, av);
             if (gate >= 0) ld8(a.mods, a.mods_f32, (int64_t)gate * a.dim + j0, gg);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[g][k] = hv[k] + av[k] * (gate >= 0 ? gg[k] : 1.0f);
-            st8(h, h_f32, i0, v[g]);
+            for (int k = 0; k < 8; ++k) v[g][k] = v[g][k] + av[k] * (gate >= 0 ? gg[k] : 1.0f);
         } else {
             ld8(a.x, a.x_f32, i0, v[g]);
         }
+    }
+    if (RESID) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) st8(h, h_f32, r * a.dim + (g * 32 + lane) * 8, v[g]);
     }
     float s = 0.0f;
 #pragma unroll
