@@ -330,6 +330,33 @@ def timed_steps(be, ext, flush, fn, steps, cushion=1):
     return [a.elapsed_time(b) for a, b in pairs]
 
 
+def bind_host_to_gpu(local_rank: int):
+    """Run this process on the host cores that NVML reports as local to the
+    GPU (read with nvmlDeviceGetCpuAffinity; nothing about the GPU is changed),
+    so that the end-to-end leg's pinned buffers are first touched, and so
+    placed, in that socket's memory and its copies cross no socket link.
+    Returns the cores, or None when NVML or the affinity call is unavailable."""
+    try:
+        import pynvml
+        import torch
+        props = torch.cuda.get_device_properties(local_rank)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            mask = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, m in enumerate(mask) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return sorted(cpus)
+    except Exception:
+        return None
+
+
 def cuda_arm(args, rank: int, world: int, local_rank: int):
     """The headline: the C2 chunk (M = 4680 token rows) through the four FP8
     linears. With N ranks the chunk's rows are split (rank r takes rows
@@ -342,6 +369,7 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     from lightx2v_cuda import F32, CudaBackend
 
     torch.cuda.set_device(local_rank)
+    host_cpus = bind_host_to_gpu(local_rank)
     dist = None
     if world > 1:
         import torch.distributed as dist_mod
@@ -507,7 +535,9 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
                     "path": "C ABI, steps pipelined: lx2v_buf_write_f32 x and h rows from pinned host (copy "
                             "stream), 4 linears, lx2v_buf_download_f32_async h; h alternates between two "
                             "device buffers; one event pair around all steps, no L2 flush (each step's "
-                            "inputs arrive from the host); bytes summed over ranks"},
+                            "inputs arrive from the host); bytes summed over ranks",
+                    "host_cores": (f"{len(host_cpus)} cores local to the GPU (NVML CPU affinity)" if host_cpus
+                                   else "unbound (NVML CPU affinity unavailable)")},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": f"bf16 dense burst, {peak_src}",
                          "traffic": profile_traffic(),

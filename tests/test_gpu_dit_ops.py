@@ -82,9 +82,10 @@ def test_layer_norm_matches_oracle(be, oracle, dim, rows):
             assert rel_l2(be.download(ob), want) <= tol, (norm[0], odt)
 
 
+# widths of 256 G values run one warp per row (G = 6, 12, 3); 96 one CTA per row
+@pytest.mark.parametrize("dim,rows", [(1536, 200), (3072, 61), (768, 77), (96, 9)])
 @pytest.mark.parametrize("gate", [2, None])
-def test_residual_norm_matches_oracle(be, oracle, gate):
-    dim, rows = 1536, 200
+def test_residual_norm_matches_oracle(be, oracle, gate, dim, rows):
     h = oracle.normal(11, rows * dim)
     a = oracle.normal(12, rows * dim)
     mods = oracle.normal(13, 6 * dim, 0.1)
@@ -104,10 +105,14 @@ def test_residual_norm_matches_oracle(be, oracle, gate):
     assert rel_l2(be.download(ob2), want_m) <= 1e-2
 
 
-def test_head_split_matches_oracle(be, oracle):
-    # the QKV output of a chunk: q and k RMS-normalised across all 12 heads,
+# (12, 128): the 1.3B chunk; (24, 128): the 5B shape; (6, 128) and (1, 128):
+# a rank's heads under tensor parallelism (warp per row, then one CTA per
+# row); (4, 64): head_dim 64
+@pytest.mark.parametrize("heads,hd", [(12, 128), (24, 128), (6, 128), (1, 128), (4, 64)])
+def test_head_split_matches_oracle(be, oracle, heads, hd):
+    # the QKV output of a chunk: q and k RMS-normalised across all heads,
     # rotated by RoPE; v passed through (dit.rs:612-640)
-    heads, hd, rows = 12, 128, 300
+    rows = 300
     d = heads * hd
     qkv = be.upload(oracle.normal(21, rows * 3 * d), BF16)
     src = be.download(qkv)
