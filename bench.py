@@ -483,17 +483,26 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
         uid = [be.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         be.comm_init(uid[0], rank, world)
-    tp = tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barrier)
+    try:  # after the headline, like the chunk step below: an error is reported in the line
+        tp = tp_ffn_measure(args, be, ext, flush, rank, world, dist, max_over_ranks, barrier)
+    except Exception as e:  # noqa: BLE001 - reported, not hidden
+        tp = {"n_gpus": world, "error": f"{type(e).__name__}: {e}"[:400]}
 
     # --- the whole 1.3B chunk step (C4), tensor-parallel on several GPUs -------------------
     chunk = None
     if not args.no_chunk:
         barrier()
-        chunk = chunk_step_measure(args, be, ext, flush, "c4", "fp8", 30, rank, world,
-                                   max_over_ranks if world > 1 else None)
-        prof = chunk.pop("_profile", None)
-        if args.profile:
-            chunk["profile_ms_per_step"] = prof
+        # measured after the headline: an error here (the same on every rank,
+        # e.g. a shape a rank count makes unsupported) is reported in the line
+        # instead of losing it
+        try:
+            chunk = chunk_step_measure(args, be, ext, flush, "c4", "fp8", 30, rank, world,
+                                       max_over_ranks if world > 1 else None)
+            prof = chunk.pop("_profile", None)
+            if args.profile:
+                chunk["profile_ms_per_step"] = prof
+        except Exception as e:  # noqa: BLE001 - reported, not hidden
+            chunk = {"n_gpus": world, "error": f"{type(e).__name__}: {e}"[:400]}
         barrier()
 
     flops_step = step_flops(M)
