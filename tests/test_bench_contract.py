@@ -23,3 +23,35 @@ def test_reference_arm_prints_the_contract_line():
     for k in ("value", "unit", "cores", "kind", "sample"):
         assert k in d["cpu_baseline"], k
     assert d["cpu_baseline"]["value"] == d["value"]
+
+
+def test_host_binding_follows_the_gpu_cpu_affinity(monkeypatch):
+    """bench.bind_host_to_gpu reads the GPU's local cores from NVML (a fake
+    here: cores 0 and 2 of the process's own set) and moves the process onto
+    them; without NVML it changes nothing and returns None."""
+    import types
+    import torch
+    sys.path.insert(0, ROOT)
+    import bench
+    own = sorted(os.sched_getaffinity(0))
+    want = {own[0], own[-1]}
+    mask = [0] * ((max(own) // 64) + 1)
+    for c in want:
+        mask[c // 64] |= 1 << (c % 64)
+    seen = {}
+    fake = types.SimpleNamespace(
+        nvmlInit=lambda: None, nvmlShutdown=lambda: None,
+        nvmlDeviceGetHandleByPciBusId=lambda bus: seen.setdefault("bus", bus),
+        nvmlDeviceGetCpuAffinity=lambda handle, n: mask[:n] + [0] * max(0, n - len(mask)))
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1B, pci_device_id=0)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda i: props)
+    try:
+        assert bench.bind_host_to_gpu(0) == sorted(want)
+        assert os.sched_getaffinity(0) == want
+        assert seen["bus"] == "00000000:1b:00.0"
+    finally:
+        os.sched_setaffinity(0, own)
+    monkeypatch.setitem(sys.modules, "pynvml", None)  # import fails: no binding
+    assert bench.bind_host_to_gpu(0) is None
+    assert sorted(os.sched_getaffinity(0)) == own
