@@ -374,12 +374,6 @@ def cuda_arm(args, rank: int, world: int, local_rank: int):
     if world > 1:
         import torch.distributed as dist_mod
         from datetime import timedelta
-        # NCCL's own initialisation lines (ranks, nranks, NVLS) on stderr, so
-        # that a run's rank count can be read from NCCL itself; stdout keeps
-        # the one JSON line
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist = dist_mod
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
