@@ -379,16 +379,27 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
             const float nm = m_run == NEG_INF ? 0.0f : -m_run;
             // P = exp2(S * scale - m) as bf16 pairs over the first 64 columns
             // of S_wg (all 128 scores are already in registers)
-            float ls0 = 0.0f, ls1 = 0.0f;
+            // the exponent arguments and the row sums two at a time (f32x2:
+            // one packed FMA / add for a pair of keys, the same rounding and
+            // the same two partial sums as the scalar form)
+            uint64_t ls2, sc2, nm2;
+            asm("mov.b64 %0, {%1, %1};" : "=l"(sc2) : "f"(sc));
+            asm("mov.b64 %0, {%1, %1};" : "=l"(nm2) : "f"(nm));
+            asm("mov.b64 %0, {%1, %1};" : "=l"(ls2) : "f"(0.0f));
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    const float a = ex2(fmaf(__uint_as_float(sv[32 * c + 2 * k]), sc, nm));
-                    const float b = ex2(fmaf(__uint_as_float(sv[32 * c + 2 * k + 1]), sc, nm));
-                    ls0 += a;
-                    ls1 += b;
+                    uint64_t s2, x2, p2;
+                    float xa, xb;
+                    asm("mov.b64 %0, {%1, %2};" : "=l"(s2) : "r"(sv[32 * c + 2 * k]), "r"(sv[32 * c + 2 * k + 1]));
+                    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(x2) : "l"(s2), "l"(sc2), "l"(nm2));
+                    asm("mov.b64 {%0, %1}, %2;" : "=f"(xa), "=f"(xb) : "l"(x2));
+                    const float a = ex2(xa);
+                    const float b = ex2(xb);
+                    asm("mov.b64 %0, {%1, %2};" : "=l"(p2) : "f"(a), "f"(b));
+                    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(ls2) : "l"(p2));
                     pk[k] = pack_bf16x2(a, b);
                 }
                 tmem_st_32x32b_x16(lane_base + s_col + (uint32_t)(c * 16), pk);
@@ -399,6 +410,8 @@ __global__ void __launch_bounds__(384, 1) attention_tc_kernel(const __grid_const
                     if (lane == 0) mbar_arrive(&p_full[2 * wg + (c >> 1)]);
                 }
             }
+            float ls0, ls1;
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(ls0), "=f"(ls1) : "l"(ls2));
             l += ls0 + ls1;
         }
         // ---------------- epilogue: out[q, h*D + c] = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) ----------------
