@@ -24,6 +24,14 @@ def test_header_declares_the_binding():
     assert set(syms) == set(L.SIGNATURES), set(syms) ^ set(L.SIGNATURES)
 
 
+def test_integration_guide_binds_every_declared_symbol():
+    # the Rust side of the boundary (the extern "C" block and the methods of
+    # the crate written out in INTEGRATION.md) names every entry point
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    missing = [s for s in declared_symbols() if not re.search(r"\b" + s + r"\b", doc)]
+    assert not missing, missing
+
+
 def test_library_exports_every_declared_symbol():
     lib = L.load()
     out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True,
